@@ -1,0 +1,116 @@
+/*
+ * decodek: the C ABI of the B200 (sm_100a) decode kernels.
+ *
+ * Every entry point takes plain device pointers, sizes in elements, row strides in elements and
+ * a CUDA stream, and returns an int status (DK_OK = 0, negative on error, with the message in
+ * dk_last_error()). Nothing allocates device memory, synchronizes or reads device memory from
+ * the host, so every call can be captured in a CUDA graph. Kernels are queued on `stream` and
+ * report launch errors through the status; asynchronous device-side conditions (a bounded wait
+ * that gave up) are recorded in a per-device error word read with dk_device_error().
+ *
+ * fp16 tensors are passed as `const void*` (IEEE binary16), e4m3 tensors as `uint8_t` bytes.
+ * Layouts are the reference's (Charlie-Gzz/llm-decode-kernels):
+ *   qweight  int32 [K/8, N], N contiguous; value i of a word is bits 4i..4i+3  (kernels/quant.py:4-8)
+ *   scales, zeros  fp16 [K/group, N]                                           (kernels/quant.py:8)
+ *   fp8 weight  e4m3 [K, N], N contiguous; scale fp16 [N]                        (kernels/fp8.py:3-6)
+ */
+#ifndef DECODEK_H_
+#define DECODEK_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* dk_stream_t; /* same type as cudaStream_t */
+
+#define DK_ABI_VERSION 1
+
+/* status codes */
+#define DK_OK 0
+#define DK_ERR_INVALID (-1)     /* shape, size or argument outside the contract */
+#define DK_ERR_ALIGN (-2)       /* pointer or stride alignment the kernel cannot handle */
+#define DK_ERR_UNSUPPORTED (-3) /* valid request this build has no kernel for */
+#define DK_ERR_CUDA (-4)        /* a CUDA runtime call failed (message has the CUDA error) */
+
+/* device error codes (dk_device_error) */
+#define DK_DEVERR_NONE 0
+#define DK_DEVERR_WAIT_FULL 1  /* a consumer gave up waiting for a stage's copies */
+#define DK_DEVERR_WAIT_EMPTY 2 /* the producer gave up waiting for a stage to be released */
+
+/* dk_matmul_config.flags */
+#define DK_FLAG_STATIC_WEIGHTS 1 /* weights are not written by any kernel still in flight on the
+                                    stream: the kernel may prefetch them before waiting for the
+                                    previous kernel (programmatic dependent launch) */
+#define DK_FLAG_GENERIC 2        /* force the simple (any alignment) kernel; for tests */
+
+/* Optional per-call tuning; zero fields mean "choose automatically". */
+typedef struct dk_matmul_config {
+  int32_t split_k; /* number of K slices reduced inside a thread-block cluster (1..8) */
+  int32_t block_n; /* output columns per CTA (32, 64 or 128) */
+  int32_t flags;   /* DK_FLAG_* */
+  int32_t reserved;
+} dk_matmul_config;
+
+/* ---- library ---------------------------------------------------------------------------- */
+int dk_abi_version(void);
+/* Message of the last failing call on this host thread ("" if none). */
+const char* dk_last_error(void);
+/* Device error word of the current device (DK_DEVERR_*); reading it synchronizes the device.
+ * No reference counterpart: the reference's kernels have no bounded waits. */
+int dk_device_error(int32_t* code);
+int dk_clear_device_error(void);
+/* Programmatic dependent launch on (1, default) or off (0) for all later launches. */
+int dk_set_pdl(int32_t enabled);
+
+/* ---- int4 format: kernels/quant.py ------------------------------------------------------- */
+/* pack_int4 (kernels/quant.py:20-28): q int32 [K, N] -> packed int32 [K/8, N]. K % 8 == 0. */
+int dk_pack_int4(const int32_t* q, int32_t* packed, int64_t K, int64_t N, dk_stream_t stream);
+/* unpack_int4 (kernels/quant.py:31-35): packed int32 [K/8, N] -> q int32 [K, N] in 0..15. */
+int dk_unpack_int4(const int32_t* packed, int32_t* q, int64_t K, int64_t N, dk_stream_t stream);
+/* quantize_rtn (kernels/quant.py:38-49): w fp16 [N, K] (row stride ldw) -> qweight, scales,
+ * zeros. Bit-exact with the reference. K % group_size == 0, group_size % 8 == 0. */
+int dk_quantize_rtn(const void* w, int64_t ldw, int32_t* qweight, void* scales, void* zeros,
+                    int64_t N, int64_t K, int64_t group_size, dk_stream_t stream);
+/* dequantize_ref (kernels/reference.py:27-36): -> fp16 [N, K], (fp16(q) - z) * s in fp16. */
+int dk_dequantize_int4(const int32_t* qweight, const void* scales, const void* zeros, void* w,
+                       int64_t N, int64_t K, int64_t group_size, dk_stream_t stream);
+
+/* ---- W4A16 matmul: kernels/w4a16.py, kernels/cuda/w4a16_decode.cu ---------------------- */
+/* w4a16_matmul (kernels/w4a16.py:301-330) and w4a16_decode (kernels/cuda/w4a16_decode.cu:136-181):
+ * y[M, N] fp16 = x[M, K] fp16 @ dequant(W).T (+ bias[N]), fp32 accumulation.
+ * x rows have stride ldx, y rows stride ldy (elements). bias may be NULL. cfg may be NULL. */
+int dk_w4a16_matmul(const void* x, int64_t ldx, const int32_t* qweight, const void* scales,
+                    const void* zeros, const void* bias, void* y, int64_t ldy, int64_t M,
+                    int64_t N, int64_t K, int64_t group_size, const dk_matmul_config* cfg,
+                    dk_stream_t stream);
+
+/* ---- FP8 e4m3 weight-only format: kernels/fp8.py ------------------------------------------ */
+/* quantize_fp8 (kernels/fp8.py:25-30): w fp16 [N, K] (row stride ldw) -> wq e4m3 [K, N],
+ * scale fp16 [N]; per-row absmax / 448 clamped >= 1e-12. Bit-exact with the reference. */
+int dk_quantize_fp8(const void* w, int64_t ldw, uint8_t* wq, void* scale, int64_t N, int64_t K,
+                    dk_stream_t stream);
+/* dequantize_fp8 (kernels/fp8.py:33-35): -> fp16 [N, K] = fp16(fp32(wq) * fp32(scale)). */
+int dk_dequantize_fp8(const uint8_t* wq, const void* scale, void* w, int64_t N, int64_t K,
+                      dk_stream_t stream);
+
+/* ---- fused RMSNorm (+ residual): kernels/rmsnorm.py ------------------------------------- */
+/* rmsnorm (kernels/rmsnorm.py:44-68): out = w * fp16(h * rsqrt(mean(h^2) + eps)) with
+ * h = x (+ residual, fp16 add, also written to residual_out). residual may be NULL (then
+ * residual_out is unused). x, residual, out, residual_out are [M, N] with the given row strides. */
+int dk_rmsnorm(const void* x, int64_t ldx, const void* residual, int64_t ldr, const void* weight,
+               void* out, int64_t ldo, void* residual_out, int64_t ldro, int64_t M, int64_t N,
+               float eps, dk_stream_t stream);
+
+/* ---- fused SwiGLU: kernels/swiglu.py ----------------------------------------------------- */
+/* swiglu / swiglu_fused (kernels/swiglu.py:49-61): out[M, I] = fp16(silu(gate)) * up.
+ * For the fused [M, 2I] layout pass gate = gu, up = gu + I, ldg = ldu = 2I. */
+int dk_swiglu(const void* gate, int64_t ldg, const void* up, int64_t ldu, void* out, int64_t ldo,
+              int64_t M, int64_t I, dk_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DECODEK_H_ */

@@ -1,0 +1,95 @@
+// Library-level entry points: error strings, the device error word, device properties, PDL switch.
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+
+namespace dk {
+
+// One copy per device that loads the library; kernels receive its address (DeviceInfo::err_word).
+__device__ int g_device_error = 0;
+
+namespace {
+thread_local char t_last_error[1024] = "";
+bool g_pdl = true;
+}  // namespace
+
+int set_error(int status, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_last_error, sizeof(t_last_error), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(DK_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
+  return DK_OK;
+}
+
+bool pdl_enabled() { return g_pdl; }
+
+const DeviceInfo& device_info() {
+  static std::mutex mu;
+  static std::vector<DeviceInfo> cache;
+  static std::vector<bool> have;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev >= static_cast<int>(cache.size())) {
+    cache.resize(dev + 1);
+    have.resize(dev + 1, false);
+  }
+  if (!have[dev]) {
+    DeviceInfo d = {};
+    cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaDeviceGetAttribute(&d.smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev);
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) p = nullptr;
+    d.err_word = static_cast<int*>(p);
+    cache[dev] = d;
+    have[dev] = true;
+  }
+  return cache[dev];
+}
+
+}  // namespace dk
+
+extern "C" {
+
+int dk_abi_version(void) { return DK_ABI_VERSION; }
+
+const char* dk_last_error(void) { return dk::t_last_error; }
+
+int dk_device_error(int32_t* code) {
+  if (code == nullptr) return dk::set_error(DK_ERR_INVALID, "dk_device_error: code is NULL");
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return dk::set_error(DK_ERR_CUDA, "dk_device_error: %s", cudaGetErrorString(e));
+  int v = 0;
+  e = cudaMemcpyFromSymbol(&v, dk::g_device_error, sizeof(int));
+  if (e != cudaSuccess) return dk::set_error(DK_ERR_CUDA, "dk_device_error: %s", cudaGetErrorString(e));
+  *code = v;
+  return DK_OK;
+}
+
+int dk_clear_device_error(void) {
+  int zero = 0;
+  cudaError_t e = cudaMemcpyToSymbol(dk::g_device_error, &zero, sizeof(int));
+  if (e != cudaSuccess) return dk::set_error(DK_ERR_CUDA, "dk_clear_device_error: %s", cudaGetErrorString(e));
+  e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return dk::set_error(DK_ERR_CUDA, "dk_clear_device_error: %s", cudaGetErrorString(e));
+  return DK_OK;
+}
+
+int dk_set_pdl(int32_t enabled) {
+  dk::g_pdl = enabled != 0;
+  return DK_OK;
+}
+
+}  // extern "C"

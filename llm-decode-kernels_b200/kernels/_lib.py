@@ -1,0 +1,116 @@
+"""Loader for `libdecodek.so`, the C ABI of the sm_100a kernels (declared in include/decodek.h).
+
+Every op in this package calls the library through ctypes with raw device pointers and torch's
+current CUDA stream. There is no CPU fallback: a CPU tensor, a missing library or a non-B200 device
+raises. A negative status from the library becomes a RuntimeError carrying `dk_last_error()`.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parents[1] / "lib" / "libdecodek.so"
+
+P = ctypes.c_void_p
+I64 = ctypes.c_int64
+I32 = ctypes.c_int32
+F32 = ctypes.c_float
+
+
+class MatmulConfig(ctypes.Structure):
+    """dk_matmul_config: zero fields mean "choose automatically"."""
+
+    _fields_ = [("split_k", I32), ("block_n", I32), ("flags", I32), ("reserved", I32)]
+
+
+FLAG_STATIC_WEIGHTS = 1
+FLAG_GENERIC = 2
+
+# name -> argtypes; every function returns int status
+SIGNATURES = {
+    "dk_abi_version": [],
+    "dk_device_error": [ctypes.POINTER(I32)],
+    "dk_clear_device_error": [],
+    "dk_set_pdl": [I32],
+    "dk_pack_int4": [P, P, I64, I64, P],
+    "dk_unpack_int4": [P, P, I64, I64, P],
+    "dk_quantize_rtn": [P, I64, P, P, P, I64, I64, I64, P],
+    "dk_dequantize_int4": [P, P, P, P, I64, I64, I64, P],
+    "dk_w4a16_matmul": [P, I64, P, P, P, P, P, I64, I64, I64, I64, I64, ctypes.POINTER(MatmulConfig), P],
+    "dk_quantize_fp8": [P, I64, P, P, I64, I64, P],
+    "dk_dequantize_fp8": [P, P, P, I64, I64, P],
+    "dk_rmsnorm": [P, I64, P, I64, P, P, I64, P, I64, I64, I64, F32, P],
+    "dk_swiglu": [P, I64, P, I64, P, I64, I64, I64, P],
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not LIB_PATH.exists():
+                    raise RuntimeError(
+                        f"{LIB_PATH} is missing: build it with `python llm-decode-kernels_b200/build.py` "
+                        "(the decode kernels have no CPU fallback)")
+                h = ctypes.CDLL(str(LIB_PATH))
+                for name, args in SIGNATURES.items():
+                    fn = getattr(h, name)
+                    fn.argtypes = args
+                    fn.restype = ctypes.c_int
+                h.dk_last_error.argtypes = []
+                h.dk_last_error.restype = ctypes.c_char_p
+                _lib = h
+    return _lib
+
+
+def check(status: int, what: str) -> None:
+    if status != 0:
+        msg = lib().dk_last_error().decode(errors="replace")
+        raise RuntimeError(f"{what}: {msg} (status {status})")
+
+
+def call(name: str, *args) -> None:
+    check(getattr(lib(), name)(*args), name)
+
+
+def ptr(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream_of(t: torch.Tensor):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def require_cuda(what: str, *tensors: torch.Tensor | None) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError(f"{what}: tensors must be on a CUDA device (no CPU path), got {t.device}")
+
+
+def require_dtype(what: str, dtype: torch.dtype, *tensors: torch.Tensor | None) -> None:
+    for t in tensors:
+        if t is not None and t.dtype != dtype:
+            raise RuntimeError(f"{what}: expected {dtype}, got {t.dtype}")
+
+
+def device_error() -> int:
+    """The library's device error word on the current device (0 = no bounded wait gave up)."""
+    code = I32(0)
+    call("dk_device_error", ctypes.byref(code))
+    return code.value
+
+
+def clear_device_error() -> None:
+    call("dk_clear_device_error")
+
+
+def set_pdl(enabled: bool) -> None:
+    call("dk_set_pdl", int(bool(enabled)))

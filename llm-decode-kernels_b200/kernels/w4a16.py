@@ -1,0 +1,82 @@
+"""W4A16 matmul: y = x @ dequant(W).T (+ bias), int4 weights, fp16 activations, fp32 accumulation.
+
+Same entry point and weight format as the reference's kernels/w4a16.py:301-330. The Triton paths
+(direct / split-K GEMM, GEMV, timed per-shape picker) are replaced by libdecodek's sm_100a kernel,
+which chooses its column tile and cluster split-K from a static cost model - no timing runs inside
+the first call, so the first call may happen under CUDA-graph capture.
+
+`config` keeps the reference's Triton-style dict: `SPLIT_K` maps to the cluster split-K factor,
+`BLOCK_N` (32/64/128) to the column tile; other keys (BLOCK_M, BLOCK_K, GROUP_M, GEMV, FACTORED)
+name Triton tiling choices that have no meaning here and are accepted and ignored. Two extra keys:
+`STATIC_WEIGHTS` (the weights are constant, so the kernel may prefetch them before the previous
+kernel finishes) and `GENERIC` (force the any-alignment kernel).
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from kernels import _lib
+
+_choices: dict[tuple, dict] = {}  # (m_key, N, K, bias) -> config used (export/import_choices)
+
+
+def _config(config: dict | None) -> _lib.MatmulConfig:
+    c = _lib.MatmulConfig(0, 0, 0, 0)
+    if not config:
+        return c
+    split = int(config.get("SPLIT_K", 0) or 0)
+    if split > 8:
+        raise RuntimeError(f"w4a16_matmul: SPLIT_K={split} exceeds the cluster limit of 8")
+    c.split_k = max(split, 0)
+    bn = int(config.get("BLOCK_N", 0) or 0)
+    c.block_n = bn if bn in (32, 64, 128) else 0
+    c.flags = (_lib.FLAG_STATIC_WEIGHTS if config.get("STATIC_WEIGHTS") else 0) | (
+        _lib.FLAG_GENERIC if config.get("GENERIC") else 0)
+    return c
+
+
+def w4a16_matmul(x, qweight, scales, zeros, group_size=128, bias=None, config=None):
+    """y = x @ dequant(W).T (+ bias). x: [..., K] fp16. Returns [..., N] in x's dtype."""
+    K = x.shape[-1]
+    N = qweight.shape[1]
+    assert qweight.shape[0] * 8 == K and K % group_size == 0
+    _lib.require_cuda("w4a16_matmul", x, qweight, scales, zeros, bias)
+    _lib.require_dtype("w4a16_matmul", torch.float16, x, scales, zeros, bias)
+    _lib.require_dtype("w4a16_matmul", torch.int32, qweight)
+    x2 = x.reshape(-1, K)
+    if x2.stride(1) != 1:
+        x2 = x2.contiguous()
+    qweight, scales, zeros = qweight.contiguous(), scales.contiguous(), zeros.contiguous()
+    if bias is not None:
+        bias = bias.contiguous()
+    M = x2.shape[0]
+    out = torch.empty((M, N), dtype=x.dtype, device=x.device)
+    cfg = _config(config)
+    _lib.call("dk_w4a16_matmul", _lib.ptr(x2), x2.stride(0), _lib.ptr(qweight), _lib.ptr(scales),
+              _lib.ptr(zeros), _lib.ptr(bias), _lib.ptr(out), out.stride(0), M, N, K, group_size,
+              ctypes.byref(cfg), _lib.stream_of(x))
+    key = (min(1 << max(M - 1, 0).bit_length(), 4096), N, K, bias is not None)
+    if key not in _choices:
+        _choices[key] = {"SPLIT_K": cfg.split_k or "auto", "BLOCK_N": cfg.block_n or "auto"}
+    return out.view(*x.shape[:-1], N)
+
+
+def export_choices() -> dict:
+    """Per-shape configs used so far (reference kernels/w4a16.py:333-335)."""
+    return {",".join(map(str, k)): v for k, v in _choices.items()}
+
+
+def import_choices(choices: dict) -> None:
+    """Accepts the reference's format; the cost model makes the choice deterministic already
+    (reference kernels/w4a16.py:338-342)."""
+    for k, v in choices.items():
+        m, n, kk, b = k.split(",")
+        _choices[(int(m), int(n), int(kk), b == "True")] = v
+
+
+def best_configs() -> dict:
+    """Choices so far, for results JSON (reference kernels/w4a16.py:345-355)."""
+    return {"decode_path": {str(k): v for k, v in _choices.items()}}

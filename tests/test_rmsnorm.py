@@ -1,0 +1,87 @@
+"""Fused RMSNorm (kernels.rmsnorm.rmsnorm, C-ABI dk_rmsnorm) vs the oracle: the residual output
+must be bit-exact (same fp16 add, reference tests/test_rmsnorm.py:30), the normalized output
+within 1 fp16 ulp of the oracle (same rounding steps, only the fp32 sum order differs) and within
+the reference's 1e-2 tolerance."""
+
+import numpy as np
+import pytest
+import torch
+
+from _util import ELEMWISE_TOL, bits16, to_cuda
+from oracle import ref
+
+pytestmark = pytest.mark.gpu
+
+SMALL = [(1, 128), (3, 1000), (5, 1536)]
+LARGE = [(1, 1536), (16, 1536), (2048, 1536), (16, 4096), (4096, 1536), (2048, 8192), (7, 8960)]
+
+
+def _inputs(M, N, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(M, N, generator=g).half().numpy()
+    r = torch.randn(M, N, generator=g).half().numpy()
+    w = (1 + 0.05 * torch.randn(N, generator=g)).half().numpy()
+    return x, r, w
+
+
+def _ulps(a, b):
+    a = bits16(a).astype(np.int32)
+    b = bits16(b).astype(np.int32)
+    a = np.where(a & 0x8000, 0x8000 - a, a)
+    b = np.where(b & 0x8000, 0x8000 - b, b)
+    return np.abs(a - b)
+
+
+def _check(M, N):
+    from kernels.rmsnorm import rmsnorm
+
+    x, r, w = _inputs(M, N)
+    xc, rc, wc = to_cuda(x, r, w)
+    out = rmsnorm(xc, wc, 1e-6)
+    o_ref = ref.rmsnorm_ref(x, w, 1e-6)
+    assert _ulps(out, o_ref).max() <= 1
+    np.testing.assert_allclose(out.float().cpu().numpy(), o_ref.astype(np.float32), **ELEMWISE_TOL)
+    out, res = rmsnorm(xc, wc, 1e-6, residual=rc)
+    o_ref, r_ref = ref.rmsnorm_ref(x, w, 1e-6, residual=r)
+    assert np.array_equal(bits16(res), bits16(r_ref))
+    assert _ulps(out, o_ref).max() <= 1
+
+
+@pytest.mark.parametrize("M,N", SMALL + LARGE)
+def test_rmsnorm(M, N):
+    _check(M, N)
+
+
+def test_rmsnorm_golden(golden):
+    from kernels.rmsnorm import rmsnorm
+
+    g = golden("norm_act")
+    for i in range(4):
+        x, r, w = to_cuda(g[f"rms{i}_x"], g[f"rms{i}_r"], g[f"rms{i}_w"])
+        assert _ulps(rmsnorm(x, w, 1e-6), g[f"rms{i}_out"]).max() <= 1
+        out, res = rmsnorm(x, w, 1e-6, residual=r)
+        assert np.array_equal(bits16(res), bits16(g[f"rms{i}_res"]))
+        assert _ulps(out, g[f"rms{i}_out_res"]).max() <= 1
+
+
+def test_rmsnorm_3d_input():
+    from kernels.rmsnorm import rmsnorm
+
+    x = torch.randn(2, 3, 256).half()
+    w = torch.ones(256).half()
+    out = rmsnorm(x.cuda(), w.cuda())
+    assert out.shape == (2, 3, 256)
+    assert _ulps(out, ref.rmsnorm_ref(x.numpy(), w.numpy())).max() <= 1
+
+
+def test_rmsnorm_strided_rows():
+    from kernels.rmsnorm import rmsnorm
+
+    x, r, w = _inputs(4, 1536)
+    big = np.zeros((4, 2048), dtype=np.float16)
+    big[:, 8:1544] = x  # row stride 2048, offset 16 bytes
+    bc, rc, wc = to_cuda(big, r, w)
+    out, res = rmsnorm(bc[:, 8:1544], wc, 1e-6, residual=rc)
+    o_ref, r_ref = ref.rmsnorm_ref(x, w, 1e-6, residual=r)
+    assert np.array_equal(bits16(res), bits16(r_ref))
+    assert _ulps(out, o_ref).max() <= 1
