@@ -47,8 +47,8 @@ typedef struct CUstream_st* dk_stream_t; /* same type as cudaStream_t */
 
 /* Optional per-call tuning; zero fields mean "choose automatically". */
 typedef struct dk_matmul_config {
-  int32_t split_k; /* number of K slices reduced inside a thread-block cluster (1..8) */
-  int32_t block_n; /* output columns per CTA (32, 64 or 128) */
+  int32_t split_k; /* K slices reduced inside a thread-block cluster (1..8; clamped to what K allows) */
+  int32_t block_n; /* output columns per CTA tile: 128 or 256 (other values mean automatic) */
   int32_t flags;   /* DK_FLAG_* */
   int32_t reserved;
 } dk_matmul_config;

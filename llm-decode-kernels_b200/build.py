@@ -72,7 +72,7 @@ def build(force: bool = False, debug: bool = False, verbose: bool = False) -> Pa
         objs = list(ex.map(compile_one, sources))
     if force or _stale(LIB, objs):
         tmp = LIB.with_suffix(f".{os.getpid()}.tmp")
-        cmd = [cc, *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-lcuda"]
+        cmd = [cc, *ARCH, "-shared", "-o", str(tmp), *map(str, objs)]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

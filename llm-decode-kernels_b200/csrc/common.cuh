@@ -115,6 +115,21 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
   return p;
 }
 
+// 2-D tiled TMA load (no multicast) of box {x, y} of `map` into this CTA's shared memory.
+// x is the innermost coordinate in elements; callers keep x * element size a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, "
+      "{%2, %3}], [%4];" ::"r"(smem_addr(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
 // ------------------------------------------------------------- programmatic dependent launch
 // Wait until the preceding kernel on the stream (if it was launched as our PDL primary) has
 // completed and its writes are visible. A no-op when there is no such kernel.
@@ -238,6 +253,12 @@ cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
 
 // Global PDL switch (dk_set_pdl); on by default.
 bool pdl_enabled();
+
+// 2-D tensor map for TMA: `inner` x `outer` elements, rows `row_bytes` apart, box
+// `box_inner` x `box_outer`. Returns false (with dk_last_error set) if the driver rejects it.
+bool make_tensor_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint64_t inner,
+                        uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                        CUtensorMapSwizzle swizzle);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

@@ -5,8 +5,9 @@ Same entry point and weight format as the reference's kernels/w4a16.py:301-330. 
 which chooses its column tile and cluster split-K from a static cost model - no timing runs inside
 the first call, so the first call may happen under CUDA-graph capture.
 
-`config` keeps the reference's Triton-style dict: `SPLIT_K` maps to the cluster split-K factor,
-`BLOCK_N` (32/64/128) to the column tile; other keys (BLOCK_M, BLOCK_K, GROUP_M, GEMV, FACTORED)
+`config` keeps the reference's Triton-style dict: `SPLIT_K` maps to the cluster split-K factor
+(clamped to what K allows), `BLOCK_N` (128 or 256; other values mean automatic) to the column
+tile of a CTA; other keys (BLOCK_M, BLOCK_K, GROUP_M, GEMV, FACTORED)
 name Triton tiling choices that have no meaning here and are accepted and ignored. Two extra keys:
 `STATIC_WEIGHTS` (the weights are constant, so the kernel may prefetch them before the previous
 kernel finishes) and `GENERIC` (force the any-alignment kernel).
@@ -32,7 +33,7 @@ def _config(config: dict | None) -> _lib.MatmulConfig:
         raise RuntimeError(f"w4a16_matmul: SPLIT_K={split} exceeds the cluster limit of 8")
     c.split_k = max(split, 0)
     bn = int(config.get("BLOCK_N", 0) or 0)
-    c.block_n = bn if bn in (32, 64, 128) else 0
+    c.block_n = bn if bn in (128, 256) else 0
     c.flags = (_lib.FLAG_STATIC_WEIGHTS if config.get("STATIC_WEIGHTS") else 0) | (
         _lib.FLAG_GENERIC if config.get("GENERIC") else 0)
     return c

@@ -1,7 +1,8 @@
 """Fused RMSNorm (kernels.rmsnorm.rmsnorm, C-ABI dk_rmsnorm) vs the oracle: the residual output
 must be bit-exact (same fp16 add, reference tests/test_rmsnorm.py:30), the normalized output
-within 1 fp16 ulp of the oracle (same rounding steps, only the fp32 sum order differs) and within
-the reference's 1e-2 tolerance."""
+within 2 fp16 ulps of the oracle (same rounding steps; the fp32 sum order differs, which can move
+the normalized value by one ulp before the fp16 multiply by the weight) and within the reference's
+1e-2 tolerance."""
 
 import numpy as np
 import pytest
@@ -39,12 +40,12 @@ def _check(M, N):
     xc, rc, wc = to_cuda(x, r, w)
     out = rmsnorm(xc, wc, 1e-6)
     o_ref = ref.rmsnorm_ref(x, w, 1e-6)
-    assert _ulps(out, o_ref).max() <= 1
+    assert _ulps(out, o_ref).max() <= 2
     np.testing.assert_allclose(out.float().cpu().numpy(), o_ref.astype(np.float32), **ELEMWISE_TOL)
     out, res = rmsnorm(xc, wc, 1e-6, residual=rc)
     o_ref, r_ref = ref.rmsnorm_ref(x, w, 1e-6, residual=r)
     assert np.array_equal(bits16(res), bits16(r_ref))
-    assert _ulps(out, o_ref).max() <= 1
+    assert _ulps(out, o_ref).max() <= 2
 
 
 @pytest.mark.parametrize("M,N", SMALL + LARGE)
@@ -58,10 +59,10 @@ def test_rmsnorm_golden(golden):
     g = golden("norm_act")
     for i in range(4):
         x, r, w = to_cuda(g[f"rms{i}_x"], g[f"rms{i}_r"], g[f"rms{i}_w"])
-        assert _ulps(rmsnorm(x, w, 1e-6), g[f"rms{i}_out"]).max() <= 1
+        assert _ulps(rmsnorm(x, w, 1e-6), g[f"rms{i}_out"]).max() <= 2
         out, res = rmsnorm(x, w, 1e-6, residual=r)
         assert np.array_equal(bits16(res), bits16(g[f"rms{i}_res"]))
-        assert _ulps(out, g[f"rms{i}_out_res"]).max() <= 1
+        assert _ulps(out, g[f"rms{i}_out_res"]).max() <= 2
 
 
 def test_rmsnorm_3d_input():
@@ -71,7 +72,7 @@ def test_rmsnorm_3d_input():
     w = torch.ones(256).half()
     out = rmsnorm(x.cuda(), w.cuda())
     assert out.shape == (2, 3, 256)
-    assert _ulps(out, ref.rmsnorm_ref(x.numpy(), w.numpy())).max() <= 1
+    assert _ulps(out, ref.rmsnorm_ref(x.numpy(), w.numpy())).max() <= 2
 
 
 def test_rmsnorm_strided_rows():
@@ -84,4 +85,4 @@ def test_rmsnorm_strided_rows():
     out, res = rmsnorm(bc[:, 8:1544], wc, 1e-6, residual=rc)
     o_ref, r_ref = ref.rmsnorm_ref(x, w, 1e-6, residual=r)
     assert np.array_equal(bits16(res), bits16(r_ref))
-    assert _ulps(out, o_ref).max() <= 1
+    assert _ulps(out, o_ref).max() <= 2
