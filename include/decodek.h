@@ -44,11 +44,15 @@ typedef struct CUstream_st* dk_stream_t; /* same type as cudaStream_t */
                                     stream: the kernel may prefetch them before waiting for the
                                     previous kernel (programmatic dependent launch) */
 #define DK_FLAG_GENERIC 2        /* force the simple (any alignment) kernel; for tests */
+#define DK_FLAG_EXACT_DEQUANT 4  /* round every dequantized weight to fp16 exactly like the
+                                    reference's dequantize-then-matmul ((q - z) * s in fp16) instead
+                                    of the default factored form s * sum(x * (q - z)) in fp32 (the
+                                    reference's FACTORED path, kernels/w4a16.py:116-119) */
 
 /* Optional per-call tuning; zero fields mean "choose automatically". */
 typedef struct dk_matmul_config {
   int32_t split_k; /* K slices reduced inside a thread-block cluster (1..8; clamped to what K allows) */
-  int32_t block_n; /* output columns per CTA tile: 128 or 256 (other values mean automatic) */
+  int32_t block_n; /* output columns per CTA tile: 32, 64, 128 or 256 (other values: automatic) */
   int32_t flags;   /* DK_FLAG_* */
   int32_t reserved;
 } dk_matmul_config;

@@ -32,6 +32,7 @@
 //   weights before the previous kernel on the stream has finished; x is read only after
 //   griddepcontrol.wait.
 #include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <map>
 #include <mutex>
@@ -70,22 +71,123 @@ struct SmemLayout {
   int w_off, sz_off, xs_off, red_off, bar_off, total;
 };
 
+constexpr int kWarps = 8;  // consumer warps per CTA (plus one producer warp)
+
 // Offsets from the 1024-byte aligned base of dynamic shared memory.
 __host__ __device__ inline SmemLayout smem_layout(int cw, int nbuf, int M, int xs_pitch, int split) {
+  const int wpc = kWarps / cw;
   SmemLayout L;
   L.w_off = 0;
   L.sz_off = nbuf * cw * kBoxBytes;
   L.xs_off = L.sz_off + nbuf * cw * 2 * kSZBytes;
   L.red_off = L.xs_off + ((M * xs_pitch + 15) / 16) * 16;
-  L.bar_off = L.red_off + (split > 1 ? M * cw * 32 * 4 : 0);
+  L.bar_off = L.red_off + ((wpc > 1 || split > 1) ? wpc * M * cw * 32 * 4 : 0);
   L.total = L.bar_off + 2 * nbuf * 8;
   return L;
 }
 
-template <int NT, int CW>
-__global__ void __launch_bounds__((CW + 1) * 32, 1)
+// One chunk-stage (32 columns x 32 packed rows) for one warp. EXACT: dequantize to fp16 exactly
+// like the reference and accumulate into acc. Otherwise (factored, the reference's FACTORED
+// numerics, kernels/w4a16.py:116-119): the MMA sums x*(q-z) per group with exact fp16 operands and
+// the group's scale multiplies the fp32 group sum, which saves the fp16 multiply per weight.
+template <int NT, bool EXACT>
+__device__ __forceinline__ void consume_chunk_stage(const uint8_t* __restrict__ wbox, const uint8_t* __restrict__ szb,
+                                                    const uint8_t* __restrict__ xrow, int xs_pitch, int M, int g,
+                                                    int t, float (&acc)[2][NT][4]) {
+  const uint32_t k1024 = 0x64006400u, nk64 = 0xD400D400u, sixteenth = 0x2C002C00u;
+#pragma unroll
+  for (int half = 0; half < kGroupsPerStage; ++half) {
+    const uint2 s4 = *reinterpret_cast<const uint2*>(szb + half * 64 + g * 8);
+    const uint2 z4 = *reinterpret_cast<const uint2*>(szb + kSZBytes + half * 64 + g * 8);
+    const uint32_t zz[4] = {prmt(z4.x, 0, 0x1010), prmt(z4.x, 0, 0x3232), prmt(z4.y, 0, 0x1010),
+                            prmt(z4.y, 0, 0x3232)};
+    uint32_t zA[4], nzB[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      zA[c] = hfma2_rn(zz[c], 0x3C003C00u, k1024);  // z + 1024, exact
+      nzB[c] = hsub2_rn(nk64, zz[c]);                // -64 - z, exact
+    }
+    uint32_t sc[4];
+    float scf[4];
+    float accg[2][NT][4];
+    if constexpr (EXACT) {
+      sc[0] = prmt(s4.x, 0, 0x1010);
+      sc[1] = prmt(s4.x, 0, 0x3232);
+      sc[2] = prmt(s4.y, 0, 0x1010);
+      sc[3] = prmt(s4.y, 0, 0x3232);
+    } else {
+      const __half2 s01 = *reinterpret_cast<const __half2*>(&s4.x);
+      const __half2 s23 = *reinterpret_cast<const __half2*>(&s4.y);
+      scf[0] = __low2float(s01);
+      scf[1] = __high2float(s01);
+      scf[2] = __low2float(s23);
+      scf[3] = __high2float(s23);
+#pragma unroll
+      for (int a = 0; a < 2; ++a)
+#pragma unroll
+        for (int b = 0; b < NT; ++b)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) accg[a][b][c] = 0.f;
+    }
+#pragma unroll
+    for (int st4 = 0; st4 < 4; ++st4) {
+      const int st = half * 4 + st4;
+      const int r = 8 * (st >> 1) + 2 * t + (st & 1);  // packed row within the stage
+      const uint4 wv = *reinterpret_cast<const uint4*>(wbox + r * 128 + ((g ^ (r & 7)) << 4));
+      uint32_t bx[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const int m = nt * 8 + g;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (m < M) v = *reinterpret_cast<const uint4*>(xrow + m * xs_pitch + r * 16);
+        bx[nt][0] = v.x;
+        bx[nt][1] = v.y;
+        bx[nt][2] = v.z;
+        bx[nt][3] = v.w;
+      }
+      const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
+      uint32_t W[4][4];  // [column][nibble pair]: (q - z) (factored) or (q - z) * s (exact)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint32_t w = words[c];
+        const uint32_t w8 = w >> 8;
+        W[c][0] = hsub2_rn(lop3_and_or(w, 0x000F000Fu, k1024), zA[c]);                 // q0, q4
+        W[c][1] = hfma2_rn(lop3_and_or(w, 0x00F000F0u, k1024), sixteenth, nzB[c]);     // q1, q5
+        W[c][2] = hsub2_rn(lop3_and_or(w8, 0x000F000Fu, k1024), zA[c]);                // q2, q6
+        W[c][3] = hfma2_rn(lop3_and_or(w8, 0x00F000F0u, k1024), sixteenth, nzB[c]);    // q3, q7
+        if constexpr (EXACT) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) W[c][i] = hmul2_rn(W[c][i], sc[c]);
+        }
+      }
+      float(&dst)[2][NT][4] = EXACT ? acc : accg;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        // tile 0: MMA rows g <- column 4g, g+8 <- 4g+1 ; tile 1: columns 4g+2, 4g+3
+        mma_16816(dst[0][nt], W[0][0], W[1][0], W[0][1], W[1][1], bx[nt][0], bx[nt][1]);
+        mma_16816(dst[0][nt], W[0][2], W[1][2], W[0][3], W[1][3], bx[nt][2], bx[nt][3]);
+        mma_16816(dst[1][nt], W[2][0], W[3][0], W[2][1], W[3][1], bx[nt][0], bx[nt][1]);
+        mma_16816(dst[1][nt], W[2][2], W[3][2], W[2][3], W[3][3], bx[nt][2], bx[nt][3]);
+      }
+    }
+    if constexpr (!EXACT) {
+#pragma unroll
+      for (int tile = 0; tile < 2; ++tile)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[tile][nt][e] = fmaf(scf[2 * tile + (e >> 1)], accg[tile][nt][e], acc[tile][nt][e]);
+    }
+  }
+}
+
+// CW chunks (32 columns each) per tile; kWarps / CW warps per chunk split the tile's stages
+// round-robin and meet in shared memory at the end of the tile.
+template <int NT, int CW, bool EXACT>
+__global__ void __launch_bounds__((kWarps + 1) * 32, 3 - NT)  // M <= 8: two CTAs per SM
     w4a16_gemv_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap ms,
                       const __grid_constant__ CUtensorMap mz, const GemvParams p) {
+  constexpr int WPC = kWarps / CW;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = gridDim.y;
@@ -119,7 +221,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
   pdl_trigger();
 
   bool ok = true;
-  if (warp == CW) {
+  if (warp == kWarps) {
     // ---------------------------------------------------------------- producer warp
     if (!p.static_weights) pdl_wait();
     if (lane == 0) {
@@ -147,7 +249,6 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
       }
     }
     __syncwarp();
-    if (p.static_weights) pdl_wait();
   } else {
     // ---------------------------------------------------------------- consumer warps
     pdl_wait();  // x comes from the previous kernel
@@ -155,7 +256,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
       // stage x[:, K slice] into shared memory, 8-element blocks permuted to (0,4,1,5,2,6,3,7)
       const int kb0 = s_begin * kStageRows;  // first packed row (block of 8 K values)
       const int nblk = nst * kStageRows;
-      for (int i = threadIdx.x; i < p.M * nblk; i += CW * 32) {
+      for (int i = threadIdx.x; i < p.M * nblk; i += kWarps * 32) {
         const int m = i / nblk, b = i % nblk;
         const int k = (kb0 + b) * 8;
         uint4 v = make_uint4(0, 0, 0, 0);
@@ -167,15 +268,17 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
         o.w = prmt(v.y, v.w, 0x7632);  // (x3, x7)
         *reinterpret_cast<uint4*>(smem + L.xs_off + m * p.xs_pitch + b * 16) = o;
       }
-      asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");
+      asm volatile("bar.sync 1, %0;" ::"r"(kWarps * 32) : "memory");
     }
     const int g = lane >> 2;  // MMA group: A rows g, g+8 ; B column g
     const int t = lane & 3;   // thread in group: K slots 2t.., 2t+8..
-    const uint32_t k1024 = 0x64006400u, nk64 = 0xD400D400u, sixteenth = 0x2C002C00u;
-    int it = 0;
-    for (int tile = c_begin; tile < c_end && ok; tile += CW) {
+    const int slot = warp % CW;  // chunk of the tile this warp works on
+    const int phase = warp / CW;  // which of the tile's stages (round-robin over WPC warps)
+    float* red = reinterpret_cast<float*>(smem + L.red_off);
+    int tile_idx = 0;
+    for (int tile = c_begin; tile < c_end; tile += CW, ++tile_idx) {
       const int nch = min(CW, c_end - tile);
-      const bool active = warp < nch;
+      const bool active = slot < nch;
       float acc[2][NT][4];
 #pragma unroll
       for (int a = 0; a < 2; ++a)
@@ -184,84 +287,25 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
 #pragma unroll
           for (int c = 0; c < 4; ++c) acc[a][b][c] = 0.f;
 
-      for (int s = s_begin; s < s_end; ++s, ++it) {
+      for (int ls = phase; ls < nst && ok; ls += WPC) {
+        const int it = tile_idx * nst + ls;
         const int buf = it % p.nbuf;
         if (!mbar_wait(&full[buf], (it / p.nbuf) & 1, p.err, DK_DEVERR_WAIT_FULL)) {
           ok = false;
           break;
         }
-        if (active) {
-          const uint8_t* wbox = smem + L.w_off + (buf * CW + warp) * kBoxBytes;
-          const uint8_t* szb = smem + L.sz_off + (buf * CW + warp) * 2 * kSZBytes;
-          const uint8_t* xrow = smem + L.xs_off + (s - s_begin) * kStageRows * 16;
-#pragma unroll
-          for (int half = 0; half < kGroupsPerStage; ++half) {
-            // dequant constants of this group for columns 4g..4g+3: zA = 1024+z, nzB = -(64+z)
-            const uint2 s4 = *reinterpret_cast<const uint2*>(szb + half * 64 + g * 8);
-            const uint2 z4 = *reinterpret_cast<const uint2*>(szb + kSZBytes + half * 64 + g * 8);
-            uint32_t zA[4], nzB[4], sc[4];
-            const uint32_t zz[4] = {prmt(z4.x, 0, 0x1010), prmt(z4.x, 0, 0x3232), prmt(z4.y, 0, 0x1010),
-                                    prmt(z4.y, 0, 0x3232)};
-            sc[0] = prmt(s4.x, 0, 0x1010);
-            sc[1] = prmt(s4.x, 0, 0x3232);
-            sc[2] = prmt(s4.y, 0, 0x1010);
-            sc[3] = prmt(s4.y, 0, 0x3232);
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              zA[c] = hfma2_rn(zz[c], 0x3C003C00u, k1024);  // z*1 + 1024, exact
-              nzB[c] = hsub2_rn(nk64, zz[c]);                // -64 - z, exact
-            }
-#pragma unroll
-            for (int st4 = 0; st4 < 4; ++st4) {
-              const int st = half * 4 + st4;
-              const int r = 8 * (st >> 1) + 2 * t + (st & 1);  // packed row within the stage
-              const uint4 wv = *reinterpret_cast<const uint4*>(wbox + r * 128 + ((g ^ (r & 7)) << 4));
-              uint32_t bx[NT][4];
-#pragma unroll
-              for (int nt = 0; nt < NT; ++nt) {
-                const int m = nt * 8 + g;
-                uint4 v = make_uint4(0, 0, 0, 0);
-                if (m < p.M) v = *reinterpret_cast<const uint4*>(xrow + m * p.xs_pitch + r * 16);
-                bx[nt][0] = v.x;
-                bx[nt][1] = v.y;
-                bx[nt][2] = v.z;
-                bx[nt][3] = v.w;
-              }
-              const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
-              uint32_t W[4][4];  // [column][nibble pair]
-#pragma unroll
-              for (int c = 0; c < 4; ++c) {
-                const uint32_t w = words[c];
-                const uint32_t w8 = w >> 8;
-                const uint32_t p0 = lop3_and_or(w, 0x000F000Fu, k1024);   // 1024 + (q0, q4)
-                const uint32_t p1 = lop3_and_or(w, 0x00F000F0u, k1024);   // 1024 + 16*(q1, q5)
-                const uint32_t p2 = lop3_and_or(w8, 0x000F000Fu, k1024);  // 1024 + (q2, q6)
-                const uint32_t p3 = lop3_and_or(w8, 0x00F000F0u, k1024);  // 1024 + 16*(q3, q7)
-                W[c][0] = hmul2_rn(hsub2_rn(p0, zA[c]), sc[c]);
-                W[c][1] = hmul2_rn(hfma2_rn(p1, sixteenth, nzB[c]), sc[c]);
-                W[c][2] = hmul2_rn(hsub2_rn(p2, zA[c]), sc[c]);
-                W[c][3] = hmul2_rn(hfma2_rn(p3, sixteenth, nzB[c]), sc[c]);
-              }
-#pragma unroll
-              for (int nt = 0; nt < NT; ++nt) {
-                // tile 0: MMA rows g <- column 4g, g+8 <- 4g+1 ; tile 1: columns 4g+2, 4g+3
-                mma_16816(acc[0][nt], W[0][0], W[1][0], W[0][1], W[1][1], bx[nt][0], bx[nt][1]);
-                mma_16816(acc[0][nt], W[0][2], W[1][2], W[0][3], W[1][3], bx[nt][2], bx[nt][3]);
-                mma_16816(acc[1][nt], W[2][0], W[3][0], W[2][1], W[3][1], bx[nt][0], bx[nt][1]);
-                mma_16816(acc[1][nt], W[2][2], W[3][2], W[2][3], W[3][3], bx[nt][2], bx[nt][3]);
-              }
-            }
-          }
-        }
+        if (active)
+          consume_chunk_stage<NT, EXACT>(smem + L.w_off + (buf * CW + slot) * kBoxBytes,
+                                         smem + L.sz_off + (buf * CW + slot) * 2 * kSZBytes,
+                                         smem + L.xs_off + ls * kStageRows * 16, p.xs_pitch, p.M, g, t, acc);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[buf]);
       }
-      if (!ok) break;
 
       // ---------------------------------------------------------------- tile epilogue
-      const int n0 = (tile + warp) * 32 + 4 * g;
-      if (S == 1) {
-        if (active) {
+      if (WPC == 1 && S == 1) {
+        if (active && ok) {
+          const int n0 = (tile + slot) * 32 + 4 * g;
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -278,7 +322,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
             }
         }
       } else {
-        float* red = reinterpret_cast<float*>(smem + L.red_off);
+        // partial sums of the WPC warps of each chunk meet in shared memory: red[phase][m][col]
         if (active) {
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt)
@@ -286,20 +330,38 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1)
             for (int e = 0; e < 2; ++e) {
               const int m = nt * 8 + 2 * t + e;
               if (m >= p.M) continue;
-              float* row = red + m * CW * 32 + warp * 32 + 4 * g;
+              float* row = red + (phase * p.M + m) * CW * 32 + slot * 32 + 4 * g;
               row[0] = acc[0][nt][e];
               row[1] = acc[0][nt][2 + e];
               row[2] = acc[1][nt][e];
               row[3] = acc[1][nt][2 + e];
             }
         }
+        asm volatile("bar.sync 1, %0;" ::"r"(kWarps * 32) : "memory");
+        const int ncols = nch * 32;
+        for (int e = threadIdx.x; e < p.M * ncols; e += kWarps * 32) {
+          const int m = e / ncols, col = e % ncols;
+          float v = red[m * CW * 32 + col];
+#pragma unroll
+          for (int j = 1; j < WPC; ++j) v += red[(j * p.M + m) * CW * 32 + col];
+          if (S == 1) {
+            const int n = tile * 32 + col;
+            if (n < p.N) {
+              if (p.bias != nullptr) v += __half2float(p.bias[n]);
+              p.y[m * p.ldy + n] = __float2half_rn(v);
+            }
+          } else {
+            red[m * CW * 32 + col] = v;  // this rank's partial, read by the cluster below
+          }
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(kWarps * 32) : "memory");
       }
     }
   }
 
   // ------------------------------------------------------------------ split-K reduction / exit
   if (__syncthreads_or(!ok)) {
-    if (warp == CW && lane == 0) {
+    if (warp == kWarps && lane == 0) {
       // wait (bounded) for the copies still in flight before the shared memory goes away
       const uint64_t t0 = globaltimer_ns();
       for (int b = 0; b < p.nbuf; ++b)
@@ -360,46 +422,61 @@ __global__ void w4a16_generic_kernel(const __half* __restrict__ x, int64_t ldx,
   y[m * ldy + n] = __float2half_rn(acc);
 }
 
-template <int NT, int CW>
-void set_smem_attr() {
+using GemvKernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const GemvParams);
+
+// All compiled variants: [NT-1][log2(CW)][EXACT].
+GemvKernel variant(int nt, int cw, bool exact) {
+  static const GemvKernel table[2][4][2] = {
+      {{w4a16_gemv_kernel<1, 1, false>, w4a16_gemv_kernel<1, 1, true>},
+       {w4a16_gemv_kernel<1, 2, false>, w4a16_gemv_kernel<1, 2, true>},
+       {w4a16_gemv_kernel<1, 4, false>, w4a16_gemv_kernel<1, 4, true>},
+       {w4a16_gemv_kernel<1, 8, false>, w4a16_gemv_kernel<1, 8, true>}},
+      {{w4a16_gemv_kernel<2, 1, false>, w4a16_gemv_kernel<2, 1, true>},
+       {w4a16_gemv_kernel<2, 2, false>, w4a16_gemv_kernel<2, 2, true>},
+       {w4a16_gemv_kernel<2, 4, false>, w4a16_gemv_kernel<2, 4, true>},
+       {w4a16_gemv_kernel<2, 8, false>, w4a16_gemv_kernel<2, 8, true>}}};
+  const int lg = cw == 1 ? 0 : cw == 2 ? 1 : cw == 4 ? 2 : 3;
+  return table[nt - 1][lg][exact ? 1 : 0];
+}
+
+// Opt every variant in to the device's shared-memory limit (once per device).
+void set_smem_attrs() {
+  static std::mutex mu;
   static bool done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
   if (dev < 64 && !done[dev]) {
-    cudaFuncSetAttribute(w4a16_gemv_kernel<NT, CW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         device_info().max_smem_optin);
+    for (int nt = 1; nt <= 2; ++nt)
+      for (int cw = 1; cw <= 8; cw *= 2)
+        for (int ex = 0; ex < 2; ++ex)
+          cudaFuncSetAttribute(variant(nt, cw, ex), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               device_info().max_smem_optin);
     done[dev] = true;
   }
 }
 
-// Resident CTAs per SM for one kernel variant and dynamic shared memory size (registers, threads
-// and shared memory all counted by the runtime's occupancy calculator).
-int occupancy_uncached(int nt, int cw, size_t smem) {
-  int n = 0;
-  cudaError_t e;
-  if (nt == 1 && cw == 4) set_smem_attr<1, 4>(), e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, w4a16_gemv_kernel<1, 4>, 160, smem);
-  else if (nt == 1) set_smem_attr<1, 8>(), e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, w4a16_gemv_kernel<1, 8>, 288, smem);
-  else if (cw == 4) set_smem_attr<2, 4>(), e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, w4a16_gemv_kernel<2, 4>, 160, smem);
-  else set_smem_attr<2, 8>(), e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, w4a16_gemv_kernel<2, 8>, 288, smem);
-  if (e != cudaSuccess) {
-    cudaGetLastError();
-    return 1;
-  }
-  return std::max(n, 1);
-}
-
+// Resident CTAs per SM of one variant at a given dynamic shared memory size (registers, threads
+// and shared memory all counted by the runtime's occupancy calculator); memoized.
 int occupancy(int nt, int cw, size_t smem) {
   static std::mutex mu;
-  static std::map<std::tuple<int, int, int, size_t>, int> cache;
+  static std::map<std::tuple<int, int, size_t>, int> cache;
   int dev = 0;
   cudaGetDevice(&dev);
-  const auto key = std::make_tuple(dev, nt * 16 + cw, 0, smem);
+  const auto key = std::make_tuple(dev, nt * 16 + cw, smem);
   {
     std::lock_guard<std::mutex> lock(mu);
     auto it = cache.find(key);
     if (it != cache.end()) return it->second;
   }
-  const int n = occupancy_uncached(nt, cw, smem);
+  set_smem_attrs();
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, variant(nt, cw, false), (kWarps + 1) * 32, smem) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    n = 1;
+  }
+  n = std::max(n, 1);
   std::lock_guard<std::mutex> lock(mu);
   cache[key] = n;
   return n;
@@ -411,18 +488,70 @@ struct Choice {
   double cost;
 };
 
-constexpr size_t kSmemBudget = 110 * 1024;  // two CTAs per SM fit, with room for the next kernel
+constexpr size_t kSmemBudget = 110 * 1024;  // two CTAs per SM fit
 constexpr size_t kXsBudget = 64 * 1024;
 
 int xs_pitch_for(int split_stages) { return split_stages * kStageRows * 16 + kXsPad; }
 
-// Choose CW (4 or 8 consumer warps), the cluster split S and the ring depth with a small cost
-// model: the busiest SM's bytes at its share of HBM bandwidth, plus latency terms per stage and
-// for the cluster reduction. cfg->split_k / cfg->block_n (= 32*CW) override.
-Choice choose_uncached(int M, int N, int K, const dk_matmul_config* cfg);
+// Cost model (microseconds) for one launch: a fixed launch/fill latency, then the slowest of the
+// busiest SM's HBM share, its instruction throughput, and one warp's serial chain of
+// chunk-stages; plus the cluster and in-CTA reductions.
+double model_cost(const DeviceInfo& dev, int chunks, int sps, int cw, int split, int nctas) {
+  const int wpc = kWarps / cw;
+  const double chunks_per_cta = std::ceil(static_cast<double>(chunks) / nctas);
+  const double tiles_per_cta = std::ceil(chunks_per_cta / cw);
+  const double ctas_per_sm = std::ceil(static_cast<double>(nctas) * split / dev.num_sms);
+  const double cs_sm = ctas_per_sm * chunks_per_cta * sps;
+  const double t_mem = cs_sm * kChunkStageBytes / (6.4e12 / dev.num_sms) * 1e6;
+  const double t_issue = cs_sm / 10.0;
+  const double t_chain = tiles_per_cta * std::ceil(static_cast<double>(sps) / wpc) * 0.5;
+  return 2.0 + std::max(t_mem, std::max(t_issue, t_chain)) + (split > 1 ? 0.5 : 0.0) +
+         (wpc > 1 ? 0.2 * tiles_per_cta : 0.0);
+}
+
+Choice choose_uncached(int M, int N, int K, const dk_matmul_config* cfg) {
+  const DeviceInfo& dev = device_info();
+  const int stages_total = (K + 256 - 1) / 256;
+  const int chunks = (N + 31) / 32;
+  const int nt = M <= 8 ? 1 : 2;
+  Choice best = {0, 0, 0, 0, 0, 1e300};
+  // requested split: clamped to what K allows (every rank needs at least one 256-wide stage)
+  int want_split = (cfg && cfg->split_k > 0) ? std::min(cfg->split_k, std::min(8, stages_total)) : 0;
+  while (want_split > 1 && (want_split - 1) * ((stages_total + want_split - 1) / want_split) >= stages_total)
+    --want_split;
+  const int want_bn = (cfg && (cfg->block_n == 32 || cfg->block_n == 64 || cfg->block_n == 128 ||
+                               cfg->block_n == 256)) ? cfg->block_n : 0;
+  for (int cw = 8; cw >= 1; cw /= 2) {
+    if (want_bn && want_bn != 32 * cw) continue;
+    for (int split = 1; split <= 8; ++split) {
+      if (want_split && want_split != split) continue;
+      if (split > stages_total) break;
+      const int sps = (stages_total + split - 1) / split;
+      if ((split - 1) * sps >= stages_total) continue;  // every rank gets at least one stage
+      const int pitch = xs_pitch_for(sps);
+      if (static_cast<size_t>(M) * pitch > kXsBudget) continue;
+      const int tiles = (chunks + cw - 1) / cw;
+      const int stages_per_cta = sps * (split > 1 ? 1 : (tiles + dev.num_sms - 1) / dev.num_sms);
+      int nbuf = std::min(std::max(stages_per_cta, 2), 16);
+      SmemLayout L = smem_layout(cw, nbuf, M, pitch, split);
+      while (nbuf > 2 && static_cast<size_t>(L.total) + 1024 > kSmemBudget) {
+        --nbuf;
+        L = smem_layout(cw, nbuf, M, pitch, split);
+      }
+      const size_t smem = static_cast<size_t>(L.total) + 1024;
+      if (smem > static_cast<size_t>(dev.max_smem_optin)) continue;
+      const int occ = occupancy(nt, cw, smem);
+      const int nctas = split == 1 ? std::min(chunks, dev.num_sms * occ) : tiles;
+      if (split > 1 && static_cast<long>(nctas) * split > static_cast<long>(dev.num_sms) * occ) continue;
+      const double cost = model_cost(dev, chunks, sps, cw, split, nctas);
+      if (cost < best.cost) best = {cw, split, nbuf, nctas, smem, cost};
+    }
+  }
+  return best;
+}
 
 // Memoized per (device, M, N, K, requested split, requested tile): the choice is a pure function
-// of these, and the calculation queries the occupancy calculator.
+// of these, and computing it queries the occupancy calculator.
 Choice choose(int M, int N, int K, const dk_matmul_config* cfg) {
   static std::mutex mu;
   static std::map<std::tuple<int, int, int, int, int, int>, Choice> cache;
@@ -434,66 +563,24 @@ Choice choose(int M, int N, int K, const dk_matmul_config* cfg) {
     auto it = cache.find(key);
     if (it != cache.end()) return it->second;
   }
-  const Choice c = choose_uncached(M, N, K, cfg);
+  Choice c = choose_uncached(M, N, K, cfg);
+  if (c.cw == 0 && cfg) {  // the requested split / tile does not fit: let the model choose
+    dk_matmul_config auto_cfg = *cfg;
+    auto_cfg.split_k = 0;
+    auto_cfg.block_n = 0;
+    c = choose_uncached(M, N, K, &auto_cfg);
+  }
   std::lock_guard<std::mutex> lock(mu);
   cache[key] = c;
   return c;
 }
 
-Choice choose_uncached(int M, int N, int K, const dk_matmul_config* cfg) {
-  const DeviceInfo& dev = device_info();
-  const int stages_total = (K + 256 - 1) / 256;
-  const int chunks = (N + 31) / 32;
-  Choice best = {0, 0, 0, 0, 0, 1e300};
-  // requested split: clamped to what K allows (every rank needs at least one 256-wide stage)
-  int want_split = (cfg && cfg->split_k > 0) ? std::min(cfg->split_k, std::min(8, stages_total)) : 0;
-  while (want_split > 1 && (want_split - 1) * ((stages_total + want_split - 1) / want_split) >= stages_total)
-    --want_split;
-  const int want_bn = (cfg && (cfg->block_n == 128 || cfg->block_n == 256)) ? cfg->block_n : 0;
-  const int cws[2] = {4, 8};
-  for (int ci = 0; ci < 2; ++ci) {
-    const int cw = cws[ci];
-    if (want_bn && want_bn != 32 * cw) continue;
-    for (int split = 1; split <= 8; ++split) {
-      if (want_split && want_split != split) continue;
-      if (split > stages_total) break;
-      const int sps = (stages_total + split - 1) / split;
-      if ((split - 1) * sps >= stages_total) continue;  // every rank gets at least one stage
-      const int pitch = xs_pitch_for(sps);
-      if (static_cast<size_t>(M) * pitch > kXsBudget) continue;
-      const int tiles = (chunks + cw - 1) / cw;
-      const int per_cta_stages = sps * (split > 1 ? 1 : (tiles + dev.num_sms - 1) / dev.num_sms);
-      int nbuf = std::min(std::max(per_cta_stages, 1), 8);
-      SmemLayout L = smem_layout(cw, nbuf, M, pitch, split);
-      while (nbuf > 2 && static_cast<size_t>(L.total) + 1024 > kSmemBudget) {
-        --nbuf;
-        L = smem_layout(cw, nbuf, M, pitch, split);
-      }
-      const size_t smem = static_cast<size_t>(L.total) + 1024;
-      if (smem > static_cast<size_t>(dev.max_smem_optin)) continue;
-      const int occ = occupancy(M <= 8 ? 1 : 2, cw, smem);
-      const int nctas = split == 1 ? std::min(chunks, dev.num_sms * occ) : tiles;
-      const long total = static_cast<long>(nctas) * split;
-      if (split > 1 && total > static_cast<long>(dev.num_sms) * occ) continue;  // clusters: one wave
-      const long per_sm = (total + dev.num_sms - 1) / dev.num_sms;
-      const long chunks_per_cta = (chunks + nctas - 1) / nctas;
-      const long rounds = (chunks_per_cta + cw - 1) / cw;
-      const double bytes_sm = static_cast<double>(per_sm) * chunks_per_cta * sps * kChunkStageBytes;
-      const double cost = bytes_sm / (6.4e12 / dev.num_sms) * 1e9 + 35.0 * sps * rounds +
-                          (split > 1 ? 700.0 : 0.0) + 150.0 * per_sm;
-      if (cost < best.cost) best = {cw, split, nbuf, nctas, smem, cost};
-    }
-  }
-  return best;
-}
-
-template <int NT, int CW>
 int launch_gemv(const CUtensorMap& mq, const CUtensorMap& ms, const CUtensorMap& mz, const GemvParams& p,
-                const Choice& c, cudaStream_t stream) {
-  auto kernel = w4a16_gemv_kernel<NT, CW>;
-  set_smem_attr<NT, CW>();
+                const Choice& c, bool exact, cudaStream_t stream) {
+  set_smem_attrs();
+  const GemvKernel kernel = variant(p.M <= 8 ? 1 : 2, c.cw, exact);
   const dim3 grid(c.nctas, c.split, 1);
-  const dim3 block((CW + 1) * 32, 1, 1);
+  const dim3 block((kWarps + 1) * 32, 1, 1);
   cudaError_t e = launch(kernel, grid, block, c.smem, stream, pdl_enabled(), dim3(1, c.split, 1), mq, ms, mz, p);
   if (e != cudaSuccess) return set_error(DK_ERR_CUDA, "w4a16 gemv launch: %s", cudaGetErrorString(e));
   return DK_OK;
@@ -542,15 +629,8 @@ extern "C" int dk_w4a16_matmul(const void* x, int64_t ldx, const int32_t* qweigh
   const DeviceInfo& dev = device_info();
   for (int64_t m0 = 0; m0 < M; m0 += 16) {
     const int mc = static_cast<int>(std::min<int64_t>(16, M - m0));
-    const Choice c1 = choose(mc, static_cast<int>(N), static_cast<int>(K), cfg);
-    Choice c2 = c1;
-    if (c2.cw == 0 && cfg) {  // the requested split/tile does not fit: let the cost model choose
-      dk_matmul_config auto_cfg = *cfg;
-      auto_cfg.split_k = 0;
-      auto_cfg.block_n = 0;
-      c2 = choose(mc, static_cast<int>(N), static_cast<int>(K), &auto_cfg);
-    }
-    if (c2.cw == 0) return set_error(DK_ERR_UNSUPPORTED, "w4a16_matmul: no tile fits (M=%d, K=%lld)", mc, (long long)K);
+    const Choice c = choose(mc, static_cast<int>(N), static_cast<int>(K), cfg);
+    if (c.cw == 0) return set_error(DK_ERR_UNSUPPORTED, "w4a16_matmul: no tile fits (M=%d, K=%lld)", mc, (long long)K);
     GemvParams p;
     p.x = static_cast<const __half*>(x) + m0 * ldx;
     p.ldx = ldx;
@@ -561,15 +641,13 @@ extern "C" int dk_w4a16_matmul(const void* x, int64_t ldx, const int32_t* qweigh
     p.N = static_cast<int>(N);
     p.K = static_cast<int>(K);
     p.stages_total = static_cast<int>((K + 255) / 256);
-    p.split_stages = (p.stages_total + c2.split - 1) / c2.split;
+    p.split_stages = (p.stages_total + c.split - 1) / c.split;
     p.chunks = static_cast<int>((N + 31) / 32);
-    p.nbuf = c2.nbuf;
+    p.nbuf = c.nbuf;
     p.xs_pitch = xs_pitch_for(p.split_stages);
     p.static_weights = (flags & DK_FLAG_STATIC_WEIGHTS) ? 1 : 0;
     p.err = dev.err_word;
-    int rc;
-    if (mc <= 8) rc = c2.cw == 4 ? launch_gemv<1, 4>(mq, ms, mz, p, c2, st) : launch_gemv<1, 8>(mq, ms, mz, p, c2, st);
-    else rc = c2.cw == 4 ? launch_gemv<2, 4>(mq, ms, mz, p, c2, st) : launch_gemv<2, 8>(mq, ms, mz, p, c2, st);
+    const int rc = launch_gemv(mq, ms, mz, p, c, (flags & DK_FLAG_EXACT_DEQUANT) != 0, st);
     if (rc != DK_OK) return rc;
   }
   return DK_OK;

@@ -6,11 +6,14 @@ which chooses its column tile and cluster split-K from a static cost model - no 
 the first call, so the first call may happen under CUDA-graph capture.
 
 `config` keeps the reference's Triton-style dict: `SPLIT_K` maps to the cluster split-K factor
-(clamped to what K allows), `BLOCK_N` (128 or 256; other values mean automatic) to the column
-tile of a CTA; other keys (BLOCK_M, BLOCK_K, GROUP_M, GEMV, FACTORED)
-name Triton tiling choices that have no meaning here and are accepted and ignored. Two extra keys:
-`STATIC_WEIGHTS` (the weights are constant, so the kernel may prefetch them before the previous
-kernel finishes) and `GENERIC` (force the any-alignment kernel).
+(clamped to what K allows), `BLOCK_N` (32, 64, 128 or 256; other values mean automatic) to the
+column tile of a CTA; other Triton tiling keys (BLOCK_M, BLOCK_K, GROUP_M, GEMV) have no meaning
+here and are accepted and ignored. `FACTORED` keeps the reference's meaning: the decode kernel
+computes s * sum(x * (q - z)) per group in fp32 by default (the reference's FACTORED numerics);
+`FACTORED=False` (or `EXACT=True`) rounds every dequantized weight to fp16 first, exactly like the
+reference's dequantize-then-matmul. Extra keys: `STATIC_WEIGHTS` (the weights are constant, so the
+kernel may prefetch them before the previous kernel finishes) and `GENERIC` (force the
+any-alignment kernel, which always rounds like the reference).
 """
 
 from __future__ import annotations
@@ -33,9 +36,10 @@ def _config(config: dict | None) -> _lib.MatmulConfig:
         raise RuntimeError(f"w4a16_matmul: SPLIT_K={split} exceeds the cluster limit of 8")
     c.split_k = max(split, 0)
     bn = int(config.get("BLOCK_N", 0) or 0)
-    c.block_n = bn if bn in (128, 256) else 0
+    c.block_n = bn if bn in (32, 64, 128, 256) else 0
+    exact = bool(config.get("EXACT")) or config.get("FACTORED") is False
     c.flags = (_lib.FLAG_STATIC_WEIGHTS if config.get("STATIC_WEIGHTS") else 0) | (
-        _lib.FLAG_GENERIC if config.get("GENERIC") else 0)
+        _lib.FLAG_GENERIC if config.get("GENERIC") else 0) | (_lib.FLAG_EXACT_DEQUANT if exact else 0)
     return c
 
 

@@ -80,10 +80,35 @@ def test_decode_qwen_shapes(M, N, K):
 
 
 @pytest.mark.parametrize("split", [1, 2, 3, 4, 5, 8])
-@pytest.mark.parametrize("block_n", [128, 256])
-def test_every_tile_and_split(split, block_n):
-    _check(4, 1536, 8960, config={"SPLIT_K": split, "BLOCK_N": block_n})
-    _check(16, 1000, 1024, bias=True, config={"SPLIT_K": split, "BLOCK_N": block_n})
+@pytest.mark.parametrize("block_n", [32, 64, 128, 256])
+@pytest.mark.parametrize("exact", [False, True])
+def test_every_tile_and_split(split, block_n, exact):
+    cfg = {"SPLIT_K": split, "BLOCK_N": block_n, "EXACT": exact}
+    _check(4, 1536, 8960, config=cfg)
+    _check(16, 1000, 1024, bias=True, config=cfg)
+    _check(1, 4096, 512, config=cfg)
+
+
+def _ulps16(a, b):
+    a = np.ascontiguousarray(a, dtype=np.float16).view(np.uint16).astype(np.int32)
+    b = np.ascontiguousarray(b, dtype=np.float16).view(np.uint16).astype(np.int32)
+    a = np.where(a & 0x8000, 0x8000 - a, a)
+    b = np.where(b & 0x8000, 0x8000 - b, b)
+    return np.abs(a - b)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 2048, 1536), (5, 1536, 8960), (16, 17920, 1536)])
+def test_exact_dequant_rounds_like_reference(M, N, K):
+    """With EXACT the kernel dequantizes with the reference's fp16 rounding, so the only
+    difference left is the fp32 summation order: the fp16 output is within one ulp of the
+    reference's fp32 result rounded to fp16."""
+    from kernels.w4a16 import w4a16_matmul
+
+    x, qw, s, z, b = w4_case(M, N, K, bias=True)
+    xc, qc, sc, zc, bc = to_cuda(x, qw, s, z, b)
+    out = w4a16_matmul(xc, qc, sc, zc, bias=bc, config={"EXACT": True}).cpu().numpy()
+    ref = w4_ref(x, qw, s, z, b).astype(np.float16)
+    assert _ulps16(out, ref).max() <= 1
 
 
 def test_lm_head_m1():
