@@ -38,6 +38,7 @@ typedef struct CUstream_st* dk_stream_t; /* same type as cudaStream_t */
 #define DK_DEVERR_NONE 0
 #define DK_DEVERR_WAIT_FULL 1  /* a consumer gave up waiting for a stage's copies */
 #define DK_DEVERR_WAIT_EMPTY 2 /* the producer gave up waiting for a stage to be released */
+#define DK_DEVERR_BAD_POSITION 3 /* decode attention: position outside [0, max_len) (no write done) */
 
 /* dk_matmul_config.flags */
 #define DK_FLAG_STATIC_WEIGHTS 1 /* weights are not written by any kernel still in flight on the
@@ -90,6 +91,16 @@ int dk_w4a16_matmul(const void* x, int64_t ldx, const int32_t* qweight, const vo
                     int64_t N, int64_t K, int64_t group_size, const dk_matmul_config* cfg,
                     dk_stream_t stream);
 
+/* gate_up projection fused with SwiGLU (kernels/e2e/model.py:247 with kernels/swiglu.py:56-61):
+ * qweight/scales/zeros hold the fused [gate; up] weight with 2I output columns; the output
+ * y[M, I] = fp16(silu(fp16(g))) * fp16(u) for g, u = the gate and up halves of x @ dequant(W).T
+ * (+ bias[2I]) - the same roundings as the two separate ops. Needs I % 32 == 0, group_size 128
+ * and 16-byte aligned operands (DK_ERR_UNSUPPORTED otherwise: run the two ops instead). */
+int dk_w4a16_swiglu(const void* x, int64_t ldx, const int32_t* qweight, const void* scales,
+                    const void* zeros, const void* bias, void* y, int64_t ldy, int64_t M,
+                    int64_t I, int64_t K, int64_t group_size, const dk_matmul_config* cfg,
+                    dk_stream_t stream);
+
 /* ---- FP8 e4m3 weight-only format: kernels/fp8.py ------------------------------------------ */
 /* quantize_fp8 (kernels/fp8.py:25-30): w fp16 [N, K] (row stride ldw) -> wq e4m3 [K, N],
  * scale fp16 [N]; per-row absmax / 448 clamped >= 1e-12. Bit-exact with the reference. */
@@ -98,6 +109,13 @@ int dk_quantize_fp8(const void* w, int64_t ldw, uint8_t* wq, void* scale, int64_
 /* dequantize_fp8 (kernels/fp8.py:33-35): -> fp16 [N, K] = fp16(fp32(wq) * fp32(scale)). */
 int dk_dequantize_fp8(const uint8_t* wq, const void* scale, void* w, int64_t N, int64_t K,
                       dk_stream_t stream);
+
+/* w8a16_matmul (kernels/fp8.py:200-223): y[M, N] fp16 = (x[M, K] @ fp16(wq)) * scale (+ bias),
+ * wq e4m3 [K, N] (N contiguous), scale fp16 [N], fp32 accumulation, the scale applied to the
+ * fp32 sum (kernels/fp8.py:81-82). cfg as for dk_w4a16_matmul (split_k, block_n, flags). */
+int dk_w8a16_matmul(const void* x, int64_t ldx, const uint8_t* wq, const void* scale, const void* bias,
+                    void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, const dk_matmul_config* cfg,
+                    dk_stream_t stream);
 
 /* ---- fused RMSNorm (+ residual): kernels/rmsnorm.py ------------------------------------- */
 /* rmsnorm (kernels/rmsnorm.py:44-68): out = w * fp16(h * rsqrt(mean(h^2) + eps)) with
@@ -112,6 +130,19 @@ int dk_rmsnorm(const void* x, int64_t ldx, const void* residual, int64_t ldr, co
  * For the fused [M, 2I] layout pass gate = gu, up = gu + I, ldg = ldu = 2I. */
 int dk_swiglu(const void* gate, int64_t ldg, const void* up, int64_t ldu, void* out, int64_t ldo,
               int64_t M, int64_t I, dk_stream_t stream);
+
+/* ---- decode attention: kernels/e2e/model.py:236-244 for one new token ---------------------- */
+/* RoPE on q and k (x*cos + rotate_half(x)*sin, fp16 rounding per op), append k and v to the cache
+ * at position *pos, and softmax(q k^T / sqrt(head_dim)) v over cache positions 0..*pos, with
+ * grouped-query heads (nq / nkv query heads per kv head). qkv [B, (nq + 2 nkv) * head_dim] is the
+ * fused projection output; caches [B, nkv, max_len, head_dim]; cos, sin [head_dim] for this
+ * position; out [B, nq * head_dim]. `pos` is a device pointer (graph-capturable); a position outside
+ * [0, max_len) writes nothing and sets DK_DEVERR_BAD_POSITION. splits: positions are cut into this
+ * many slices combined inside a thread-block cluster (0 = automatic, max 8). head_dim 128. */
+int dk_decode_attention(const void* qkv, void* k_cache, void* v_cache, const int64_t* pos,
+                        const void* cos, const void* sin, void* out, int64_t B, int64_t nq,
+                        int64_t nkv, int64_t head_dim, int64_t max_len, int32_t splits,
+                        dk_stream_t stream);
 
 #ifdef __cplusplus
 }

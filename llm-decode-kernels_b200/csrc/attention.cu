@@ -1,0 +1,244 @@
+// Decode attention for one new token per sequence: RoPE on q and k, KV-cache append, and softmax
+// attention over the cached positions 0..pos only.
+//
+// Replaces, for T == 1, the reference runner's per-layer sequence (kernels/e2e/model.py:236-244):
+//   q, k = rope(q), rope(k)            x * cos + cat(-x2, x1) * sin, fp16 rounding after each op
+//   k_cache[:, :, pos] = k ; v_cache[:, :, pos] = v
+//   attn = SDPA(q, k_cache, v_cache, mask = keys <= pos, enable_gqa=True)
+// The reference's SDPA reads all `max_len` cached positions every step and masks most of them; this
+// kernel reads positions 0..pos. Scores, softmax and the weighted sum of V are fp32.
+//
+// Grid (n_kv, B, S) with the S CTAs of one (kv head, sequence) forming a thread-block cluster
+// ("split-KV"): each CTA covers a contiguous slice of the positions, keeps its softmax partials
+// (max, sum, unnormalized output) in shared memory, and the cluster combines them through
+// distributed shared memory. The CTA whose slice holds `pos` takes the new token's k, v from
+// registers and writes them to the cache; no other CTA reads position `pos`, so no ordering between
+// CTAs is needed. `pos` is read on the device, so the launch can be captured in a CUDA graph once and
+// replayed for every step.
+#include <algorithm>
+#include <cfloat>
+
+#include "common.cuh"
+
+namespace dk {
+namespace {
+
+constexpr int kHd = 128;     // head dim supported by this kernel (Qwen2.5 1.5B and 7B)
+constexpr int kThreads = 128;
+constexpr int kMaxGroup = 8;  // query heads per kv head
+constexpr int kMaxSplit = 8;
+
+struct AttnParams {
+  const __half* qkv;  // [B, (nq + 2 nkv) * hd]
+  __half* k_cache;    // [B, nkv, max_len, hd]
+  __half* v_cache;
+  const int64_t* pos;  // [1]
+  const __half* cos;   // [hd]
+  const __half* sin;   // [hd]
+  __half* out;         // [B, nq * hd]
+  int nq, nkv, max_len;
+  float scale;
+  int* err;
+};
+
+// RoPE for element d of one head, with the reference's fp16 rounding:
+// x*cos + rot*sin, rot = -x[d+64] (d < 64) or x[d-64] (d >= 64).
+__device__ __forceinline__ __half rope_elem(const __half* x, int d, const __half* cs, const __half* sn) {
+  const __half rot = d < kHd / 2 ? __hneg(x[d + kHd / 2]) : x[d - kHd / 2];
+  return __hadd_rn(__hmul_rn(x[d], cs[d]), __hmul_rn(rot, sn[d]));
+}
+
+template <int G>
+__global__ void __launch_bounds__(kThreads) decode_attention_kernel(const AttnParams p) {
+  __shared__ float qs[G][kHd];          // rotated q (fp32)
+  __shared__ __half knew[kHd], vnew[kHd];
+  __shared__ float part_o[G][kHd];      // this CTA's unnormalized output
+  __shared__ float part_m[G], part_l[G];
+  extern __shared__ float scores[];     // [G][slice]
+
+  pdl_trigger();
+  pdl_wait();
+  const int h = blockIdx.x, b = blockIdx.y, rank = blockIdx.z, S = gridDim.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t pos64 = *p.pos;
+  if (pos64 < 0 || pos64 >= p.max_len) {  // same decision in every CTA of the cluster
+    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
+      record_device_error(p.err, DK_DEVERR_BAD_POSITION);
+    return;
+  }
+  const int L = static_cast<int>(pos64) + 1;  // positions 0..pos
+  const int slice = (L + S - 1) / S;
+  const int j0 = min(rank * slice, L), j1 = min(j0 + slice, L);
+  const int pos = L - 1;
+  const int row = (p.nq + 2 * p.nkv) * kHd;
+  const __half* qrow = p.qkv + static_cast<int64_t>(b) * row;
+  const __half* krow = qrow + p.nq * kHd + h * kHd;
+  const __half* vrow = qrow + (p.nq + p.nkv) * kHd + h * kHd;
+  const int64_t cache_base = (static_cast<int64_t>(b) * p.nkv + h) * p.max_len * kHd;
+  __half* kc = p.k_cache + cache_base;
+  __half* vc = p.v_cache + cache_base;
+
+  for (int d = tid; d < kHd; d += kThreads) {
+    for (int g = 0; g < G; ++g)
+      qs[g][d] = __half2float(rope_elem(qrow + (h * G + g) * kHd, d, p.cos, p.sin)) * p.scale;
+    knew[d] = rope_elem(krow, d, p.cos, p.sin);
+    vnew[d] = vrow[d];
+  }
+  __syncthreads();
+  if (pos >= j0 && pos < j1) {  // this CTA owns the new token: append it to the cache
+    for (int d = tid; d < kHd; d += kThreads) {
+      kc[static_cast<int64_t>(pos) * kHd + d] = knew[d];
+      vc[static_cast<int64_t>(pos) * kHd + d] = vnew[d];
+    }
+  }
+
+  // scores: each warp takes positions j0+warp, j0+warp+4, ...; lanes split the head dim (4 each)
+  const int n = j1 - j0;
+  for (int jj = warp; jj < n; jj += kThreads / 32) {
+    const int j = j0 + jj;
+    float kv[4];
+    if (j == pos) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) kv[e] = __half2float(knew[lane * 4 + e]);
+    } else {
+      const uint2 raw = __ldcg(reinterpret_cast<const uint2*>(kc + static_cast<int64_t>(j) * kHd) + lane);
+      const __half* kh = reinterpret_cast<const __half*>(&raw);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) kv[e] = __half2float(kh[e]);
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float s = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s = fmaf(qs[g][lane * 4 + e], kv[e], s);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      if (lane == 0) scores[g * slice + jj] = s;
+    }
+  }
+  __syncthreads();
+  // softmax partials per head (warp g handles head g, g+4, ...)
+  for (int g = warp; g < G; g += kThreads / 32) {
+    float m = -FLT_MAX;
+    for (int jj = lane; jj < n; jj += 32) m = fmaxf(m, scores[g * slice + jj]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float l = 0.f;
+    for (int jj = lane; jj < n; jj += 32) {
+      const float e = __expf(scores[g * slice + jj] - m);
+      scores[g * slice + jj] = e;
+      l += e;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    if (lane == 0) {
+      part_m[g] = m;
+      part_l[g] = l;
+    }
+  }
+  __syncthreads();
+  // unnormalized output: thread d accumulates sum_j p[g][j] * v[j][d] for all heads of the group
+  for (int d = tid; d < kHd; d += kThreads) {
+    float acc[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) acc[g] = 0.f;
+    for (int jj = 0; jj < n; ++jj) {
+      const int j = j0 + jj;
+      const float v = (j == pos) ? __half2float(vnew[d]) : __half2float(__ldcg(vc + static_cast<int64_t>(j) * kHd + d));
+#pragma unroll
+      for (int g = 0; g < G; ++g) acc[g] = fmaf(scores[g * slice + jj], v, acc[g]);
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) part_o[g][d] = acc[g];
+  }
+
+  if (S == 1) {
+    __syncthreads();
+    for (int e = tid; e < G * kHd; e += kThreads) {
+      const int g = e / kHd, d = e % kHd;
+      p.out[static_cast<int64_t>(b) * p.nq * kHd + (h * G + g) * kHd + d] = __float2half_rn(part_o[g][d] / part_l[g]);
+    }
+    return;
+  }
+  // combine the S partials of the cluster: rank r writes dims d with d % S == r
+  cluster_sync();
+  for (int e = tid; e < G * kHd; e += kThreads) {
+    const int g = e / kHd, d = e % kHd;
+    if (d % S != rank) continue;
+    float M = -FLT_MAX;
+    for (int q = 0; q < S; ++q) {
+      const float l = ld_shared_cluster_f32(map_shared_rank(&part_l[g], q));
+      if (l > 0.f) M = fmaxf(M, ld_shared_cluster_f32(map_shared_rank(&part_m[g], q)));
+    }
+    float num = 0.f, den = 0.f;
+    for (int q = 0; q < S; ++q) {
+      const float l = ld_shared_cluster_f32(map_shared_rank(&part_l[g], q));
+      if (l <= 0.f) continue;
+      const float w = __expf(ld_shared_cluster_f32(map_shared_rank(&part_m[g], q)) - M);
+      num = fmaf(w, ld_shared_cluster_f32(map_shared_rank(&part_o[g][d], q)), num);
+      den = fmaf(w, l, den);
+    }
+    p.out[static_cast<int64_t>(b) * p.nq * kHd + (h * G + g) * kHd + d] = __float2half_rn(num / den);
+  }
+  cluster_sync();  // keep partials alive until every rank has read them
+}
+
+}  // namespace
+}  // namespace dk
+
+using namespace dk;
+
+extern "C" int dk_decode_attention(const void* qkv, void* k_cache, void* v_cache, const int64_t* pos,
+                                   const void* cos, const void* sin, void* out, int64_t B, int64_t nq,
+                                   int64_t nkv, int64_t head_dim, int64_t max_len, int32_t splits,
+                                   dk_stream_t stream) {
+  if (B <= 0 || nq <= 0 || nkv <= 0 || max_len <= 0) return set_error(DK_ERR_INVALID, "decode_attention: bad sizes");
+  if (head_dim != kHd) return set_error(DK_ERR_UNSUPPORTED, "decode_attention: head_dim %lld (only 128)", (long long)head_dim);
+  if (nq % nkv != 0 || nq / nkv > kMaxGroup)
+    return set_error(DK_ERR_UNSUPPORTED, "decode_attention: %lld query heads per kv head (max %d)",
+                     (long long)(nq / nkv), kMaxGroup);
+  if (B > 65535 || nkv > 65535) return set_error(DK_ERR_INVALID, "decode_attention: grid too large");
+  if (!qkv || !k_cache || !v_cache || !pos || !cos || !sin || !out)
+    return set_error(DK_ERR_INVALID, "decode_attention: NULL pointer");
+  int S = splits > 0 ? splits : static_cast<int>(std::min<int64_t>(kMaxSplit, (max_len + 255) / 256));
+  S = std::max(1, std::min(S, kMaxSplit));
+  AttnParams p;
+  p.qkv = static_cast<const __half*>(qkv);
+  p.k_cache = static_cast<__half*>(k_cache);
+  p.v_cache = static_cast<__half*>(v_cache);
+  p.pos = pos;
+  p.cos = static_cast<const __half*>(cos);
+  p.sin = static_cast<const __half*>(sin);
+  p.out = static_cast<__half*>(out);
+  p.nq = static_cast<int>(nq);
+  p.nkv = static_cast<int>(nkv);
+  p.max_len = static_cast<int>(max_len);
+  p.scale = 1.0f / sqrtf(static_cast<float>(head_dim));
+  p.err = device_info().err_word;
+  const int G = static_cast<int>(nq / nkv);
+  const int slice_max = static_cast<int>((max_len + S - 1) / S);
+  const size_t smem = static_cast<size_t>(G) * slice_max * sizeof(float);
+  const dim3 grid(static_cast<unsigned>(nkv), static_cast<unsigned>(B), static_cast<unsigned>(S));
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e;
+#define DK_ATTN(GG)                                                                                      \
+  case GG: {                                                                                             \
+    auto k = decode_attention_kernel<GG>;                                                                \
+    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    e = launch(k, grid, dim3(kThreads), smem, st, pdl_enabled(), dim3(1, 1, S), p);                       \
+    break;                                                                                               \
+  }
+  switch (G) {
+    DK_ATTN(1)
+    DK_ATTN(2)
+    DK_ATTN(4)
+    DK_ATTN(6)
+    DK_ATTN(7)
+    DK_ATTN(8)
+    default:
+      return set_error(DK_ERR_UNSUPPORTED, "decode_attention: group size %d", G);
+  }
+#undef DK_ATTN
+  if (e != cudaSuccess) return set_error(DK_ERR_CUDA, "decode_attention launch: %s", cudaGetErrorString(e));
+  return DK_OK;
+}

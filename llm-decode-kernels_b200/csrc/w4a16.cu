@@ -64,6 +64,7 @@ struct GemvParams {
   int nbuf;          // ring depth
   int xs_pitch;      // bytes per staged x row
   int static_weights;
+  int swiglu_i;      // > 0: fused SwiGLU over gate columns [0, I) and up columns [I, 2I); y is [M, I]
   int* err;
 };
 
@@ -84,6 +85,19 @@ __host__ __device__ inline SmemLayout smem_layout(int cw, int nbuf, int M, int x
   L.bar_off = L.red_off + ((wpc > 1 || split > 1) ? wpc * M * cw * 32 * 4 : 0);
   L.total = L.bar_off + 2 * nbuf * 8;
   return L;
+}
+
+// Fused SwiGLU epilogue with the reference's rounding: the gate_up matmul output is rounded to
+// fp16 (kernels/w4a16.py:95), silu runs in fp32 on the fp16 gate and is rounded to fp16, and the
+// product with the fp16 up value is an fp16 multiply (kernels/swiglu.py:26-28).
+__device__ __forceinline__ __half swiglu_out(float g, float u, const __half* bias, int n, int I) {
+  if (bias != nullptr) {
+    g += __half2float(bias[n]);
+    u += __half2float(bias[I + n]);
+  }
+  const float gf = __half2float(__float2half_rn(g));
+  const __half act = __float2half_rn(__fdiv_rn(gf, __fadd_rn(1.0f, expf(-gf))));
+  return __hmul_rn(act, __float2half_rn(u));
 }
 
 // One chunk-stage (32 columns x 32 packed rows) for one warp. EXACT: dequantize to fp16 exactly
@@ -201,13 +215,18 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 3 - NT)  // M <= 8: two CTA
   const int s_begin = rank * p.split_stages;
   const int s_end = min(s_begin + p.split_stages, p.stages_total);
   const int nst = max(0, s_end - s_begin);
-  int c_begin, c_end;  // this CTA's chunk range
+  // Work units: 32-column chunks, or (fused SwiGLU) pairs of a gate chunk and its up chunk. A tile
+  // holds UPT units in CW box slots; with SwiGLU slot s is the gate (s < UPT) or up (s >= UPT)
+  // chunk of unit tile + s % UPT.
+  const bool swiglu = p.swiglu_i > 0;
+  const int UPT = swiglu ? CW / 2 : CW;
+  int c_begin, c_end;  // this CTA's unit range
   if (S == 1) {
     c_begin = static_cast<int>((static_cast<int64_t>(blockIdx.x) * p.chunks) / gridDim.x);
     c_end = static_cast<int>((static_cast<int64_t>(blockIdx.x + 1) * p.chunks) / gridDim.x);
   } else {
-    c_begin = blockIdx.x * CW;
-    c_end = min(c_begin + CW, p.chunks);
+    c_begin = blockIdx.x * UPT;
+    c_end = min(c_begin + UPT, p.chunks);
   }
 
   if (threadIdx.x == 0) {
@@ -229,17 +248,18 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 3 - NT)  // M <= 8: two CTA
       prefetch_tensormap(&ms);
       prefetch_tensormap(&mz);
       int it = 0;
-      for (int tile = c_begin; tile < c_end && ok; tile += CW) {
-        const int nch = min(CW, c_end - tile);
+      for (int tile = c_begin; tile < c_end && ok; tile += UPT) {
+        const int nch = min(UPT, c_end - tile);
         for (int s = s_begin; s < s_end; ++s, ++it) {
           const int buf = it % p.nbuf;
           if (it >= p.nbuf && !mbar_wait(&empty[buf], ((it / p.nbuf) - 1) & 1, p.err, DK_DEVERR_WAIT_EMPTY)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[buf], nch * kChunkStageBytes);
-          for (int c = 0; c < nch; ++c) {
-            const int col = (tile + c) * 32;
+          mbar_arrive_expect_tx(&full[buf], (swiglu ? 2 : 1) * nch * kChunkStageBytes);
+          for (int c = 0; c < CW; ++c) {
+            if (c % UPT >= nch) continue;
+            const int col = (tile + c % UPT) * 32 + (c >= UPT ? p.swiglu_i : 0);
             tma_load_2d(smem + L.w_off + (buf * CW + c) * kBoxBytes, &mq, col, s * kStageRows, &full[buf]);
             uint8_t* sz = smem + L.sz_off + (buf * CW + c) * 2 * kSZBytes;
             tma_load_2d(sz, &ms, col, s * kGroupsPerStage, &full[buf]);
@@ -276,9 +296,9 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 3 - NT)  // M <= 8: two CTA
     const int phase = warp / CW;  // which of the tile's stages (round-robin over WPC warps)
     float* red = reinterpret_cast<float*>(smem + L.red_off);
     int tile_idx = 0;
-    for (int tile = c_begin; tile < c_end; tile += CW, ++tile_idx) {
-      const int nch = min(CW, c_end - tile);
-      const bool active = slot < nch;
+    for (int tile = c_begin; tile < c_end; tile += UPT, ++tile_idx) {
+      const int nch = min(UPT, c_end - tile);
+      const bool active = slot % UPT < nch;
       float acc[2][NT][4];
 #pragma unroll
       for (int a = 0; a < 2; ++a)
@@ -303,7 +323,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 3 - NT)  // M <= 8: two CTA
       }
 
       // ---------------------------------------------------------------- tile epilogue
-      if (WPC == 1 && S == 1) {
+      if (WPC == 1 && S == 1 && !swiglu) {
         if (active && ok) {
           const int n0 = (tile + slot) * 32 + 4 * g;
 #pragma unroll
@@ -339,19 +359,29 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 3 - NT)  // M <= 8: two CTA
         }
         asm volatile("bar.sync 1, %0;" ::"r"(kWarps * 32) : "memory");
         const int ncols = nch * 32;
+        const int nhalves = swiglu ? 2 : 1;
         for (int e = threadIdx.x; e < p.M * ncols; e += kWarps * 32) {
           const int m = e / ncols, col = e % ncols;
-          float v = red[m * CW * 32 + col];
+          float v[2];
+          for (int hh = 0; hh < nhalves; ++hh) {
+            const int rc = hh * UPT * 32 + col;  // column of slot (gate or up) in red
+            float a = red[m * CW * 32 + rc];
 #pragma unroll
-          for (int j = 1; j < WPC; ++j) v += red[(j * p.M + m) * CW * 32 + col];
+            for (int j = 1; j < WPC; ++j) a += red[(j * p.M + m) * CW * 32 + rc];
+            v[hh] = a;
+          }
           if (S == 1) {
             const int n = tile * 32 + col;
-            if (n < p.N) {
-              if (p.bias != nullptr) v += __half2float(p.bias[n]);
-              p.y[m * p.ldy + n] = __float2half_rn(v);
+            if (!swiglu && n < p.N) {
+              float a = v[0];
+              if (p.bias != nullptr) a += __half2float(p.bias[n]);
+              p.y[m * p.ldy + n] = __float2half_rn(a);
+            } else if (swiglu && n < p.swiglu_i) {
+              p.y[m * p.ldy + n] = swiglu_out(v[0], v[1], p.bias, n, p.swiglu_i);
             }
           } else {
-            red[m * CW * 32 + col] = v;  // this rank's partial, read by the cluster below
+            for (int hh = 0; hh < nhalves; ++hh)  // this rank's partial, read by the cluster below
+              red[m * CW * 32 + hh * UPT * 32 + col] = v[hh];
           }
         }
         asm volatile("bar.sync 1, %0;" ::"r"(kWarps * 32) : "memory");
@@ -378,17 +408,23 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 3 - NT)  // M <= 8: two CTA
   if (S > 1) {
     cluster_sync();
     const float* red = reinterpret_cast<const float*>(smem + L.red_off);
-    const int ncols = min(CW, c_end - c_begin) * 32;
+    const int ncols = min(UPT, c_end - c_begin) * 32;
     for (int e = threadIdx.x; e < p.M * ncols; e += blockDim.x) {
       if (e % S != rank) continue;
       const int m = e / ncols, col = e % ncols;
       const int n = c_begin * 32 + col;
-      if (n >= p.N) continue;
-      const float* src = red + m * CW * 32 + col;
-      float v = 0.f;
-      for (int q = 0; q < S; ++q) v += ld_shared_cluster_f32(map_shared_rank(src, q));
-      if (p.bias != nullptr) v += __half2float(p.bias[n]);
-      p.y[m * p.ldy + n] = __float2half_rn(v);
+      if (n >= (swiglu ? p.swiglu_i : p.N)) continue;
+      float v[2] = {0.f, 0.f};
+      for (int hh = 0; hh < (swiglu ? 2 : 1); ++hh) {
+        const float* src = red + m * CW * 32 + hh * UPT * 32 + col;
+        for (int q = 0; q < S; ++q) v[hh] += ld_shared_cluster_f32(map_shared_rank(src, q));
+      }
+      if (swiglu) {
+        p.y[m * p.ldy + n] = swiglu_out(v[0], v[1], p.bias, n, p.swiglu_i);
+      } else {
+        if (p.bias != nullptr) v[0] += __half2float(p.bias[n]);
+        p.y[m * p.ldy + n] = __float2half_rn(v[0]);
+      }
     }
     cluster_sync();  // keep this CTA's partial sums alive until every rank has read them
   }
@@ -495,13 +531,14 @@ int xs_pitch_for(int split_stages) { return split_stages * kStageRows * 16 + kXs
 
 // Cost model (microseconds) for one launch: a fixed launch/fill latency, then the slowest of the
 // busiest SM's HBM share, its instruction throughput, and one warp's serial chain of
-// chunk-stages; plus the cluster and in-CTA reductions.
-double model_cost(const DeviceInfo& dev, int chunks, int sps, int cw, int split, int nctas) {
+// chunk-stages; plus the cluster and in-CTA reductions. `units` are 32-column chunks (or
+// gate/up chunk pairs, bpu = 2 boxes per unit), `upt` units per tile.
+double model_cost(const DeviceInfo& dev, int units, int bpu, int sps, int cw, int upt, int split, int nctas) {
   const int wpc = kWarps / cw;
-  const double chunks_per_cta = std::ceil(static_cast<double>(chunks) / nctas);
-  const double tiles_per_cta = std::ceil(chunks_per_cta / cw);
+  const double units_per_cta = std::ceil(static_cast<double>(units) / nctas);
+  const double tiles_per_cta = std::ceil(units_per_cta / upt);
   const double ctas_per_sm = std::ceil(static_cast<double>(nctas) * split / dev.num_sms);
-  const double cs_sm = ctas_per_sm * chunks_per_cta * sps;
+  const double cs_sm = ctas_per_sm * units_per_cta * bpu * sps;
   const double t_mem = cs_sm * kChunkStageBytes / (6.4e12 / dev.num_sms) * 1e6;
   const double t_issue = cs_sm / 10.0;
   const double t_chain = tiles_per_cta * std::ceil(static_cast<double>(sps) / wpc) * 0.5;
@@ -509,10 +546,9 @@ double model_cost(const DeviceInfo& dev, int chunks, int sps, int cw, int split,
          (wpc > 1 ? 0.2 * tiles_per_cta : 0.0);
 }
 
-Choice choose_uncached(int M, int N, int K, const dk_matmul_config* cfg) {
+Choice choose_uncached(int M, int units, int K, bool swiglu, const dk_matmul_config* cfg) {
   const DeviceInfo& dev = device_info();
   const int stages_total = (K + 256 - 1) / 256;
-  const int chunks = (N + 31) / 32;
   const int nt = M <= 8 ? 1 : 2;
   Choice best = {0, 0, 0, 0, 0, 1e300};
   // requested split: clamped to what K allows (every rank needs at least one 256-wide stage)
@@ -523,6 +559,8 @@ Choice choose_uncached(int M, int N, int K, const dk_matmul_config* cfg) {
                                cfg->block_n == 256)) ? cfg->block_n : 0;
   for (int cw = 8; cw >= 1; cw /= 2) {
     if (want_bn && want_bn != 32 * cw) continue;
+    if (swiglu && cw < 2) continue;
+    const int upt = swiglu ? cw / 2 : cw;
     for (int split = 1; split <= 8; ++split) {
       if (want_split && want_split != split) continue;
       if (split > stages_total) break;
@@ -530,7 +568,7 @@ Choice choose_uncached(int M, int N, int K, const dk_matmul_config* cfg) {
       if ((split - 1) * sps >= stages_total) continue;  // every rank gets at least one stage
       const int pitch = xs_pitch_for(sps);
       if (static_cast<size_t>(M) * pitch > kXsBudget) continue;
-      const int tiles = (chunks + cw - 1) / cw;
+      const int tiles = (units + upt - 1) / upt;
       const int stages_per_cta = sps * (split > 1 ? 1 : (tiles + dev.num_sms - 1) / dev.num_sms);
       int nbuf = std::min(std::max(stages_per_cta, 2), 16);
       SmemLayout L = smem_layout(cw, nbuf, M, pitch, split);
@@ -541,34 +579,34 @@ Choice choose_uncached(int M, int N, int K, const dk_matmul_config* cfg) {
       const size_t smem = static_cast<size_t>(L.total) + 1024;
       if (smem > static_cast<size_t>(dev.max_smem_optin)) continue;
       const int occ = occupancy(nt, cw, smem);
-      const int nctas = split == 1 ? std::min(chunks, dev.num_sms * occ) : tiles;
+      const int nctas = split == 1 ? std::min(units, dev.num_sms * occ) : tiles;
       if (split > 1 && static_cast<long>(nctas) * split > static_cast<long>(dev.num_sms) * occ) continue;
-      const double cost = model_cost(dev, chunks, sps, cw, split, nctas);
+      const double cost = model_cost(dev, units, swiglu ? 2 : 1, sps, cw, upt, split, nctas);
       if (cost < best.cost) best = {cw, split, nbuf, nctas, smem, cost};
     }
   }
   return best;
 }
 
-// Memoized per (device, M, N, K, requested split, requested tile): the choice is a pure function
-// of these, and computing it queries the occupancy calculator.
-Choice choose(int M, int N, int K, const dk_matmul_config* cfg) {
+// Memoized per (device, M, units, K, mode, requested split, requested tile): the choice is a pure
+// function of these, and computing it queries the occupancy calculator.
+Choice choose(int M, int units, int K, bool swiglu, const dk_matmul_config* cfg) {
   static std::mutex mu;
-  static std::map<std::tuple<int, int, int, int, int, int>, Choice> cache;
+  static std::map<std::tuple<int, int, int, int, int, int, int>, Choice> cache;
   int dev = 0;
   cudaGetDevice(&dev);
-  const auto key = std::make_tuple(dev, M, N, K, cfg ? cfg->split_k : 0, cfg ? cfg->block_n : 0);
+  const auto key = std::make_tuple(dev, M, units, K, swiglu ? 1 : 0, cfg ? cfg->split_k : 0, cfg ? cfg->block_n : 0);
   {
     std::lock_guard<std::mutex> lock(mu);
     auto it = cache.find(key);
     if (it != cache.end()) return it->second;
   }
-  Choice c = choose_uncached(M, N, K, cfg);
+  Choice c = choose_uncached(M, units, K, swiglu, cfg);
   if (c.cw == 0 && cfg) {  // the requested split / tile does not fit: let the model choose
     dk_matmul_config auto_cfg = *cfg;
     auto_cfg.split_k = 0;
     auto_cfg.block_n = 0;
-    c = choose_uncached(M, N, K, &auto_cfg);
+    c = choose_uncached(M, units, K, swiglu, &auto_cfg);
   }
   std::lock_guard<std::mutex> lock(mu);
   cache[key] = c;
@@ -586,38 +624,11 @@ int launch_gemv(const CUtensorMap& mq, const CUtensorMap& ms, const CUtensorMap&
   return DK_OK;
 }
 
-}  // namespace
-}  // namespace dk
-
-extern "C" int dk_w4a16_matmul(const void* x, int64_t ldx, const int32_t* qweight, const void* scales,
-                               const void* zeros, const void* bias, void* y, int64_t ldy, int64_t M,
-                               int64_t N, int64_t K, int64_t group_size, const dk_matmul_config* cfg,
-                               dk_stream_t stream) {
-  using namespace dk;
-  if (M < 0 || N < 0 || K < 0) return set_error(DK_ERR_INVALID, "w4a16_matmul: negative size");
-  if (group_size <= 0 || group_size % 8 != 0 || K % group_size != 0)
-    return set_error(DK_ERR_INVALID,
-                     "w4a16_matmul: need K %% group_size == 0 and group_size %% 8 == 0 (K=%lld, group_size=%lld)",
-                     (long long)K, (long long)group_size);
-  if (ldx < K || ldy < N) return set_error(DK_ERR_INVALID, "w4a16_matmul: row stride smaller than the row");
-  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX || (K / 8) * N > (int64_t(1) << 40))
-    return set_error(DK_ERR_INVALID, "w4a16_matmul: size out of range");
-  if (M == 0 || N == 0) return DK_OK;
-  if (!x || !qweight || !scales || !zeros || !y) return set_error(DK_ERR_INVALID, "w4a16_matmul: NULL pointer");
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+// Shared host path of dk_w4a16_matmul (swiglu_i == 0) and dk_w4a16_swiglu (swiglu_i == I, N == 2I).
+int run_fast(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const void* zeros,
+             const void* bias, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group_size,
+             const dk_matmul_config* cfg, int swiglu_i, cudaStream_t st) {
   const int flags = cfg ? cfg->flags : 0;
-  const bool fast = !(flags & DK_FLAG_GENERIC) && N % 8 == 0 && group_size == 128 && K > 0 && aligned16(x) &&
-                    ldx % 8 == 0 && aligned16(qweight) && aligned16(scales) && aligned16(zeros);
-  if (!fast) {
-    const dim3 grid(static_cast<unsigned>((N + 127) / 128), static_cast<unsigned>(M), 1);
-    cudaError_t e = launch(w4a16_generic_kernel, grid, dim3(128, 1, 1), 0, st, pdl_enabled(), dim3(1, 1, 1),
-                           static_cast<const __half*>(x), ldx, qweight, static_cast<const __half*>(scales),
-                           static_cast<const __half*>(zeros), static_cast<const __half*>(bias),
-                           static_cast<__half*>(y), ldy, static_cast<int>(M), static_cast<int>(N),
-                           static_cast<int>(K), static_cast<int>(group_size));
-    if (e != cudaSuccess) return set_error(DK_ERR_CUDA, "w4a16 generic launch: %s", cudaGetErrorString(e));
-    return DK_OK;
-  }
   CUtensorMap mq, ms, mz;
   if (!make_tensor_map_2d(&mq, qweight, CU_TENSOR_MAP_DATA_TYPE_INT32, N, K / 8, N * 4, 32, kStageRows,
                           CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -627,10 +638,11 @@ extern "C" int dk_w4a16_matmul(const void* x, int64_t ldx, const int32_t* qweigh
                           kGroupsPerStage, CU_TENSOR_MAP_SWIZZLE_NONE))
     return DK_ERR_CUDA;
   const DeviceInfo& dev = device_info();
+  const int units = swiglu_i > 0 ? (swiglu_i + 31) / 32 : static_cast<int>((N + 31) / 32);
   for (int64_t m0 = 0; m0 < M; m0 += 16) {
     const int mc = static_cast<int>(std::min<int64_t>(16, M - m0));
-    const Choice c = choose(mc, static_cast<int>(N), static_cast<int>(K), cfg);
-    if (c.cw == 0) return set_error(DK_ERR_UNSUPPORTED, "w4a16_matmul: no tile fits (M=%d, K=%lld)", mc, (long long)K);
+    const Choice c = choose(mc, units, static_cast<int>(K), swiglu_i > 0, cfg);
+    if (c.cw == 0) return set_error(DK_ERR_UNSUPPORTED, "w4a16: no tile fits (M=%d, K=%lld)", mc, (long long)K);
     GemvParams p;
     p.x = static_cast<const __half*>(x) + m0 * ldx;
     p.ldx = ldx;
@@ -642,13 +654,77 @@ extern "C" int dk_w4a16_matmul(const void* x, int64_t ldx, const int32_t* qweigh
     p.K = static_cast<int>(K);
     p.stages_total = static_cast<int>((K + 255) / 256);
     p.split_stages = (p.stages_total + c.split - 1) / c.split;
-    p.chunks = static_cast<int>((N + 31) / 32);
+    p.chunks = units;
     p.nbuf = c.nbuf;
     p.xs_pitch = xs_pitch_for(p.split_stages);
     p.static_weights = (flags & DK_FLAG_STATIC_WEIGHTS) ? 1 : 0;
+    p.swiglu_i = swiglu_i;
     p.err = dev.err_word;
     const int rc = launch_gemv(mq, ms, mz, p, c, (flags & DK_FLAG_EXACT_DEQUANT) != 0, st);
     if (rc != DK_OK) return rc;
   }
   return DK_OK;
+}
+
+int check_w4a16_args(const char* what, const void* x, int64_t ldx, const int32_t* qweight, const void* scales,
+                     const void* zeros, const void* y, int64_t ldy, int64_t M, int64_t N, int64_t ycols,
+                     int64_t K, int64_t group_size) {
+  if (M < 0 || N < 0 || K < 0) return set_error(DK_ERR_INVALID, "%s: negative size", what);
+  if (group_size <= 0 || group_size % 8 != 0 || K % group_size != 0)
+    return set_error(DK_ERR_INVALID, "%s: need K %% group_size == 0 and group_size %% 8 == 0 (K=%lld, group_size=%lld)",
+                     what, (long long)K, (long long)group_size);
+  if (ldx < K || ldy < ycols) return set_error(DK_ERR_INVALID, "%s: row stride smaller than the row", what);
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX || (K / 8) * N > (int64_t(1) << 40))
+    return set_error(DK_ERR_INVALID, "%s: size out of range", what);
+  if (M > 0 && N > 0 && (!x || !qweight || !scales || !zeros || !y))
+    return set_error(DK_ERR_INVALID, "%s: NULL pointer", what);
+  return DK_OK;
+}
+
+bool fast_ok(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const void* zeros, int64_t N,
+             int64_t K, int64_t group_size, int flags) {
+  return !(flags & DK_FLAG_GENERIC) && N % 8 == 0 && group_size == 128 && K > 0 && aligned16(x) && ldx % 8 == 0 &&
+         aligned16(qweight) && aligned16(scales) && aligned16(zeros);
+}
+
+}  // namespace
+}  // namespace dk
+
+extern "C" int dk_w4a16_matmul(const void* x, int64_t ldx, const int32_t* qweight, const void* scales,
+                               const void* zeros, const void* bias, void* y, int64_t ldy, int64_t M,
+                               int64_t N, int64_t K, int64_t group_size, const dk_matmul_config* cfg,
+                               dk_stream_t stream) {
+  using namespace dk;
+  int rc = check_w4a16_args("w4a16_matmul", x, ldx, qweight, scales, zeros, y, ldy, M, N, N, K, group_size);
+  if (rc != DK_OK) return rc;
+  if (M == 0 || N == 0) return DK_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int flags = cfg ? cfg->flags : 0;
+  if (!fast_ok(x, ldx, qweight, scales, zeros, N, K, group_size, flags)) {
+    const dim3 grid(static_cast<unsigned>((N + 127) / 128), static_cast<unsigned>(M), 1);
+    cudaError_t e = launch(w4a16_generic_kernel, grid, dim3(128, 1, 1), 0, st, pdl_enabled(), dim3(1, 1, 1),
+                           static_cast<const __half*>(x), ldx, qweight, static_cast<const __half*>(scales),
+                           static_cast<const __half*>(zeros), static_cast<const __half*>(bias),
+                           static_cast<__half*>(y), ldy, static_cast<int>(M), static_cast<int>(N),
+                           static_cast<int>(K), static_cast<int>(group_size));
+    if (e != cudaSuccess) return set_error(DK_ERR_CUDA, "w4a16 generic launch: %s", cudaGetErrorString(e));
+    return DK_OK;
+  }
+  return run_fast(x, ldx, qweight, scales, zeros, bias, y, ldy, M, N, K, group_size, cfg, 0, st);
+}
+
+extern "C" int dk_w4a16_swiglu(const void* x, int64_t ldx, const int32_t* qweight, const void* scales,
+                               const void* zeros, const void* bias, void* y, int64_t ldy, int64_t M,
+                               int64_t I, int64_t K, int64_t group_size, const dk_matmul_config* cfg,
+                               dk_stream_t stream) {
+  using namespace dk;
+  int rc = check_w4a16_args("w4a16_swiglu", x, ldx, qweight, scales, zeros, y, ldy, M, 2 * I, I, K, group_size);
+  if (rc != DK_OK) return rc;
+  if (M == 0 || I == 0) return DK_OK;
+  const int flags = cfg ? cfg->flags : 0;
+  if (I % 32 != 0 || !fast_ok(x, ldx, qweight, scales, zeros, 2 * I, K, group_size, flags))
+    return set_error(DK_ERR_UNSUPPORTED,
+                     "w4a16_swiglu: the fused kernel needs I %% 32 == 0, group_size 128 and 16-byte aligned operands");
+  return run_fast(x, ldx, qweight, scales, zeros, bias, y, ldy, M, 2 * I, K, group_size, cfg, static_cast<int>(I),
+                  reinterpret_cast<cudaStream_t>(stream));
 }

@@ -1,0 +1,28 @@
+"""Decode attention for one new token per sequence (the T == 1 case of the reference runner's
+RoPE + KV-cache append + SDPA, kernels/e2e/model.py:236-244): one libdecodek kernel that reads only
+the cached positions 0..pos instead of the whole max_len cache."""
+
+from __future__ import annotations
+
+import torch
+
+from kernels import _lib
+
+
+def decode_attention(qkv, k_cache, v_cache, pos, cos, sin, n_heads, n_kv, splits=0):
+    """qkv [B, 1, (nq + 2 nkv) * hd] fp16; k_cache, v_cache [B, nkv, max_len, hd] fp16 (updated
+    in place at `pos`); pos int64 [1] (device); cos, sin [1, hd] fp16. Returns [B, 1, nq * hd]."""
+    B, T, width = qkv.shape
+    hd = k_cache.shape[-1]
+    max_len = k_cache.shape[-2]
+    assert T == 1 and width == (n_heads + 2 * n_kv) * hd
+    _lib.require_cuda("decode_attention", qkv, k_cache, v_cache, pos, cos, sin)
+    _lib.require_dtype("decode_attention", torch.float16, qkv, k_cache, v_cache, cos, sin)
+    _lib.require_dtype("decode_attention", torch.int64, pos)
+    assert k_cache.is_contiguous() and v_cache.is_contiguous()
+    qkv = qkv.contiguous()
+    out = torch.empty((B, 1, n_heads * hd), dtype=qkv.dtype, device=qkv.device)
+    _lib.call("dk_decode_attention", _lib.ptr(qkv), _lib.ptr(k_cache), _lib.ptr(v_cache), _lib.ptr(pos),
+              _lib.ptr(cos.contiguous()), _lib.ptr(sin.contiguous()), _lib.ptr(out), B, n_heads, n_kv, hd,
+              max_len, splits, _lib.stream_of(qkv))
+    return out

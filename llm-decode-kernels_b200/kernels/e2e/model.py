@@ -1,0 +1,311 @@
+"""A Qwen2 decode runner on a Hugging Face model object, with swappable kernel backends.
+
+Same structure and API as the reference's kernels/e2e/model.py: a static KV cache, RoPE, and the
+fused qkv and gate/up projections, with the linear / norm / activation ops supplied by a backend.
+The fp16 and w4_ref backends keep the reference's plain PyTorch numerics (the fp16 cuBLAS
+baseline and the quality reference). The `ours*` backends run libdecodek's sm_100a kernels:
+W4A16 (or FP8) linears with weight prefetch across kernels, fused residual+RMSNorm, SwiGLU fused
+into the gate_up kernel's epilogue, and a decode-attention kernel that reads only the cached
+positions (the reference's SDPA reads the whole `max_len` cache every step).
+
+Kept in fp16 on every backend: embeddings, RoPE tables, the KV cache. lm_head (tied to the
+embeddings) stays fp16 unless the backend name ends in `_lm`, which also quantizes a copy of it.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from kernels import config
+
+# ------------------------------------------------------------------------------------- ops
+
+
+@dataclass
+class Linear:
+    """One projection. fp16 holds `w`; quantized backends hold the packed tensors
+    (reference kernels/e2e/model.py:25-33)."""
+
+    w: torch.Tensor | None = None
+    qweight: torch.Tensor | None = None
+    scales: torch.Tensor | None = None
+    zeros: torch.Tensor | None = None
+    bias: torch.Tensor | None = None
+
+
+class Backend:
+    """fp16 eager PyTorch ops with Hugging Face Qwen2 numerics (reference model.py:36-52)."""
+
+    name = "fp16"
+    quantized = False
+    fused_decode = False  # True: the runner uses attention_decode / gate_up_act hooks
+
+    def linear(self, x, p: Linear):
+        return F.linear(x, p.w, p.bias)
+
+    def norm(self, x, w, eps, residual=None):
+        from kernels.reference import rmsnorm_ref
+
+        return rmsnorm_ref(x, w, eps, residual)
+
+    def act(self, gate_up):
+        i = gate_up.shape[-1] // 2
+        return F.silu(gate_up[..., :i]) * gate_up[..., i:]
+
+    def gate_up_act(self, x, p: Linear):
+        return self.act(self.linear(x, p))
+
+
+class W4RefBackend(Backend):
+    """RTN 4-bit weights dequantized once to fp16, then cuBLAS (reference model.py:55-67): the
+    same quality as the kernels, so quality changes come from quantization, not the kernels."""
+
+    name = "w4_ref"
+    quantized = True
+
+    def linear(self, x, p: Linear):
+        from kernels.reference import dequantize_ref
+
+        if p.w is None:  # dequantize once, cache
+            p.w = dequantize_ref(p.qweight, p.scales, p.zeros, config.GROUP_SIZE)
+        return F.linear(x, p.w, p.bias)
+
+
+class OursBackend(Backend):
+    """libdecodek kernels: W4A16 linears, fused residual+RMSNorm, SwiGLU (reference model.py:70-97).
+
+    `decode_kernel` keeps the reference's names ("triton" -> `ours`, "cuda" -> `ours_cuda`); both
+    run the same sm_100a kernels here (`ours_cuda` goes through w4a16_decode_cuda for <= 16 rows,
+    like the reference)."""
+
+    quantized = True
+    fused_decode = True
+    # weights of a runner never change: let each kernel prefetch them before the previous ends
+    LINEAR_CFG = {"STATIC_WEIGHTS": True}
+
+    def __init__(self, decode_kernel: str = "triton"):
+        self.decode_kernel = decode_kernel
+        self.name = "ours" if decode_kernel == "triton" else f"ours_{decode_kernel}"
+
+    def linear(self, x, p: Linear):
+        from kernels.w4a16 import w4a16_matmul
+
+        rows = x.numel() // x.shape[-1]
+        if self.decode_kernel == "cuda" and rows <= 16:
+            from kernels.cuda.w4a16_cuda import w4a16_decode_cuda
+
+            return w4a16_decode_cuda(x, p.qweight, p.scales, p.zeros, bias=p.bias)
+        return w4a16_matmul(x, p.qweight, p.scales, p.zeros, bias=p.bias, config=self.LINEAR_CFG)
+
+    def norm(self, x, w, eps, residual=None):
+        from kernels.rmsnorm import rmsnorm
+
+        return rmsnorm(x, w, eps, residual)
+
+    def act(self, gate_up):
+        from kernels.swiglu import swiglu_fused
+
+        return swiglu_fused(gate_up)
+
+    def gate_up_act(self, x, p: Linear):
+        from kernels.w4a16 import w4a16_swiglu
+
+        return w4a16_swiglu(x, p.qweight, p.scales, p.zeros, bias=p.bias, config=self.LINEAR_CFG)
+
+
+class OursFP8Backend(OursBackend):
+    """FP8 (e4m3) weight-only linears with the same fused norm/activation kernels
+    (reference model.py:100-118)."""
+
+    name = "ours_fp8"
+
+    def __init__(self):
+        super().__init__("triton")
+        self.name = "ours_fp8"
+
+    def quantize(self, w, b) -> Linear:
+        from kernels.fp8 import quantize_fp8
+
+        wq, s = quantize_fp8(w)
+        return Linear(qweight=wq, scales=s, bias=b)
+
+    def linear(self, x, p: Linear):
+        from kernels.fp8 import w8a16_matmul
+
+        return w8a16_matmul(x, p.qweight, p.scales, bias=p.bias, config=self.LINEAR_CFG)
+
+    def gate_up_act(self, x, p: Linear):
+        return self.act(self.linear(x, p))
+
+
+def make_backend(name: str) -> Backend:
+    """`<name>_lm` = the quantized backend `<name>` with lm_head quantized as well
+    (reference model.py:121-136)."""
+    base, quant_lm_head = (name[:-3], True) if name.endswith("_lm") else (name, False)
+    be = {
+        "fp16": Backend,
+        "w4_ref": W4RefBackend,
+        "ours": lambda: OursBackend("triton"),
+        "ours_cuda": lambda: OursBackend("cuda"),
+        "ours_fp8": OursFP8Backend,
+    }[base]()
+    if quant_lm_head:
+        if not be.quantized:
+            raise ValueError(f"{name}: only quantized backends can quantize lm_head")
+        be.name = name
+    be.quant_lm_head = quant_lm_head
+    return be
+
+
+# ------------------------------------------------------------------------------------- model
+@dataclass
+class Layer:
+    ln1: torch.Tensor
+    ln2: torch.Tensor
+    qkv: Linear
+    o: Linear
+    gate_up: Linear
+    down: Linear
+
+
+class QwenRunner:
+    """Qwen2 forward on a static KV cache (reference model.py:150-253)."""
+
+    def __init__(self, hf_model, backend: Backend, max_len: int = 2048, batch: int = 1):
+        cfg = hf_model.config
+        self.backend = backend
+        self.eps = cfg.rms_norm_eps
+        self.n_heads = cfg.num_attention_heads
+        self.n_kv = cfg.num_key_value_heads
+        self.head_dim = getattr(cfg, "head_dim", None) or cfg.hidden_size // self.n_heads
+        self.max_len = max_len
+        self.batch = batch
+        m = hf_model.model
+        dev = m.embed_tokens.weight.device
+        self.embed = m.embed_tokens.weight
+        self.lm_head = hf_model.lm_head.weight
+        self.final_norm = m.norm.weight
+        rope = getattr(cfg, "rope_parameters", None) or {}
+        theta = rope.get("rope_theta", getattr(cfg, "rope_theta", 10000.0))
+        d = self.head_dim
+        self.inv_freq = 1.0 / (theta ** (torch.arange(0, d, 2, device=dev, dtype=torch.float) / d))
+
+        def lin(*mods) -> Linear:
+            w = torch.cat([mm.weight.data for mm in mods], 0)
+            b = None
+            if mods[0].bias is not None:
+                b = torch.cat([mm.bias.data for mm in mods], 0)
+            if not backend.quantized:
+                return Linear(w=w, bias=b)
+            if hasattr(backend, "quantize"):  # formats other than int4 RTN (FP8)
+                return backend.quantize(w, b)
+            from kernels.quant import quantize_rtn
+
+            qw, s, z = quantize_rtn(w, config.GROUP_SIZE)
+            return Linear(qweight=qw, scales=s, zeros=z, bias=b)
+
+        # Optional quantized copy of lm_head (the fp16 table stays for the embedding lookup).
+        self.head_q = lin(hf_model.lm_head) if getattr(backend, "quant_lm_head", False) else None
+        self.layers = []
+        for layer in m.layers:
+            a, mlp = layer.self_attn, layer.mlp
+            self.layers.append(Layer(
+                ln1=layer.input_layernorm.weight, ln2=layer.post_attention_layernorm.weight,
+                qkv=lin(a.q_proj, a.k_proj, a.v_proj), o=lin(a.o_proj),
+                gate_up=lin(mlp.gate_proj, mlp.up_proj), down=lin(mlp.down_proj),
+            ))
+        shape = (len(self.layers), batch, self.n_kv, max_len, self.head_dim)
+        self.k_cache = torch.zeros(shape, device=dev, dtype=self.embed.dtype)
+        self.v_cache = torch.zeros(shape, device=dev, dtype=self.embed.dtype)
+
+    def weight_bytes(self) -> dict:
+        """Bytes of the swapped layers vs the parts that stay fp16 (reference model.py:196-210)."""
+
+        def nbytes(t):
+            return 0 if t is None else t.numel() * t.element_size()
+
+        def size(p: Linear):
+            if self.backend.quantized:
+                return nbytes(p.qweight) + nbytes(p.scales) + nbytes(p.zeros) + nbytes(p.bias)
+            return nbytes(p.w) + nbytes(p.bias)
+
+        layers = sum(size(p) for L in self.layers for p in (L.qkv, L.o, L.gate_up, L.down))
+        head = size(self.head_q) if self.head_q is not None else nbytes(self.lm_head)
+        return {"linear_layers": layers, "embed": nbytes(self.embed), "lm_head_read": head,
+                "lm_head_quantized": self.head_q is not None,
+                "lm_head_shared_with_embed": self.lm_head.data_ptr() == self.embed.data_ptr()}
+
+    def _rope(self, x, cos, sin):
+        x1, x2 = x[..., : self.head_dim // 2], x[..., self.head_dim // 2:]
+        return x * cos + torch.cat((-x2, x1), dim=-1) * sin
+
+    def _attention_sdpa(self, i, qkv, pos, cos, sin, mask, B, T):
+        """RoPE, cache write and SDPA over the whole cache, as the reference does
+        (reference model.py:236-244)."""
+        nq, nkv, hd = self.n_heads, self.n_kv, self.head_dim
+        q, k, v = qkv.split([nq * hd, nkv * hd, nkv * hd], dim=-1)
+        q = self._rope(q.view(B, T, nq, hd).transpose(1, 2), cos, sin)
+        k = self._rope(k.view(B, T, nkv, hd).transpose(1, 2), cos, sin)
+        v = v.view(B, T, nkv, hd).transpose(1, 2)
+        self.k_cache[i].index_copy_(2, pos, k)
+        self.v_cache[i].index_copy_(2, pos, v)
+        attn = F.scaled_dot_product_attention(
+            q, self.k_cache[i], self.v_cache[i], attn_mask=mask, enable_gqa=True)
+        return attn.transpose(1, 2).reshape(B, T, nq * hd)
+
+    @torch.no_grad()
+    def forward(self, tokens: torch.Tensor, pos: torch.Tensor, all_logits: bool = False):
+        """tokens [B, T]; pos: int64 tensor [T] of absolute positions. Graph-capturable."""
+        be, eps = self.backend, self.eps
+        B, T = tokens.shape
+        x = F.embedding(tokens, self.embed)
+        freqs = pos[:, None].float() * self.inv_freq[None, :]
+        emb = torch.cat((freqs, freqs), dim=-1)
+        cos, sin = emb.cos().to(x.dtype), emb.sin().to(x.dtype)
+        decode = be.fused_decode and T == 1
+        mask = None
+        if not decode:
+            keys = torch.arange(self.max_len, device=x.device)
+            mask = keys[None, :] <= pos[:, None]  # [T, max_len], True = attend
+
+        residual, h = x, None
+        for i, L in enumerate(self.layers):
+            if h is None:
+                h = be.norm(x, L.ln1, eps)
+            else:  # fused: residual += previous MLP output, then input norm of this layer
+                h, residual = be.norm(h, L.ln1, eps, residual=residual)
+            qkv = be.linear(h, L.qkv)
+            if decode:
+                from kernels.attention import decode_attention
+
+                attn = decode_attention(qkv, self.k_cache[i], self.v_cache[i], pos, cos, sin,
+                                        self.n_heads, self.n_kv)
+            else:
+                attn = self._attention_sdpa(i, qkv, pos, cos, sin, mask, B, T)
+            o = be.linear(attn, L.o)
+            h, residual = be.norm(o, L.ln2, eps, residual=residual)
+            h = be.linear(be.gate_up_act(h, L.gate_up), L.down)
+        h, _ = be.norm(h, self.final_norm, eps, residual=residual)
+        if not all_logits:
+            h = h[:, -1:]
+        if self.head_q is not None:
+            return be.linear(h, self.head_q)
+        return F.linear(h, self.lm_head)
+
+
+def random_qwen2(arch: dict, dtype=torch.float16, device="cuda", seed: int = 0):
+    """A Hugging Face Qwen2ForCausalLM of the given architecture with seeded random weights
+    (normal(0, 0.02) linears and embeddings, HF's own init), built directly on `device`. The
+    benchmark configs use random-init weights: no checkpoint is downloaded."""
+    import transformers
+
+    arch = dict(arch)
+    theta = arch.pop("rope_theta", 10000.0)
+    cfg = transformers.Qwen2Config(**arch, rope_parameters={"rope_theta": theta, "rope_type": "default"})
+    torch.manual_seed(seed)
+    with torch.device(device):
+        model = transformers.Qwen2ForCausalLM(cfg)
+    return model.to(dtype=dtype).eval()

@@ -69,6 +69,37 @@ def w4a16_matmul(x, qweight, scales, zeros, group_size=128, bias=None, config=No
     return out.view(*x.shape[:-1], N)
 
 
+def w4a16_swiglu(x, qweight, scales, zeros, group_size=128, bias=None, config=None):
+    """silu(g) * u for [g, u] = x @ dequant(W).T (+ bias): the gate_up projection with SwiGLU
+    fused into its epilogue (same roundings as w4a16_matmul followed by kernels.swiglu.swiglu_fused).
+    W holds [gate; up] (2I output columns); returns [..., I]. Shapes the fused kernel does not cover
+    (I % 32 != 0, other group sizes, unaligned operands) run the two kernels instead."""
+    K = x.shape[-1]
+    N = qweight.shape[1]
+    assert qweight.shape[0] * 8 == K and K % group_size == 0 and N % 2 == 0
+    I = N // 2
+    _lib.require_cuda("w4a16_swiglu", x, qweight, scales, zeros, bias)
+    _lib.require_dtype("w4a16_swiglu", torch.float16, x, scales, zeros, bias)
+    x2 = x.reshape(-1, K)
+    if x2.stride(1) != 1:
+        x2 = x2.contiguous()
+    aligned = all(t.data_ptr() % 16 == 0 for t in (x2, qweight, scales, zeros)) and x2.stride(0) % 8 == 0
+    cfg = _config(config)
+    if I % 32 != 0 or group_size != 128 or not aligned or cfg.flags & _lib.FLAG_GENERIC:
+        from kernels.swiglu import swiglu_fused
+
+        return swiglu_fused(w4a16_matmul(x, qweight, scales, zeros, group_size, bias, config))
+    qweight, scales, zeros = qweight.contiguous(), scales.contiguous(), zeros.contiguous()
+    if bias is not None:
+        bias = bias.contiguous()
+    M = x2.shape[0]
+    out = torch.empty((M, I), dtype=x.dtype, device=x.device)
+    _lib.call("dk_w4a16_swiglu", _lib.ptr(x2), x2.stride(0), _lib.ptr(qweight), _lib.ptr(scales),
+              _lib.ptr(zeros), _lib.ptr(bias), _lib.ptr(out), out.stride(0), M, I, K, group_size,
+              ctypes.byref(cfg), _lib.stream_of(x))
+    return out.view(*x.shape[:-1], I)
+
+
 def export_choices() -> dict:
     """Per-shape configs used so far (reference kernels/w4a16.py:333-335)."""
     return {",".join(map(str, k)): v for k, v in _choices.items()}

@@ -52,3 +52,49 @@ def swiglu_ref(gate, up) -> np.ndarray:
     with np.errstate(over="ignore"):
         act = (g / (np.float32(1.0) + np.exp(-g))).astype(np.float16)
     return act * np.asarray(up, dtype=np.float16)
+
+
+def rope_ref(x, cos, sin):
+    """x * cos + cat(-x2, x1) * sin in fp16, one rounding per op (kernels/e2e/model.py:212-214).
+    x [..., hd] fp16; cos, sin [hd] fp16."""
+    x = np.asarray(x, dtype=np.float16)
+    h = x.shape[-1] // 2
+    rot = np.concatenate([-x[..., h:], x[..., :h]], axis=-1)
+    return (x * cos) + (rot * sin)
+
+
+def rope_tables(pos: int, head_dim: int, theta: float):
+    """cos, sin fp16 [hd] for one position, as the runner computes them in fp32 and rounds
+    (kernels/e2e/model.py:166, 222-224)."""
+    inv = (1.0 / (theta ** (np.arange(0, head_dim, 2, dtype=np.float32) / head_dim))).astype(np.float32)
+    f = np.float32(pos) * inv
+    emb = np.concatenate([f, f]).astype(np.float32)
+    return np.cos(emb).astype(np.float16), np.sin(emb).astype(np.float16)
+
+
+def decode_attention_ref(qkv, k_cache, v_cache, pos, cos, sin, nq, nkv):
+    """One new token per sequence: RoPE on q, k; append k, v at `pos`; softmax attention over
+    positions 0..pos in fp32 (kernels/e2e/model.py:236-244 with T == 1).
+    qkv [B, (nq+2nkv)*hd] fp16; caches [B, nkv, max_len, hd] fp16 (updated in place).
+    Returns out [B, nq*hd] fp32."""
+    B = qkv.shape[0]
+    hd = k_cache.shape[-1]
+    G = nq // nkv
+    out = np.zeros((B, nq * hd), dtype=np.float32)
+    for b in range(B):
+        row = qkv[b]
+        q = row[: nq * hd].reshape(nq, hd)
+        k = row[nq * hd:(nq + nkv) * hd].reshape(nkv, hd)
+        v = row[(nq + nkv) * hd:].reshape(nkv, hd)
+        q = rope_ref(q, cos, sin)
+        k = rope_ref(k, cos, sin)
+        k_cache[b, :, pos] = k
+        v_cache[b, :, pos] = v
+        for hq in range(nq):
+            hk = hq // G
+            K = k_cache[b, hk, : pos + 1].astype(np.float32)
+            V = v_cache[b, hk, : pos + 1].astype(np.float32)
+            s = K @ q[hq].astype(np.float32) / np.float32(np.sqrt(hd))
+            s = np.exp(s - s.max())
+            out[b, hq * hd:(hq + 1) * hd] = (s / s.sum()) @ V
+    return out

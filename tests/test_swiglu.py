@@ -62,3 +62,19 @@ def test_swiglu_3d():
     assert out.shape == (2, 5, 256)
     exp = ref.swiglu_ref(gu[..., :256].numpy(), gu[..., 256:].numpy())
     assert _ulps(out, exp).max() <= 2
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 17920, 1536), (4, 2 * 8960, 1536), (16, 512, 1024), (2, 2 * 96, 256)])
+def test_gate_up_with_fused_swiglu(M, N, K):
+    """w4a16_swiglu (gate_up GEMV with SwiGLU in its epilogue) == swiglu_fused(w4a16_matmul(...))
+    within 1 fp16 ulp: the fused epilogue rounds g and u to fp16 before the activation exactly like
+    the two-kernel path, only the fp32 summation order of the GEMV differs."""
+    from kernels.w4a16 import w4a16_matmul, w4a16_swiglu
+    from _util import MATMUL_TOL, w4_case, w4_ref
+
+    x, qw, s, z, _ = w4_case(M, N, K)
+    xc, qc, sc, zc = to_cuda(x, qw, s, z)
+    fused = w4a16_swiglu(xc, qc, sc, zc).cpu().numpy()
+    gu = w4_ref(x, qw, s, z, None).astype(np.float16)
+    exp = ref.swiglu_ref(gu[:, : N // 2], gu[:, N // 2:])
+    np.testing.assert_allclose(fused.astype(np.float32), exp.astype(np.float32), rtol=2e-2, atol=4e-3)

@@ -101,14 +101,17 @@ def _ulps16(a, b):
 def test_exact_dequant_rounds_like_reference(M, N, K):
     """With EXACT the kernel dequantizes with the reference's fp16 rounding, so the only
     difference left is the fp32 summation order: the fp16 output is within one ulp of the
-    reference's fp32 result rounded to fp16."""
+    reference's fp32 result rounded to fp16, or within 2e-5 absolute where cancellation makes
+    the output so small that an ulp is below the summation-order noise."""
     from kernels.w4a16 import w4a16_matmul
 
     x, qw, s, z, b = w4_case(M, N, K, bias=True)
     xc, qc, sc, zc, bc = to_cuda(x, qw, s, z, b)
     out = w4a16_matmul(xc, qc, sc, zc, bias=bc, config={"EXACT": True}).cpu().numpy()
-    ref = w4_ref(x, qw, s, z, b).astype(np.float16)
-    assert _ulps16(out, ref).max() <= 1
+    ref32 = w4_ref(x, qw, s, z, b)
+    ref = ref32.astype(np.float16)
+    close = np.abs(out.astype(np.float32) - ref32) <= 2e-5
+    assert ((_ulps16(out, ref) <= 1) | close).all()
 
 
 def test_lm_head_m1():
