@@ -1,0 +1,425 @@
+#!/usr/bin/env python
+"""Benchmark of the decode hot path: Qwen2.5-1.5B-architecture batch-1 decode tok/s under CUDA
+graphs with libdecodek's W4A16 kernels, plus the W4A16 GEMV roofline.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--batch B]
+
+One process per GPU (torchrun for N > 1). The batch-1 1.5B path does not shard (each GPU holds the
+whole model), so N GPUs run N independent replicas: weak scaling, `value` = tokens of all ranks /
+the slowest rank's time. A "step" is one decode token (one graph replay) per replica.
+
+`--impl reference` times the reference's CPU path for the same config on the host cores: the
+oracle's restatement of the runner with dequantize-then-matmul fp32 linears
+(kernels/reference.py:39-45), a bounded number of decode steps at the same cache length.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for p in (str(ROOT), str(ROOT / "llm-decode-kernels_b200")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+import torch  # noqa: E402
+
+METRIC = "Qwen2.5-1.5B decode tok/s batch 1"
+PROMPT = 512
+MAX_LEN = 2048
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--backend", default="ours", help="runner backend of our arm (ours, ours_lm, ours_fp8)")
+    ap.add_argument("--no-extras", action="store_true", help="skip fp16 baseline, GEMV sweep and CPU baseline")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------------------ distributed
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi samples during the timed region (clocks, power, throttle reasons)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------ model
+def build_model(batch: int, seed: int = 0):
+    from kernels import config
+    from kernels.e2e.model import random_qwen2
+
+    model = random_qwen2(config.QWEN15, dtype=torch.float16, device="cuda", seed=seed)
+    return model
+
+
+def prompt_ids(vocab: int, batch: int, seed: int = 1, device="cuda"):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    return torch.randint(0, vocab, (batch, PROMPT), generator=g).to(device)
+
+
+def time_decode(dec, ids, steps: int, warmup: int, world: int) -> float:
+    """Seconds for `steps` graph replays after `warmup` untimed ones, bracketed by barrier + sync."""
+    dec.prefill(ids)
+    for _ in range(warmup):
+        dec.graph.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        dec.graph.replay()
+    end.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    return start.elapsed_time(end) / 1e3
+
+
+def gemv_roofline(runner, peak_gbs: float) -> dict:
+    """The dominant kernel (W4A16 GEMV): one decode step's linears (per layer qkv, o, gate_up with
+    fused SwiGLU, down; M = 1) captured back to back in one CUDA graph on the current stream and
+    timed with CUDA events; achieved = algorithmic bytes of those launches / their time."""
+    from kernels.bench.harness import capture
+    from kernels.quant import weight_bytes
+
+    be = runner.backend
+    H = runner.embed.shape[1]
+    x = torch.randn(1, 1, H, device="cuda", dtype=torch.float16)
+    nq, hd = runner.n_heads, runner.head_dim
+    a = torch.randn(1, 1, nq * hd, device="cuda", dtype=torch.float16)
+    I = runner.layers[0].down.qweight.shape[0] * 8
+
+    def chain():
+        for L in runner.layers:
+            be.linear(x, L.qkv)
+            be.linear(a, L.o)
+            act = be.gate_up_act(x, L.gate_up)
+            be.linear(act, L.down)
+
+    chain()
+    torch.cuda.synchronize()
+    graph, _ = capture(chain)
+    graph.replay()
+    torch.cuda.synchronize()
+    reps = 20
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(reps):
+        graph.replay()
+    end.record()
+    torch.cuda.synchronize()
+    sec = start.elapsed_time(end) / 1e3 / reps
+    launches = 4 * len(runner.layers)
+    byts = 0
+    for L in runner.layers:
+        for p, k_in, n_out in ((L.qkv, H, L.qkv.qweight.shape[1]), (L.o, nq * hd, H),
+                               (L.gate_up, H, I), (L.down, I, H)):
+            N = p.qweight.shape[1]
+            K = p.qweight.shape[0] * 8
+            byts += weight_bytes(N, K) + 2 * k_in + 2 * n_out + (2 * N if p.bias is not None else 0)
+    del graph
+    achieved = byts / launches / (sec / launches) / 1e9
+    return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
+            "frac": round(achieved / peak_gbs, 4), "traffic": traffic_per_launch(),
+            "kernel": "w4a16_gemv_kernel (28 x {qkv, o_proj, gate_up+SwiGLU, down}, M=1)",
+            "bytes_per_launch": round(byts / launches), "us_per_launch": round(sec / launches * 1e6, 3)}
+
+
+def traffic_per_launch():
+    """DRAM bytes per launch of the GEMV from the committed ncu summary of the same decode chain."""
+    f = ROOT / "profiles" / "w4a16_gemv_decode_chain.json"
+    try:
+        return json.loads(f.read_text())["dram_bytes_per_launch"]
+    except Exception:
+        return None
+
+
+def gemv_sweep(peak_gbs: float) -> dict:
+    """W4A16 GEMV % of HBM peak at M = 1 on every Qwen2.5-1.5B linear shape, timed like the
+    reference's harness (CUDA graph, rotating weight copies >= 4x L2)."""
+    from kernels import config
+    from kernels.bench.harness import time_rotating
+    from kernels.quant import quantize_rtn, weight_bytes
+    from kernels.w4a16 import w4a16_matmul
+
+    out = {}
+    cfg = {"STATIC_WEIGHTS": True}
+    for label, N, K in config.QWEN15_SHAPES:
+        w = (torch.randn(N, K, device="cuda") * 0.02).half()
+        qw, s, z = quantize_rtn(w, 128)
+        del w
+        x = torch.randn(1, K, device="cuda", dtype=torch.float16)
+        ms = time_rotating(lambda xx, q, ss, zz: w4a16_matmul(xx, q, ss, zz, config=cfg), (x, qw, s, z),
+                           rotate=(1, 2, 3))
+        byts = weight_bytes(N, K) + 2 * K + 2 * N
+        gbs = byts / (ms * 1e-3) / 1e9
+        out[label] = {"N": N, "K": K, "us": round(ms * 1e3, 2), "gbs": round(gbs), "pct_peak": round(100 * gbs / peak_gbs, 1)}
+        del qw, s, z
+        torch.cuda.empty_cache()
+    return out
+
+
+# ------------------------------------------------------------------------------ CPU baseline
+def cpu_decode_rate(model, steps: int, threads: int | None = None) -> dict:
+    """The reference's CPU path on the same model: OracleRunner (dequantize-then-fp32-matmul
+    linears), KV cache filled to the prompt length, `steps` timed decode tokens after one untimed."""
+    from kernels import config
+    from oracle.runner import OracleRunner
+
+    threads = threads or os.cpu_count()
+    torch.set_num_threads(threads)
+    weights = oracle_weights(model)
+    cfg = config.QWEN15
+    r = OracleRunner(weights, cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["head_dim"],
+                     cfg["rms_norm_eps"], cfg["rope_theta"], max_len=PROMPT + steps + 2)
+    g = torch.Generator().manual_seed(2)
+    r.k[:, :, :PROMPT] = torch.randn(r.k[:, :, :PROMPT].shape, generator=g)
+    r.v[:, :, :PROMPT] = torch.randn(r.v[:, :, :PROMPT].shape, generator=g)
+    tok = 1
+    r.step(tok, PROMPT)
+    t0 = time.perf_counter()
+    for i in range(steps):
+        tok = int(r.step(tok, PROMPT + 1 + i).argmax())
+    sec = time.perf_counter() - t0
+    return {"value": round(steps / sec, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{steps} decode tokens of the same model at cache length {PROMPT} on {threads} host threads "
+                      f"(oracle/runner.py, fp32 dequantize-then-matmul linears), after 1 untimed token"}
+
+
+def oracle_weights(model) -> dict:
+    """Packed int4 weights for the CPU oracle, quantized by libdecodek on the GPU (bit-exact with the
+    oracle's quantizer, tests/test_quant.py) to keep the setup short, then moved to the host."""
+    from kernels.quant import quantize_rtn
+
+    def q(*mods):
+        w = torch.cat([mm.weight.data for mm in mods], 0)
+        qw, s, z = quantize_rtn(w, 128)
+        return (qw.cpu().numpy(), s.cpu().numpy(), z.cpu().numpy())
+
+    def npy(t):
+        return t.detach().float().cpu().numpy()
+
+    m = model.model
+    layers = []
+    for layer in m.layers:
+        a, mlp = layer.self_attn, layer.mlp
+        layers.append({"ln1": npy(layer.input_layernorm.weight), "ln2": npy(layer.post_attention_layernorm.weight),
+                       "qkv": q(a.q_proj, a.k_proj, a.v_proj),
+                       "qkv_bias": torch.cat([a.q_proj.bias, a.k_proj.bias, a.v_proj.bias]).float().cpu().numpy(),
+                       "o": q(a.o_proj), "gate_up": q(mlp.gate_proj, mlp.up_proj), "down": q(mlp.down_proj)})
+    return {"embed": npy(m.embed_tokens.weight), "final_norm": npy(m.norm.weight), "layers": layers, "lm_head": None}
+
+
+# ------------------------------------------------------------------------------ arms
+def run_reference(args, world, rank):
+    """Reference arm: the reference's CPU path (oracle restatement) on the host cores, rank 0 only."""
+    if rank != 0:
+        return None
+    steps = max(1, min(args.steps, 16))
+    model = build_model(args.batch) if torch.cuda.is_available() else None
+    if model is None:
+        return {"impl": "reference", "unavailable": "needs a GPU to generate the benchmark model's weights"}
+    base = cpu_decode_rate(model, steps)
+    v = base["value"]
+    return {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": steps, "warmup": 1, "ms_per_step": round(1e3 / v, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_config(args, world),
+            "cpu_baseline": {**base, "value": v},
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def workload_config(args, world) -> dict:
+    return {"workload": "BASELINE configs[3]: Qwen2.5-1.5B-architecture decode (28 layers, hidden 1536, 12/2 heads, "
+                        "MLP 8960, vocab 151936, tied fp16 lm_head), random-init weights, W4A16 g128 linears, "
+                        f"uniform random {PROMPT}-token prompt, greedy decode under CUDA graphs",
+            "backend": args.backend, "global_batch": args.batch * world, "seq_len": PROMPT, "max_len": MAX_LEN,
+            "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+            "l2": "inputs larger than L2: each step reads ~1.2 GB of weights"}
+
+
+def run_ours(args, world, rank, local):
+    from kernels import _lib, config
+    from kernels.e2e.model import QwenRunner, make_backend
+    from kernels.e2e.run import GraphDecoder
+
+    peaks = config.peaks()
+    model = build_model(args.batch)
+    ids = prompt_ids(model.config.vocab_size, args.batch)
+    assert PROMPT + args.warmup + args.steps + 8 < MAX_LEN, "steps + warmup exceed the cache"
+    runner = QwenRunner(model, make_backend(args.backend), max_len=MAX_LEN, batch=args.batch)
+    dec = GraphDecoder(runner)
+    dec.capture(ids)
+    with ClockSampler(local) as clocks:
+        sec = time_decode(dec, ids, args.steps, max(args.warmup, 3), world)
+    sec = max_over_ranks(sec, world)
+    value = world * args.batch * args.steps / sec
+
+    # e2e: the public per-token API with host buffers (pinned H2D of the token, D2H of the next)
+    dec.prefill(ids)
+    t = dec.tok.cpu()
+    for _ in range(3):
+        t = dec.step_host(t).clone()
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        t = dec.step_host(t).clone()
+    e2e_sec = max_over_ranks(time.perf_counter() - t0, world)
+    e2e_value = world * args.batch * args.steps / e2e_sec
+
+    extras = {}
+    if not args.no_extras:
+        roof = gemv_roofline(runner, peaks["hbm_gbs"])
+        extras["roofline"] = {**roof, "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs, copy bandwidth)"}
+        if rank == 0:
+            extras["gemv_sweep"] = gemv_sweep(peaks["hbm_gbs"])
+        # fp16 cuBLAS baseline runner (the reference's fp16 backend) on the same model
+        base_runner = QwenRunner(model, make_backend("fp16"), max_len=MAX_LEN, batch=args.batch)
+        bdec = GraphDecoder(base_runner)
+        bdec.capture(ids)
+        bsec = max_over_ranks(time_decode(bdec, ids, args.steps, 3, world), world)
+        fp16_value = world * args.batch * args.steps / bsec
+        extras["fp16_baseline"] = {"tok_s": round(fp16_value, 1), "speedup": round(value / fp16_value, 3),
+                                   "what": "reference fp16 backend (cuBLAS F.linear, torch RMSNorm/SiLU, SDPA over "
+                                           "max_len) on the same model and graph decoder"}
+        del bdec, base_runner
+        torch.cuda.empty_cache()
+        if world == 1 and rank == 0:
+            extras["cpu_baseline"] = cpu_decode_rate(model, steps=4)
+    assert _lib.device_error() == 0, "a kernel recorded a device-side error"
+    per_step_launches = 7 * len(runner.layers) + 1 + (1 if runner.head_q is not None else 0)
+    if rank != 0:
+        return None
+    return {"metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": round(sec / args.steps * 1e3, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "w4a16 (fp16 activations, int4 weights, fp32 accumulation)",
+            "data": "synthetic (random-init weights, uniform random prompt ids)",
+            "config": workload_config(args, world), **extras,
+            "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": 8 * args.batch,
+                    "d2h_bytes_per_step": 8 * args.batch,
+                    "what": "GraphDecoder.step_host: pinned-host token -> device, graph replay, next token -> host, "
+                            "host wait, every step"},
+            "gpu_launches": per_step_launches * args.steps,
+            "clocks": clocks.summary()}
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_setup()
+    try:
+        if args.impl == "reference":
+            out = run_reference(args, world, rank)
+        else:
+            out = run_ours(args, world, rank, local)
+        if out is not None:
+            print(json.dumps(out), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
