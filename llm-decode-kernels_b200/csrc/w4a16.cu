@@ -75,14 +75,15 @@ struct SmemLayout {
 constexpr int kWarps = 8;  // consumer warps per CTA (plus one producer warp)
 
 // Offsets from the 1024-byte aligned base of dynamic shared memory.
-__host__ __device__ inline SmemLayout smem_layout(int cw, int nbuf, int M, int xs_pitch, int split) {
+__host__ __device__ inline SmemLayout smem_layout(int cw, int nbuf, int M, int xs_pitch, int /*split*/) {
   const int wpc = kWarps / cw;
   SmemLayout L;
   L.w_off = 0;
   L.sz_off = nbuf * cw * kBoxBytes;
   L.xs_off = L.sz_off + nbuf * cw * 2 * kSZBytes;
   L.red_off = L.xs_off + ((M * xs_pitch + 15) / 16) * 16;
-  L.bar_off = L.red_off + ((wpc > 1 || split > 1) ? wpc * M * cw * 32 * 4 : 0);
+  // reduction scratch, always present: the fused-SwiGLU and split-K epilogues use it at any wpc
+  L.bar_off = L.red_off + wpc * M * cw * 32 * 4;
   L.total = L.bar_off + 2 * nbuf * 8;
   return L;
 }

@@ -49,13 +49,13 @@ struct Layout8 {
   int w_off, xs_off, red_off, bar_off, total;
 };
 
-__host__ __device__ inline Layout8 layout8(int cw, int nbuf, int M, int xs_pitch, int split) {
+__host__ __device__ inline Layout8 layout8(int cw, int nbuf, int M, int xs_pitch, int /*split*/) {
   const int wpc = kWarps8 / cw;
   Layout8 L;
   L.w_off = 0;
   L.xs_off = nbuf * cw * kBox;
   L.red_off = L.xs_off + ((M * xs_pitch + 15) / 16) * 16;
-  L.bar_off = L.red_off + ((wpc > 1 || split > 1) ? wpc * M * cw * 32 * 4 : 0);
+  L.bar_off = L.red_off + wpc * M * cw * 32 * 4;  // the epilogue always reduces through it
   L.total = L.bar_off + 2 * nbuf * 8;
   return L;
 }
