@@ -305,7 +305,7 @@ def oracle_weights(model) -> dict:
         a, mlp = layer.self_attn, layer.mlp
         layers.append({"ln1": npy(layer.input_layernorm.weight), "ln2": npy(layer.post_attention_layernorm.weight),
                        "qkv": q(a.q_proj, a.k_proj, a.v_proj),
-                       "qkv_bias": torch.cat([a.q_proj.bias, a.k_proj.bias, a.v_proj.bias]).float().cpu().numpy(),
+                       "qkv_bias": torch.cat([a.q_proj.bias, a.k_proj.bias, a.v_proj.bias]).detach().float().cpu().numpy(),
                        "o": q(a.o_proj), "gate_up": q(mlp.gate_proj, mlp.up_proj), "down": q(mlp.down_proj)})
     return {"embed": npy(m.embed_tokens.weight), "final_norm": npy(m.norm.weight), "layers": layers, "lm_head": None}
 

@@ -138,7 +138,7 @@ int dk_swiglu(const void* gate, int64_t ldg, const void* up, int64_t ldu, void* 
  * fused projection output; caches [B, nkv, max_len, head_dim]; cos, sin [head_dim] for this
  * position; out [B, nq * head_dim]. `pos` is a device pointer (graph-capturable); a position outside
  * [0, max_len) writes nothing and sets DK_DEVERR_BAD_POSITION. splits: positions are cut into this
- * many slices combined inside a thread-block cluster (0 = automatic, max 8). head_dim 128. */
+ * many slices combined inside a thread-block cluster (0 = automatic, max 8). head_dim 32, 64 or 128. */
 int dk_decode_attention(const void* qkv, void* k_cache, void* v_cache, const int64_t* pos,
                         const void* cos, const void* sin, void* out, int64_t B, int64_t nq,
                         int64_t nkv, int64_t head_dim, int64_t max_len, int32_t splits,

@@ -23,7 +23,6 @@
 namespace dk {
 namespace {
 
-constexpr int kHd = 128;     // head dim supported by this kernel (Qwen2.5 1.5B and 7B)
 constexpr int kThreads = 128;
 constexpr int kMaxGroup = 8;  // query heads per kv head
 constexpr int kMaxSplit = 8;
@@ -42,14 +41,34 @@ struct AttnParams {
 };
 
 // RoPE for element d of one head, with the reference's fp16 rounding:
-// x*cos + rot*sin, rot = -x[d+64] (d < 64) or x[d-64] (d >= 64).
+// x*cos + rot*sin, rot = -x[d+hd/2] (d < hd/2) or x[d-hd/2] (d >= hd/2).
+template <int kHd>
 __device__ __forceinline__ __half rope_elem(const __half* x, int d, const __half* cs, const __half* sn) {
   const __half rot = d < kHd / 2 ? __hneg(x[d + kHd / 2]) : x[d - kHd / 2];
   return __hadd_rn(__hmul_rn(x[d], cs[d]), __hmul_rn(rot, sn[d]));
 }
 
-template <int G>
+// kHd / 32 consecutive fp16 values of a cache row for one lane, as fp32.
+template <int E>
+__device__ __forceinline__ void load_lane(const __half* row, int lane, float (&v)[E]) {
+  if constexpr (E == 4) {
+    const uint2 raw = __ldcg(reinterpret_cast<const uint2*>(row) + lane);
+    const __half* h = reinterpret_cast<const __half*>(&raw);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] = __half2float(h[e]);
+  } else if constexpr (E == 2) {
+    const unsigned raw = __ldcg(reinterpret_cast<const unsigned*>(row) + lane);
+    const __half* h = reinterpret_cast<const __half*>(&raw);
+    v[0] = __half2float(h[0]);
+    v[1] = __half2float(h[1]);
+  } else {
+    v[0] = __half2float(__ldcg(row + lane));
+  }
+}
+
+template <int G, int kHd>
 __global__ void __launch_bounds__(kThreads) decode_attention_kernel(const AttnParams p) {
+  constexpr int E = kHd / 32;  // head-dim elements per lane in the score loop
   __shared__ float qs[G][kHd];          // rotated q (fp32)
   __shared__ __half knew[kHd], vnew[kHd];
   __shared__ float part_o[G][kHd];      // this CTA's unnormalized output
@@ -80,8 +99,8 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(const AttnPa
 
   for (int d = tid; d < kHd; d += kThreads) {
     for (int g = 0; g < G; ++g)
-      qs[g][d] = __half2float(rope_elem(qrow + (h * G + g) * kHd, d, p.cos, p.sin)) * p.scale;
-    knew[d] = rope_elem(krow, d, p.cos, p.sin);
+      qs[g][d] = __half2float(rope_elem<kHd>(qrow + (h * G + g) * kHd, d, p.cos, p.sin)) * p.scale;
+    knew[d] = rope_elem<kHd>(krow, d, p.cos, p.sin);
     vnew[d] = vrow[d];
   }
   __syncthreads();
@@ -96,21 +115,18 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(const AttnPa
   const int n = j1 - j0;
   for (int jj = warp; jj < n; jj += kThreads / 32) {
     const int j = j0 + jj;
-    float kv[4];
+    float kv[E];
     if (j == pos) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) kv[e] = __half2float(knew[lane * 4 + e]);
+      for (int e = 0; e < E; ++e) kv[e] = __half2float(knew[lane * E + e]);
     } else {
-      const uint2 raw = __ldcg(reinterpret_cast<const uint2*>(kc + static_cast<int64_t>(j) * kHd) + lane);
-      const __half* kh = reinterpret_cast<const __half*>(&raw);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) kv[e] = __half2float(kh[e]);
+      load_lane<E>(kc + static_cast<int64_t>(j) * kHd, lane, kv);
     }
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       float s = 0.f;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) s = fmaf(qs[g][lane * 4 + e], kv[e], s);
+      for (int e = 0; e < E; ++e) s = fmaf(qs[g][lane * E + e], kv[e], s);
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
       if (lane == 0) scores[g * slice + jj] = s;
@@ -193,7 +209,8 @@ extern "C" int dk_decode_attention(const void* qkv, void* k_cache, void* v_cache
                                    int64_t nkv, int64_t head_dim, int64_t max_len, int32_t splits,
                                    dk_stream_t stream) {
   if (B <= 0 || nq <= 0 || nkv <= 0 || max_len <= 0) return set_error(DK_ERR_INVALID, "decode_attention: bad sizes");
-  if (head_dim != kHd) return set_error(DK_ERR_UNSUPPORTED, "decode_attention: head_dim %lld (only 128)", (long long)head_dim);
+  if (head_dim != 32 && head_dim != 64 && head_dim != 128)
+    return set_error(DK_ERR_UNSUPPORTED, "decode_attention: head_dim %lld (32, 64 or 128)", (long long)head_dim);
   if (nq % nkv != 0 || nq / nkv > kMaxGroup)
     return set_error(DK_ERR_UNSUPPORTED, "decode_attention: %lld query heads per kv head (max %d)",
                      (long long)(nq / nkv), kMaxGroup);
@@ -223,7 +240,8 @@ extern "C" int dk_decode_attention(const void* qkv, void* k_cache, void* v_cache
   cudaError_t e;
 #define DK_ATTN(GG)                                                                                      \
   case GG: {                                                                                             \
-    auto k = decode_attention_kernel<GG>;                                                                \
+    auto k = head_dim == 128 ? decode_attention_kernel<GG, 128>                                          \
+             : head_dim == 64 ? decode_attention_kernel<GG, 64> : decode_attention_kernel<GG, 32>;       \
     if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
     e = launch(k, grid, dim3(kThreads), smem, st, pdl_enabled(), dim3(1, 1, S), p);                       \
     break;                                                                                               \
