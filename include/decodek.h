@@ -101,6 +101,20 @@ int dk_w4a16_swiglu(const void* x, int64_t ldx, const int32_t* qweight, const vo
                     int64_t I, int64_t K, int64_t group_size, const dk_matmul_config* cfg,
                     dk_stream_t stream);
 
+/* Fused residual add + RMSNorm + W4A16 projection (kernels/e2e/model.py:231-235 and 246-247 in one
+ * kernel): h = x (+ residual, fp16 add, written to residual_out when residual != NULL);
+ * xn = norm_weight * fp16(h * rsqrt(mean(h^2) + eps)) (the same roundings as dk_rmsnorm); then
+ * y = xn @ dequant(W).T (+ bias), or with swiglu != 0 the gate_up + SwiGLU output of
+ * dk_w4a16_swiglu (N = 2I columns of W, y is [M, I]). residual_out must not alias x or residual.
+ * Needs the fast-path conditions of dk_w4a16_swiglu / dk_w4a16_matmul (DK_ERR_UNSUPPORTED
+ * otherwise: run dk_rmsnorm then the projection). */
+int dk_w4a16_rmsnorm_matmul(const void* x, int64_t ldx, const void* residual, int64_t ldr,
+                            const void* norm_weight, float eps, void* residual_out, int64_t ldro,
+                            const int32_t* qweight, const void* scales, const void* zeros,
+                            const void* bias, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
+                            int64_t group_size, int32_t swiglu, const dk_matmul_config* cfg,
+                            dk_stream_t stream);
+
 /* ---- FP8 e4m3 weight-only format: kernels/fp8.py ------------------------------------------ */
 /* quantize_fp8 (kernels/fp8.py:25-30): w fp16 [N, K] (row stride ldw) -> wq e4m3 [K, N],
  * scale fp16 [N]; per-row absmax / 448 clamped >= 1e-12. Bit-exact with the reference. */
@@ -139,10 +153,13 @@ int dk_swiglu(const void* gate, int64_t ldg, const void* up, int64_t ldu, void* 
  * position; out [B, nq * head_dim]. `pos` is a device pointer (graph-capturable); a position outside
  * [0, max_len) writes nothing and sets DK_DEVERR_BAD_POSITION. splits: positions are cut into this
  * many slices combined inside a thread-block cluster (0 = automatic, max 8). head_dim 32, 64 or 128. */
+#define DK_ATTN_STATIC_CACHE 1 /* flags: the cache rows before *pos and *pos itself were not written
+                                  by the kernel immediately before this one (true inside a decode
+                                  step): the cache slice is fetched before waiting for that kernel */
 int dk_decode_attention(const void* qkv, void* k_cache, void* v_cache, const int64_t* pos,
                         const void* cos, const void* sin, void* out, int64_t B, int64_t nq,
                         int64_t nkv, int64_t head_dim, int64_t max_len, int32_t splits,
-                        dk_stream_t stream);
+                        int32_t flags, dk_stream_t stream);
 
 #ifdef __cplusplus
 }

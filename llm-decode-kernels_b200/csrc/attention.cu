@@ -36,6 +36,8 @@ struct AttnParams {
   const __half* sin;   // [hd]
   __half* out;         // [B, nq * hd]
   int nq, nkv, max_len;
+  int slice_max;     // positions per CTA at most (sizes the shared-memory slices)
+  int static_cache;  // see DK_ATTN_STATIC_CACHE
   float scale;
   int* err;
 };
@@ -69,18 +71,27 @@ __device__ __forceinline__ void load_lane(const __half* row, int lane, float (&v
 template <int G, int kHd>
 __global__ void __launch_bounds__(kThreads) decode_attention_kernel(const AttnParams p) {
   constexpr int E = kHd / 32;  // head-dim elements per lane in the score loop
-  __shared__ float qs[G][kHd];          // rotated q (fp32)
+  __shared__ float qs[G][kHd];          // rotated q (fp32, pre-scaled)
   __shared__ __half knew[kHd], vnew[kHd];
   __shared__ float part_o[G][kHd];      // this CTA's unnormalized output
   __shared__ float part_m[G], part_l[G];
-  extern __shared__ float scores[];     // [G][slice]
+  __shared__ __align__(8) uint64_t bar;
+  extern __shared__ __align__(128) uint8_t dsm[];  // Ks[slice][hd] | Vs[slice][hd] | scores[G][slice]
 
-  pdl_trigger();
-  pdl_wait();
   const int h = blockIdx.x, b = blockIdx.y, rank = blockIdx.z, S = gridDim.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_trigger();
+  // With a static cache the rows before `pos` and `pos` itself were written by kernels that
+  // finished before the previous one started, so the slice can be fetched before waiting.
+  if (!p.static_cache) pdl_wait();
   const int64_t pos64 = *p.pos;
   if (pos64 < 0 || pos64 >= p.max_len) {  // same decision in every CTA of the cluster
+    if (p.static_cache) pdl_wait();
     if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
       record_device_error(p.err, DK_DEVERR_BAD_POSITION);
     return;
@@ -88,15 +99,26 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(const AttnPa
   const int L = static_cast<int>(pos64) + 1;  // positions 0..pos
   const int slice = (L + S - 1) / S;
   const int j0 = min(rank * slice, L), j1 = min(j0 + slice, L);
+  const int n = j1 - j0;
   const int pos = L - 1;
+  const int64_t cache_base = (static_cast<int64_t>(b) * p.nkv + h) * p.max_len * kHd;
+  __half* kc = p.k_cache + cache_base;
+  __half* vc = p.v_cache + cache_base;
+  __half* Ks = reinterpret_cast<__half*>(dsm);
+  __half* Vs = Ks + static_cast<size_t>(p.slice_max) * kHd;
+  float* scores = reinterpret_cast<float*>(Vs + static_cast<size_t>(p.slice_max) * kHd);
+  if (tid == 0 && n > 0) {
+    const uint32_t bytes = static_cast<uint32_t>(n) * kHd * 2;
+    mbar_arrive_expect_tx(&bar, 2 * bytes);
+    bulk_g2s(Ks, kc + static_cast<int64_t>(j0) * kHd, bytes, &bar);
+    bulk_g2s(Vs, vc + static_cast<int64_t>(j0) * kHd, bytes, &bar);
+  }
+  if (p.static_cache) pdl_wait();  // qkv comes from the previous kernel
+
   const int row = (p.nq + 2 * p.nkv) * kHd;
   const __half* qrow = p.qkv + static_cast<int64_t>(b) * row;
   const __half* krow = qrow + p.nq * kHd + h * kHd;
   const __half* vrow = qrow + (p.nq + p.nkv) * kHd + h * kHd;
-  const int64_t cache_base = (static_cast<int64_t>(b) * p.nkv + h) * p.max_len * kHd;
-  __half* kc = p.k_cache + cache_base;
-  __half* vc = p.v_cache + cache_base;
-
   for (int d = tid; d < kHd; d += kThreads) {
     for (int g = 0; g < G; ++g)
       qs[g][d] = __half2float(rope_elem<kHd>(qrow + (h * G + g) * kHd, d, p.cos, p.sin)) * p.scale;
@@ -104,24 +126,31 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(const AttnPa
     vnew[d] = vrow[d];
   }
   __syncthreads();
-  if (pos >= j0 && pos < j1) {  // this CTA owns the new token: append it to the cache
+  // The new token's k, v come from registers/shared memory; the owner of `pos` appends them to the
+  // cache (the bulk copy may have read the stale row at `pos`: that row is never used below).
+  if (pos >= j0 && pos < j1) {
     for (int d = tid; d < kHd; d += kThreads) {
       kc[static_cast<int64_t>(pos) * kHd + d] = knew[d];
       vc[static_cast<int64_t>(pos) * kHd + d] = vnew[d];
     }
   }
+  bool ok = true;
+  if (n > 0) ok = mbar_wait(&bar, 0, p.err, DK_DEVERR_WAIT_FULL);
+  if (__syncthreads_or(!ok)) {
+    if (S > 1) {
+      cluster_sync();
+      cluster_sync();
+    }
+    return;
+  }
 
-  // scores: each warp takes positions j0+warp, j0+warp+4, ...; lanes split the head dim (4 each)
-  const int n = j1 - j0;
+  // scores: warp w takes positions j0+w, j0+w+4, ...; lanes split the head dim (E each)
   for (int jj = warp; jj < n; jj += kThreads / 32) {
     const int j = j0 + jj;
     float kv[E];
-    if (j == pos) {
+    const __half* ksrc = (j == pos) ? knew : Ks + static_cast<size_t>(jj) * kHd;
 #pragma unroll
-      for (int e = 0; e < E; ++e) kv[e] = __half2float(knew[lane * E + e]);
-    } else {
-      load_lane<E>(kc + static_cast<int64_t>(j) * kHd, lane, kv);
-    }
+    for (int e = 0; e < E; ++e) kv[e] = __half2float(ksrc[lane * E + e]);
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       float s = 0.f;
@@ -129,20 +158,20 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(const AttnPa
       for (int e = 0; e < E; ++e) s = fmaf(qs[g][lane * E + e], kv[e], s);
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if (lane == 0) scores[g * slice + jj] = s;
+      if (lane == 0) scores[g * p.slice_max + jj] = s;
     }
   }
   __syncthreads();
-  // softmax partials per head (warp g handles head g, g+4, ...)
+  // softmax partials per head (warp w handles heads w, w+4, ...)
   for (int g = warp; g < G; g += kThreads / 32) {
     float m = -FLT_MAX;
-    for (int jj = lane; jj < n; jj += 32) m = fmaxf(m, scores[g * slice + jj]);
+    for (int jj = lane; jj < n; jj += 32) m = fmaxf(m, scores[g * p.slice_max + jj]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     float l = 0.f;
     for (int jj = lane; jj < n; jj += 32) {
-      const float e = __expf(scores[g * slice + jj] - m);
-      scores[g * slice + jj] = e;
+      const float e = __expf(scores[g * p.slice_max + jj] - m);
+      scores[g * p.slice_max + jj] = e;
       l += e;
     }
 #pragma unroll
@@ -159,10 +188,9 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(const AttnPa
 #pragma unroll
     for (int g = 0; g < G; ++g) acc[g] = 0.f;
     for (int jj = 0; jj < n; ++jj) {
-      const int j = j0 + jj;
-      const float v = (j == pos) ? __half2float(vnew[d]) : __half2float(__ldcg(vc + static_cast<int64_t>(j) * kHd + d));
+      const float v = (j0 + jj == pos) ? __half2float(vnew[d]) : __half2float(Vs[static_cast<size_t>(jj) * kHd + d]);
 #pragma unroll
-      for (int g = 0; g < G; ++g) acc[g] = fmaf(scores[g * slice + jj], v, acc[g]);
+      for (int g = 0; g < G; ++g) acc[g] = fmaf(scores[g * p.slice_max + jj], v, acc[g]);
     }
 #pragma unroll
     for (int g = 0; g < G; ++g) part_o[g][d] = acc[g];
@@ -207,7 +235,7 @@ using namespace dk;
 extern "C" int dk_decode_attention(const void* qkv, void* k_cache, void* v_cache, const int64_t* pos,
                                    const void* cos, const void* sin, void* out, int64_t B, int64_t nq,
                                    int64_t nkv, int64_t head_dim, int64_t max_len, int32_t splits,
-                                   dk_stream_t stream) {
+                                   int32_t flags, dk_stream_t stream) {
   if (B <= 0 || nq <= 0 || nkv <= 0 || max_len <= 0) return set_error(DK_ERR_INVALID, "decode_attention: bad sizes");
   if (head_dim != 32 && head_dim != 64 && head_dim != 128)
     return set_error(DK_ERR_UNSUPPORTED, "decode_attention: head_dim %lld (32, 64 or 128)", (long long)head_dim);
@@ -234,7 +262,12 @@ extern "C" int dk_decode_attention(const void* qkv, void* k_cache, void* v_cache
   p.err = device_info().err_word;
   const int G = static_cast<int>(nq / nkv);
   const int slice_max = static_cast<int>((max_len + S - 1) / S);
-  const size_t smem = static_cast<size_t>(G) * slice_max * sizeof(float);
+  p.slice_max = slice_max;
+  p.static_cache = (flags & DK_ATTN_STATIC_CACHE) ? 1 : 0;
+  const size_t smem = 2 * static_cast<size_t>(slice_max) * head_dim * 2 + static_cast<size_t>(G) * slice_max * 4;
+  if (smem > static_cast<size_t>(device_info().max_smem_optin) - 8 * 1024)
+    return set_error(DK_ERR_UNSUPPORTED, "decode_attention: max_len %lld needs more shared memory per CTA than "
+                     "the device has (use more splits)", (long long)max_len);
   const dim3 grid(static_cast<unsigned>(nkv), static_cast<unsigned>(B), static_cast<unsigned>(S));
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   cudaError_t e;
@@ -242,7 +275,7 @@ extern "C" int dk_decode_attention(const void* qkv, void* k_cache, void* v_cache
   case GG: {                                                                                             \
     auto k = head_dim == 128 ? decode_attention_kernel<GG, 128>                                          \
              : head_dim == 64 ? decode_attention_kernel<GG, 64> : decode_attention_kernel<GG, 32>;       \
-    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);                    \
     e = launch(k, grid, dim3(kThreads), smem, st, pdl_enabled(), dim3(1, 1, S), p);                       \
     break;                                                                                               \
   }

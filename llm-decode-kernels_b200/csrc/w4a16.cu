@@ -65,6 +65,13 @@ struct GemvParams {
   int xs_pitch;      // bytes per staged x row
   int static_weights;
   int swiglu_i;      // > 0: fused SwiGLU over gate columns [0, I) and up columns [I, 2I); y is [M, I]
+  // optional fused residual + RMSNorm of x before the matmul (norm_w == nullptr: x as given)
+  const __half* norm_w;
+  const __half* res;  // may be nullptr (norm without residual add)
+  int64_t ldr;
+  __half* res_out;    // receives x + res (written by one CTA) when res != nullptr
+  int64_t ldro;
+  float eps;
   int* err;
 };
 
@@ -196,6 +203,89 @@ __device__ __forceinline__ void consume_chunk_stage(const uint8_t* __restrict__ 
   }
 }
 
+// Stage x[:, K slice of this CTA] into shared memory, each 8-element block permuted to
+// (0,4,1,5,2,6,3,7) for the MMA fragments. With `norm_w` the staged rows are the fused residual
+// add + RMSNorm of the input, with the rounding of kernels/rmsnorm.py:28-37 (and the rmsnorm kernel
+// of this library): h = x + residual (fp16 add), var = sum(h^2)/K in fp32, out = w * fp16(h / sqrt(
+// var + eps)); every CTA reads the whole row for the sum of squares (per-warp partials added in a
+// fixed order: deterministic), and `writer` (one CTA) stores h as the new residual stream.
+__device__ __forceinline__ void stage_x(const GemvParams& p, uint8_t* xs, int s_begin, int nst, bool writer) {
+  constexpr int kThr = kWarps * 32;
+  const int tid = threadIdx.x;
+  const int kb0 = s_begin * kStageRows;  // first packed row (block of 8 K values)
+  const int nblk = nst * kStageRows;
+  __shared__ float inv[16];
+  __shared__ float part[16][kWarps];
+  const bool norm = p.norm_w != nullptr;
+  if (norm) {
+    const int nv = p.K / 8;
+    for (int m = 0; m < p.M; ++m) {
+      float acc = 0.f;
+      for (int v = tid; v < nv; v += kThr) {
+        uint4 a = __ldcg(reinterpret_cast<const uint4*>(p.x + m * p.ldx) + v);
+        if (p.res != nullptr) {
+          const uint4 r = __ldcg(reinterpret_cast<const uint4*>(p.res + m * p.ldr) + v);
+          __half2* ah = reinterpret_cast<__half2*>(&a);
+          const __half2* rh = reinterpret_cast<const __half2*>(&r);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) ah[j] = __hadd2_rn(ah[j], rh[j]);
+          if (writer) reinterpret_cast<uint4*>(p.res_out + m * p.ldro)[v] = a;
+        }
+        const __half2* ah = reinterpret_cast<const __half2*>(&a);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __half22float2(ah[j]);
+          acc = fmaf(f.x, f.x, acc);
+          acc = fmaf(f.y, f.y, acc);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if ((tid & 31) == 0) part[m][tid >> 5] = acc;
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(kThr) : "memory");
+    if (tid < p.M) {
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) tot += part[tid][w];
+      inv[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(p.K)), p.eps)));
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(kThr) : "memory");
+  }
+  for (int i = tid; i < p.M * nblk; i += kThr) {
+    const int m = i / nblk, b = i % nblk;
+    const int k = (kb0 + b) * 8;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (k < p.K) {
+      v = __ldcg(reinterpret_cast<const uint4*>(p.x + m * p.ldx + k));
+      if (norm) {
+        __half2* vh = reinterpret_cast<__half2*>(&v);
+        if (p.res != nullptr) {
+          const uint4 r = __ldcg(reinterpret_cast<const uint4*>(p.res + m * p.ldr + k));
+          const __half2* rh = reinterpret_cast<const __half2*>(&r);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) vh[j] = __hadd2_rn(vh[j], rh[j]);
+        }
+        const uint4 wv = __ldg(reinterpret_cast<const uint4*>(p.norm_w + k));
+        const __half2* wh = reinterpret_cast<const __half2*>(&wv);
+        const float s = inv[m];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __half22float2(vh[j]);
+          vh[j] = __hmul2_rn(wh[j], __floats2half2_rn(__fmul_rn(f.x, s), __fmul_rn(f.y, s)));
+        }
+      }
+    }
+    uint4 o;
+    o.x = prmt(v.x, v.z, 0x5410);  // (x0, x4)
+    o.y = prmt(v.x, v.z, 0x7632);  // (x1, x5)
+    o.z = prmt(v.y, v.w, 0x5410);  // (x2, x6)
+    o.w = prmt(v.y, v.w, 0x7632);  // (x3, x7)
+    *reinterpret_cast<uint4*>(xs + m * p.xs_pitch + b * 16) = o;
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(kThr) : "memory");
+}
+
 // CW chunks (32 columns each) per tile; kWarps / CW warps per chunk split the tile's stages
 // round-robin and meet in shared memory at the end of the tile.
 template <int NT, int CW, bool EXACT>
@@ -272,25 +362,8 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 3 - NT)  // M <= 8: two CTA
     __syncwarp();
   } else {
     // ---------------------------------------------------------------- consumer warps
-    pdl_wait();  // x comes from the previous kernel
-    {
-      // stage x[:, K slice] into shared memory, 8-element blocks permuted to (0,4,1,5,2,6,3,7)
-      const int kb0 = s_begin * kStageRows;  // first packed row (block of 8 K values)
-      const int nblk = nst * kStageRows;
-      for (int i = threadIdx.x; i < p.M * nblk; i += kWarps * 32) {
-        const int m = i / nblk, b = i % nblk;
-        const int k = (kb0 + b) * 8;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (k < p.K) v = __ldcg(reinterpret_cast<const uint4*>(p.x + m * p.ldx + k));
-        uint4 o;
-        o.x = prmt(v.x, v.z, 0x5410);  // (x0, x4)
-        o.y = prmt(v.x, v.z, 0x7632);  // (x1, x5)
-        o.z = prmt(v.y, v.w, 0x5410);  // (x2, x6)
-        o.w = prmt(v.y, v.w, 0x7632);  // (x3, x7)
-        *reinterpret_cast<uint4*>(smem + L.xs_off + m * p.xs_pitch + b * 16) = o;
-      }
-      asm volatile("bar.sync 1, %0;" ::"r"(kWarps * 32) : "memory");
-    }
+    pdl_wait();  // x (and the residual) come from the previous kernels
+    stage_x(p, smem + L.xs_off, s_begin, nst, blockIdx.x == 0 && blockIdx.y == 0);
     const int g = lane >> 2;  // MMA group: A rows g, g+8 ; B column g
     const int t = lane & 3;   // thread in group: K slots 2t.., 2t+8..
     const int slot = warp % CW;  // chunk of the tile this warp works on
@@ -626,9 +699,18 @@ int launch_gemv(const CUtensorMap& mq, const CUtensorMap& ms, const CUtensorMap&
 }
 
 // Shared host path of dk_w4a16_matmul (swiglu_i == 0) and dk_w4a16_swiglu (swiglu_i == I, N == 2I).
+struct NormArgs {
+  const void* w = nullptr;  // RMSNorm weight [K]; nullptr = no fused norm
+  const void* res = nullptr;
+  int64_t ldr = 0;
+  void* res_out = nullptr;
+  int64_t ldro = 0;
+  float eps = 1e-6f;
+};
+
 int run_fast(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const void* zeros,
              const void* bias, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group_size,
-             const dk_matmul_config* cfg, int swiglu_i, cudaStream_t st) {
+             const dk_matmul_config* cfg, int swiglu_i, const NormArgs& na, cudaStream_t st) {
   const int flags = cfg ? cfg->flags : 0;
   CUtensorMap mq, ms, mz;
   if (!make_tensor_map_2d(&mq, qweight, CU_TENSOR_MAP_DATA_TYPE_INT32, N, K / 8, N * 4, 32, kStageRows,
@@ -660,6 +742,12 @@ int run_fast(const void* x, int64_t ldx, const int32_t* qweight, const void* sca
     p.xs_pitch = xs_pitch_for(p.split_stages);
     p.static_weights = (flags & DK_FLAG_STATIC_WEIGHTS) ? 1 : 0;
     p.swiglu_i = swiglu_i;
+    p.norm_w = static_cast<const __half*>(na.w);
+    p.res = na.res ? static_cast<const __half*>(na.res) + m0 * na.ldr : nullptr;
+    p.ldr = na.ldr;
+    p.res_out = na.res_out ? static_cast<__half*>(na.res_out) + m0 * na.ldro : nullptr;
+    p.ldro = na.ldro;
+    p.eps = na.eps;
     p.err = dev.err_word;
     const int rc = launch_gemv(mq, ms, mz, p, c, (flags & DK_FLAG_EXACT_DEQUANT) != 0, st);
     if (rc != DK_OK) return rc;
@@ -711,7 +799,7 @@ extern "C" int dk_w4a16_matmul(const void* x, int64_t ldx, const int32_t* qweigh
     if (e != cudaSuccess) return set_error(DK_ERR_CUDA, "w4a16 generic launch: %s", cudaGetErrorString(e));
     return DK_OK;
   }
-  return run_fast(x, ldx, qweight, scales, zeros, bias, y, ldy, M, N, K, group_size, cfg, 0, st);
+  return run_fast(x, ldx, qweight, scales, zeros, bias, y, ldy, M, N, K, group_size, cfg, 0, NormArgs(), st);
 }
 
 extern "C" int dk_w4a16_swiglu(const void* x, int64_t ldx, const int32_t* qweight, const void* scales,
@@ -727,5 +815,38 @@ extern "C" int dk_w4a16_swiglu(const void* x, int64_t ldx, const int32_t* qweigh
     return set_error(DK_ERR_UNSUPPORTED,
                      "w4a16_swiglu: the fused kernel needs I %% 32 == 0, group_size 128 and 16-byte aligned operands");
   return run_fast(x, ldx, qweight, scales, zeros, bias, y, ldy, M, 2 * I, K, group_size, cfg, static_cast<int>(I),
-                  reinterpret_cast<cudaStream_t>(stream));
+                  NormArgs(), reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int dk_w4a16_rmsnorm_matmul(const void* x, int64_t ldx, const void* residual, int64_t ldr,
+                                       const void* norm_weight, float eps, void* residual_out, int64_t ldro,
+                                       const int32_t* qweight, const void* scales, const void* zeros,
+                                       const void* bias, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
+                                       int64_t group_size, int32_t swiglu, const dk_matmul_config* cfg,
+                                       dk_stream_t stream) {
+  using namespace dk;
+  const int64_t ycols = swiglu ? N / 2 : N;
+  int rc = check_w4a16_args("w4a16_rmsnorm_matmul", x, ldx, qweight, scales, zeros, y, ldy, M, N, ycols, K, group_size);
+  if (rc != DK_OK) return rc;
+  if (M == 0 || N == 0) return DK_OK;
+  if (!norm_weight) return set_error(DK_ERR_INVALID, "w4a16_rmsnorm_matmul: norm_weight is NULL");
+  if (residual && (!residual_out || ldr < K || ldro < K))
+    return set_error(DK_ERR_INVALID, "w4a16_rmsnorm_matmul: residual needs residual_out and row strides >= K");
+  const int flags = cfg ? cfg->flags : 0;
+  const bool aligned = aligned16(norm_weight) && (!residual || (aligned16(residual) && aligned16(residual_out) &&
+                                                                 ldr % 8 == 0 && ldro % 8 == 0));
+  if (!aligned || K % 8 != 0 || (swiglu && (N % 2 != 0 || (N / 2) % 32 != 0)) ||
+      !fast_ok(x, ldx, qweight, scales, zeros, N, K, group_size, flags))
+    return set_error(DK_ERR_UNSUPPORTED,
+                     "w4a16_rmsnorm_matmul: the fused kernel needs group_size 128, N %% 8 == 0 (I %% 32 == 0 with "
+                     "swiglu) and 16-byte aligned operands and strides");
+  NormArgs na;
+  na.w = norm_weight;
+  na.res = residual;
+  na.ldr = ldr;
+  na.res_out = residual_out;
+  na.ldro = ldro;
+  na.eps = eps;
+  return run_fast(x, ldx, qweight, scales, zeros, bias, y, ldy, M, N, K, group_size, cfg,
+                  swiglu ? static_cast<int>(N / 2) : 0, na, reinterpret_cast<cudaStream_t>(stream));
 }

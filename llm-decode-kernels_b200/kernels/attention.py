@@ -9,9 +9,11 @@ import torch
 from kernels import _lib
 
 
-def decode_attention(qkv, k_cache, v_cache, pos, cos, sin, n_heads, n_kv, splits=0):
+def decode_attention(qkv, k_cache, v_cache, pos, cos, sin, n_heads, n_kv, splits=0, static_cache=False):
     """qkv [B, 1, (nq + 2 nkv) * hd] fp16; k_cache, v_cache [B, nkv, max_len, hd] fp16 (updated
-    in place at `pos`); pos int64 [1] (device); cos, sin [1, hd] fp16. Returns [B, 1, nq * hd]."""
+    in place at `pos`); pos int64 [1] (device); cos, sin [1, hd] fp16. Returns [B, 1, nq * hd].
+    static_cache: the cache and `pos` were not written by the kernel just before this one (true
+    inside a decode step), so the kernel fetches its cache slice before waiting for that kernel."""
     B, T, width = qkv.shape
     hd = k_cache.shape[-1]
     max_len = k_cache.shape[-2]
@@ -24,5 +26,5 @@ def decode_attention(qkv, k_cache, v_cache, pos, cos, sin, n_heads, n_kv, splits
     out = torch.empty((B, 1, n_heads * hd), dtype=qkv.dtype, device=qkv.device)
     _lib.call("dk_decode_attention", _lib.ptr(qkv), _lib.ptr(k_cache), _lib.ptr(v_cache), _lib.ptr(pos),
               _lib.ptr(cos.contiguous()), _lib.ptr(sin.contiguous()), _lib.ptr(out), B, n_heads, n_kv, hd,
-              max_len, splits, _lib.stream_of(qkv))
+              max_len, splits, 1 if static_cache else 0, _lib.stream_of(qkv))
     return out

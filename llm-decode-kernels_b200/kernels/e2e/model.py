@@ -58,6 +58,17 @@ class Backend:
     def gate_up_act(self, x, p: Linear):
         return self.act(self.linear(x, p))
 
+    def norm_linear(self, x, w, eps, residual, p: Linear):
+        """(linear(norm(x [+ residual])), new residual or None) - fused by kernel backends."""
+        if residual is None:
+            return self.linear(self.norm(x, w, eps), p), None
+        h, residual = self.norm(x, w, eps, residual=residual)
+        return self.linear(h, p), residual
+
+    def norm_gate_up_act(self, x, w, eps, residual, p: Linear):
+        h, residual = self.norm(x, w, eps, residual=residual)
+        return self.gate_up_act(h, p), residual
+
 
 class W4RefBackend(Backend):
     """RTN 4-bit weights dequantized once to fp16, then cuBLAS (reference model.py:55-67): the
@@ -115,6 +126,18 @@ class OursBackend(Backend):
 
         return w4a16_swiglu(x, p.qweight, p.scales, p.zeros, bias=p.bias, config=self.LINEAR_CFG)
 
+    def norm_linear(self, x, w, eps, residual, p: Linear):
+        from kernels.w4a16 import w4a16_rmsnorm_matmul
+
+        return w4a16_rmsnorm_matmul(x, w, eps, residual, p.qweight, p.scales, p.zeros, bias=p.bias,
+                                    config=self.LINEAR_CFG)
+
+    def norm_gate_up_act(self, x, w, eps, residual, p: Linear):
+        from kernels.w4a16 import w4a16_rmsnorm_matmul
+
+        return w4a16_rmsnorm_matmul(x, w, eps, residual, p.qweight, p.scales, p.zeros, bias=p.bias, swiglu=True,
+                                    config=self.LINEAR_CFG)
+
 
 class OursFP8Backend(OursBackend):
     """FP8 (e4m3) weight-only linears with the same fused norm/activation kernels
@@ -139,6 +162,12 @@ class OursFP8Backend(OursBackend):
 
     def gate_up_act(self, x, p: Linear):
         return self.act(self.linear(x, p))
+
+    def norm_linear(self, x, w, eps, residual, p: Linear):
+        return Backend.norm_linear(self, x, w, eps, residual, p)
+
+    def norm_gate_up_act(self, x, w, eps, residual, p: Linear):
+        return Backend.norm_gate_up_act(self, x, w, eps, residual, p)
 
 
 def make_backend(name: str) -> Backend:
@@ -273,18 +302,26 @@ class QwenRunner:
 
         residual, h = x, None
         for i, L in enumerate(self.layers):
+            if decode:
+                # one kernel each: norm + qkv, attention, o, norm + gate_up + SwiGLU, down
+                from kernels.attention import decode_attention
+
+                if h is None:
+                    qkv, _ = be.norm_linear(x, L.ln1, eps, None, L.qkv)
+                else:  # residual += previous MLP output, input norm of this layer, qkv
+                    qkv, residual = be.norm_linear(h, L.ln1, eps, residual, L.qkv)
+                attn = decode_attention(qkv, self.k_cache[i], self.v_cache[i], pos, cos, sin,
+                                        self.n_heads, self.n_kv, static_cache=True)
+                o = be.linear(attn, L.o)
+                act, residual = be.norm_gate_up_act(o, L.ln2, eps, residual, L.gate_up)
+                h = be.linear(act, L.down)
+                continue
             if h is None:
                 h = be.norm(x, L.ln1, eps)
             else:  # fused: residual += previous MLP output, then input norm of this layer
                 h, residual = be.norm(h, L.ln1, eps, residual=residual)
             qkv = be.linear(h, L.qkv)
-            if decode:
-                from kernels.attention import decode_attention
-
-                attn = decode_attention(qkv, self.k_cache[i], self.v_cache[i], pos, cos, sin,
-                                        self.n_heads, self.n_kv)
-            else:
-                attn = self._attention_sdpa(i, qkv, pos, cos, sin, mask, B, T)
+            attn = self._attention_sdpa(i, qkv, pos, cos, sin, mask, B, T)
             o = be.linear(attn, L.o)
             h, residual = be.norm(o, L.ln2, eps, residual=residual)
             h = be.linear(be.gate_up_act(h, L.gate_up), L.down)

@@ -100,6 +100,52 @@ def w4a16_swiglu(x, qweight, scales, zeros, group_size=128, bias=None, config=No
     return out.view(*x.shape[:-1], I)
 
 
+def w4a16_rmsnorm_matmul(x, norm_weight, eps, residual, qweight, scales, zeros, group_size=128, bias=None,
+                         swiglu=False, config=None):
+    """Residual add + RMSNorm fused into the projection that consumes it.
+
+    h = x + residual (fp16 add; h = x when residual is None); xn = rmsnorm(h, norm_weight, eps)
+    (same roundings as kernels.rmsnorm.rmsnorm); returns (y, h_or_None) with y = xn @ dequant(W).T
+    (+ bias), or silu(g) * u of that product when `swiglu` (W holds [gate; up]). One kernel on the
+    fast path; shapes it does not cover run rmsnorm and the projection separately."""
+    K = x.shape[-1]
+    N = qweight.shape[1]
+    assert qweight.shape[0] * 8 == K and K % group_size == 0
+    _lib.require_cuda("w4a16_rmsnorm_matmul", x, residual, norm_weight, qweight, scales, zeros, bias)
+    _lib.require_dtype("w4a16_rmsnorm_matmul", torch.float16, x, residual, norm_weight, scales, zeros, bias)
+    x2 = x.reshape(-1, K)
+    if x2.stride(1) != 1:
+        x2 = x2.contiguous()
+    r2 = None if residual is None else residual.reshape(-1, K)
+    if r2 is not None and r2.stride(1) != 1:
+        r2 = r2.contiguous()
+    M = x2.shape[0]
+    cfg = _config(config)
+    I = N // 2
+    tensors = [x2, qweight, scales, zeros, norm_weight] + ([r2] if r2 is not None else [])
+    fast = (group_size == 128 and N % 8 == 0 and (not swiglu or I % 32 == 0) and not cfg.flags & _lib.FLAG_GENERIC
+            and all(t.data_ptr() % 16 == 0 for t in tensors) and x2.stride(0) % 8 == 0
+            and (r2 is None or r2.stride(0) % 8 == 0) and norm_weight.is_contiguous())
+    if not fast:
+        from kernels.rmsnorm import rmsnorm
+
+        normed = rmsnorm(x, norm_weight, eps, residual)
+        h, res = (normed, None) if residual is None else normed
+        fn = w4a16_swiglu if swiglu else w4a16_matmul
+        return fn(h, qweight, scales, zeros, group_size, bias, config), res
+    qweight, scales, zeros = qweight.contiguous(), scales.contiguous(), zeros.contiguous()
+    if bias is not None:
+        bias = bias.contiguous()
+    out = torch.empty((M, I if swiglu else N), dtype=x.dtype, device=x.device)
+    res_out = None if r2 is None else torch.empty((M, K), dtype=x.dtype, device=x.device)
+    _lib.call("dk_w4a16_rmsnorm_matmul", _lib.ptr(x2), x2.stride(0), _lib.ptr(r2), 0 if r2 is None else r2.stride(0),
+              _lib.ptr(norm_weight), float(eps), _lib.ptr(res_out), 0 if res_out is None else res_out.stride(0),
+              _lib.ptr(qweight), _lib.ptr(scales), _lib.ptr(zeros), _lib.ptr(bias), _lib.ptr(out), out.stride(0),
+              M, N, K, group_size, 1 if swiglu else 0, ctypes.byref(cfg), _lib.stream_of(x))
+    y = out.view(*x.shape[:-1], out.shape[-1])
+    return y, None if res_out is None else res_out.view(x.shape)
+
+
 def export_choices() -> dict:
     """Per-shape configs used so far (reference kernels/w4a16.py:333-335)."""
     return {",".join(map(str, k)): v for k, v in _choices.items()}

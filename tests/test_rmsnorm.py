@@ -86,3 +86,32 @@ def test_rmsnorm_strided_rows():
     o_ref, r_ref = ref.rmsnorm_ref(x, w, 1e-6, residual=r)
     assert np.array_equal(bits16(res), bits16(r_ref))
     assert _ulps(out, o_ref).max() <= 2
+
+
+@pytest.mark.parametrize("M,N,K,swiglu,with_res", [(1, 2048, 1536, False, True), (1, 2048, 1536, False, False),
+                                                   (4, 17920, 1536, True, True), (16, 1536, 8960, False, True),
+                                                   (3, 512, 1024, True, False)])
+def test_rmsnorm_fused_into_matmul(M, N, K, swiglu, with_res):
+    """w4a16_rmsnorm_matmul == the two-kernel path rmsnorm -> w4a16_matmul / w4a16_swiglu: the new
+    residual bit-exactly, the projection within the matmul tolerance of the oracle computed on the
+    oracle's normalized activations."""
+    from kernels.w4a16 import w4a16_rmsnorm_matmul
+    from _util import MATMUL_TOL, w4_case, w4_ref
+
+    x, r, w = _inputs(M, K, seed=7)
+    _, qw, s, z, b = w4_case(M, N, K, bias=not swiglu)
+    xc, rc, wc, qc, sc, zc, bc = to_cuda(x, r, w, qw, s, z, b)
+    y, res = w4a16_rmsnorm_matmul(xc, wc, 1e-6, rc if with_res else None, qc, sc, zc, bias=bc, swiglu=swiglu)
+    if with_res:
+        xn, r_ref = ref.rmsnorm_ref(x, w, 1e-6, residual=r)
+        assert np.array_equal(bits16(res), bits16(r_ref))
+    else:
+        xn = ref.rmsnorm_ref(x, w, 1e-6)
+        assert res is None
+    yr = w4_ref(xn, qw, s, z, b)
+    if swiglu:
+        yr16 = yr.astype(np.float16)
+        yr = ref.swiglu_ref(yr16[:, : N // 2], yr16[:, N // 2:]).astype(np.float32)
+        np.testing.assert_allclose(y.float().cpu().numpy(), yr, rtol=2e-2, atol=4e-3)
+    else:
+        np.testing.assert_allclose(y.float().cpu().numpy(), yr, **MATMUL_TOL)
