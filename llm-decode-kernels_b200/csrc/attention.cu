@@ -275,7 +275,8 @@ extern "C" int dk_decode_attention(const void* qkv, void* k_cache, void* v_cache
   case GG: {                                                                                             \
     auto k = head_dim == 128 ? decode_attention_kernel<GG, 128>                                          \
              : head_dim == 64 ? decode_attention_kernel<GG, 64> : decode_attention_kernel<GG, 32>;       \
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);                    \
+    if (opt_in_dynamic_smem(k) < static_cast<int>(smem))                                                   \
+      return set_error(DK_ERR_UNSUPPORTED, "decode_attention: %zu bytes of shared memory do not fit", smem); \
     e = launch(k, grid, dim3(kThreads), smem, st, pdl_enabled(), dim3(1, 1, S), p);                       \
     break;                                                                                               \
   }

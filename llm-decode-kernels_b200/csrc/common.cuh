@@ -262,4 +262,21 @@ bool make_tensor_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType 
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Opt a kernel in to the largest dynamic shared memory the device allows next to its static shared
+// memory. Returns the dynamic limit in bytes (0 if the attribute could not be set).
+template <typename F>
+int opt_in_dynamic_smem(F* kernel) {
+  cudaFuncAttributes a;
+  if (cudaFuncGetAttributes(&a, kernel) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  const int limit = device_info().max_smem_optin - static_cast<int>(a.sharedSizeBytes);
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, limit) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return limit;
+}
+
 }  // namespace dk

@@ -560,8 +560,7 @@ void set_smem_attrs() {
     for (int nt = 1; nt <= 2; ++nt)
       for (int cw = 1; cw <= 8; cw *= 2)
         for (int ex = 0; ex < 2; ++ex)
-          cudaFuncSetAttribute(variant(nt, cw, ex), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               device_info().max_smem_optin);
+          opt_in_dynamic_smem(variant(nt, cw, ex));
     done[dev] = true;
   }
 }

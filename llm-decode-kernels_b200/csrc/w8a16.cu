@@ -303,7 +303,7 @@ void set_attrs8() {
   if (dev < 64 && !done[dev]) {
     for (int nt = 1; nt <= 2; ++nt)
       for (int cw = 1; cw <= 8; cw *= 2)
-        cudaFuncSetAttribute(variant8(nt, cw), cudaFuncAttributeMaxDynamicSharedMemorySize, device_info().max_smem_optin);
+        opt_in_dynamic_smem(variant8(nt, cw));
     done[dev] = true;
   }
 }
