@@ -69,12 +69,14 @@ __device__ __forceinline__ void load_lane(const __half* row, int lane, float (&v
 }
 
 template <int G, int kHd>
-__global__ void __launch_bounds__(kThreads) decode_attention_kernel(const AttnParams p) {
-  constexpr int E = kHd / 32;  // head-dim elements per lane in the score loop
-  __shared__ float qs[G][kHd];          // rotated q (fp32, pre-scaled)
+__global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const AttnParams p) {
+  static_assert(G <= 8, "query heads per kv head");
+  __shared__ __align__(16) __half qs[8][kHd];  // rotated q, fp16 (rows G..7 zero: MMA padding)
   __shared__ __half knew[kHd], vnew[kHd];
-  __shared__ float part_o[G][kHd];      // this CTA's unnormalized output
+  __shared__ float part_o[G][kHd];  // this CTA's unnormalized output
   __shared__ float part_m[G], part_l[G];
+  __shared__ float wq[G][kMaxSplit];  // combine weights exp(m_q - M) of every rank
+  __shared__ float inv_den[G];
   __shared__ __align__(8) uint64_t bar;
   extern __shared__ __align__(128) uint8_t dsm[];  // Ks[slice][hd] | Vs[slice][hd] | scores[G][slice]
 
@@ -120,15 +122,15 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(const AttnPa
   const __half* krow = qrow + p.nq * kHd + h * kHd;
   const __half* vrow = qrow + (p.nq + p.nkv) * kHd + h * kHd;
   for (int d = tid; d < kHd; d += kThreads) {
-    for (int g = 0; g < G; ++g)
-      qs[g][d] = __half2float(rope_elem<kHd>(qrow + (h * G + g) * kHd, d, p.cos, p.sin)) * p.scale;
+#pragma unroll
+    for (int g = 0; g < 8; ++g)
+      qs[g][d] = g < G ? rope_elem<kHd>(qrow + (h * G + g) * kHd, d, p.cos, p.sin) : __float2half(0.f);
     knew[d] = rope_elem<kHd>(krow, d, p.cos, p.sin);
     vnew[d] = vrow[d];
   }
   __syncthreads();
-  // The new token's k, v come from registers/shared memory; the owner of `pos` appends them to the
-  // cache (the bulk copy may have read the stale row at `pos`: that row is never used below).
-  if (pos >= j0 && pos < j1) {
+  const bool owner = pos >= j0 && pos < j1;
+  if (owner) {  // append the new token to the cache
     for (int d = tid; d < kHd; d += kThreads) {
       kc[static_cast<int64_t>(pos) * kHd + d] = knew[d];
       vc[static_cast<int64_t>(pos) * kHd + d] = vnew[d];
@@ -143,22 +145,36 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(const AttnPa
     }
     return;
   }
+  if (owner) {  // the slice copy holds the stale row at `pos`: replace it with the new k, v
+    for (int d = tid; d < kHd; d += kThreads) {
+      Ks[static_cast<size_t>(pos - j0) * kHd + d] = knew[d];
+      Vs[static_cast<size_t>(pos - j0) * kHd + d] = vnew[d];
+    }
+  }
+  __syncthreads();
 
-  // scores: warp w takes positions j0+w, j0+w+4, ...; lanes split the head dim (E each)
-  for (int jj = warp; jj < n; jj += kThreads / 32) {
-    const int j = j0 + jj;
-    float kv[E];
-    const __half* ksrc = (j == pos) ? knew : Ks + static_cast<size_t>(jj) * kHd;
+  // scores[g][j] = (q_g . k_j) * scale on tensor cores: A = q (8 heads padded to 16 rows) x 16 dims,
+  // B = K^T (16 dims x 8 positions), fp32 accumulation; warp w takes position tiles w, w+4, ...
+  {
+    const int g = lane >> 2, t = lane & 3;
+    const int ntiles = (n + 7) / 8;
+    for (int nt = warp; nt < ntiles; nt += kThreads / 32) {
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      const int prow = min(nt * 8 + g, max(n - 1, 0));  // clamp: padded columns read a valid row
+      const __half* krow_s = Ks + static_cast<size_t>(prow) * kHd;
 #pragma unroll
-    for (int e = 0; e < E; ++e) kv[e] = __half2float(ksrc[lane * E + e]);
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float s = 0.f;
-#pragma unroll
-      for (int e = 0; e < E; ++e) s = fmaf(qs[g][lane * E + e], kv[e], s);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if (lane == 0) scores[g * p.slice_max + jj] = s;
+      for (int k0 = 0; k0 < kHd; k0 += 16) {
+        const uint32_t a0 = *reinterpret_cast<const uint32_t*>(&qs[g][k0 + 2 * t]);
+        const uint32_t a2 = *reinterpret_cast<const uint32_t*>(&qs[g][k0 + 2 * t + 8]);
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(krow_s + k0 + 2 * t);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(krow_s + k0 + 2 * t + 8);
+        mma_16816(acc, a0, 0u, a2, 0u, b0, b1);
+      }
+      if (g < G) {
+        const int jj = nt * 8 + 2 * t;
+        if (jj < n) scores[g * p.slice_max + jj] = acc[0] * p.scale;
+        if (jj + 1 < n) scores[g * p.slice_max + jj + 1] = acc[1] * p.scale;
+      }
     }
   }
   __syncthreads();
@@ -188,7 +204,7 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(const AttnPa
 #pragma unroll
     for (int g = 0; g < G; ++g) acc[g] = 0.f;
     for (int jj = 0; jj < n; ++jj) {
-      const float v = (j0 + jj == pos) ? __half2float(vnew[d]) : __half2float(Vs[static_cast<size_t>(jj) * kHd + d]);
+      const float v = __half2float(Vs[static_cast<size_t>(jj) * kHd + d]);
 #pragma unroll
       for (int g = 0; g < G; ++g) acc[g] = fmaf(scores[g * p.slice_max + jj], v, acc[g]);
     }
@@ -204,25 +220,34 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(const AttnPa
     }
     return;
   }
-  // combine the S partials of the cluster: rank r writes dims d with d % S == r
+  // combine the S partials of the cluster: per head the weights exp(m_q - M) of every rank, then
+  // rank r writes the dims d with d % S == r
   cluster_sync();
+  if (tid < G) {
+    const int g = tid;
+    float mq[kMaxSplit], lq[kMaxSplit];
+    float M = -FLT_MAX;
+    for (int q = 0; q < S; ++q) {
+      mq[q] = ld_shared_cluster_f32(map_shared_rank(&part_m[g], q));
+      lq[q] = ld_shared_cluster_f32(map_shared_rank(&part_l[g], q));
+      if (lq[q] > 0.f) M = fmaxf(M, mq[q]);
+    }
+    float den = 0.f;
+    for (int q = 0; q < S; ++q) {
+      const float w = lq[q] > 0.f ? __expf(mq[q] - M) : 0.f;
+      wq[g][q] = w;
+      den = fmaf(w, lq[q], den);
+    }
+    inv_den[g] = 1.0f / den;
+  }
+  __syncthreads();
   for (int e = tid; e < G * kHd; e += kThreads) {
     const int g = e / kHd, d = e % kHd;
     if (d % S != rank) continue;
-    float M = -FLT_MAX;
-    for (int q = 0; q < S; ++q) {
-      const float l = ld_shared_cluster_f32(map_shared_rank(&part_l[g], q));
-      if (l > 0.f) M = fmaxf(M, ld_shared_cluster_f32(map_shared_rank(&part_m[g], q)));
-    }
-    float num = 0.f, den = 0.f;
-    for (int q = 0; q < S; ++q) {
-      const float l = ld_shared_cluster_f32(map_shared_rank(&part_l[g], q));
-      if (l <= 0.f) continue;
-      const float w = __expf(ld_shared_cluster_f32(map_shared_rank(&part_m[g], q)) - M);
-      num = fmaf(w, ld_shared_cluster_f32(map_shared_rank(&part_o[g][d], q)), num);
-      den = fmaf(w, l, den);
-    }
-    p.out[static_cast<int64_t>(b) * p.nq * kHd + (h * G + g) * kHd + d] = __float2half_rn(num / den);
+    float num = 0.f;
+    for (int q = 0; q < S; ++q)
+      if (wq[g][q] != 0.f) num = fmaf(wq[g][q], ld_shared_cluster_f32(map_shared_rank(&part_o[g][d], q)), num);
+    p.out[static_cast<int64_t>(b) * p.nq * kHd + (h * G + g) * kHd + d] = __float2half_rn(num * inv_den[g]);
   }
   cluster_sync();  // keep partials alive until every rank has read them
 }
