@@ -152,7 +152,7 @@ int dk_swiglu(const void* gate, int64_t ldg, const void* up, int64_t ldu, void* 
  * fused projection output; caches [B, nkv, max_len, head_dim]; cos, sin [head_dim] for this
  * position; out [B, nq * head_dim]. `pos` is a device pointer (graph-capturable); a position outside
  * [0, max_len) writes nothing and sets DK_DEVERR_BAD_POSITION. splits: positions are cut into this
- * many slices combined inside a thread-block cluster (0 = automatic, max 8). head_dim 32, 64 or 128. */
+ * many slices combined inside a thread-block cluster (0 = automatic, max 16). head_dim 32, 64 or 128. */
 #define DK_ATTN_STATIC_CACHE 1 /* flags: the cache rows before *pos and *pos itself were not written
                                   by the kernel immediately before this one (true inside a decode
                                   step): the cache slice is fetched before waiting for that kernel */

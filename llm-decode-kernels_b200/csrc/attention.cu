@@ -25,7 +25,7 @@ namespace {
 
 constexpr int kThreads = 128;
 constexpr int kMaxGroup = 8;  // query heads per kv head
-constexpr int kMaxSplit = 8;
+constexpr int kMaxSplit = 16;  // cluster of up to 16 CTAs (non-portable size, allowed on B200)
 
 struct AttnParams {
   const __half* qkv;  // [B, (nq + 2 nkv) * hd]
@@ -36,7 +36,7 @@ struct AttnParams {
   const __half* sin;   // [hd]
   __half* out;         // [B, nq * hd]
   int nq, nkv, max_len;
-  int slice_max;     // positions per CTA at most (sizes the shared-memory slices)
+  int slice_max;     // positions per CTA at most, a multiple of 16 (sizes the shared-memory slices)
   int static_cache;  // see DK_ATTN_STATIC_CACHE
   float scale;
   int* err;
@@ -198,18 +198,47 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const Att
     }
   }
   __syncthreads();
-  // unnormalized output: thread d accumulates sum_j p[g][j] * v[j][d] for all heads of the group
-  for (int d = tid; d < kHd; d += kThreads) {
-    float acc[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) acc[g] = 0.f;
-    for (int jj = 0; jj < n; ++jj) {
-      const float v = __half2float(Vs[static_cast<size_t>(jj) * kHd + d]);
-#pragma unroll
-      for (int g = 0; g < G; ++g) acc[g] = fmaf(scores[g * p.slice_max + jj], v, acc[g]);
+  // unnormalized output O = P V on tensor cores: A = P (fp16, heads padded to 16 rows) x 16
+  // positions, B = V (16 positions x 8 dims, ldmatrix.trans from the row-major slice); rows of the
+  // last 16-position step beyond n are zero in both P and V.
+  {
+    const int kpad = (n + 15) / 16 * 16;
+    for (int i = n * kHd + tid * 8; i < kpad * kHd; i += kThreads * 8)
+      *reinterpret_cast<uint4*>(Vs + i) = make_uint4(0, 0, 0, 0);
+    __syncthreads();
+    const int g = lane >> 2, t = lane & 3;
+    constexpr int kTiles = kHd / 8;  // 8-dim output tiles, two per ldmatrix.x4
+    for (int tp = warp; tp < kTiles / 2; tp += kThreads / 32) {
+      const int nb = tp * 16;
+      float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int k0 = 0; k0 < kpad; k0 += 16) {
+        uint32_t a0 = 0, a2 = 0;
+        if (g < G) {
+          const float* sr = scores + g * p.slice_max;
+          const int j = k0 + 2 * t;
+          const float p0 = j < n ? sr[j] : 0.f, p1 = j + 1 < n ? sr[j + 1] : 0.f;
+          const float p8 = j + 8 < n ? sr[j + 8] : 0.f, p9 = j + 9 < n ? sr[j + 9] : 0.f;
+          a0 = half2_bits(__float2half_rn(p0), __float2half_rn(p1));
+          a2 = half2_bits(__float2half_rn(p8), __float2half_rn(p9));
+        }
+        // lane i addresses row (i % 8) of 8x8 tile (i / 8): tiles (k lo, d lo), (k hi, d lo),
+        // (k lo, d hi), (k hi, d hi)
+        const int tl = lane >> 3, r = lane & 7;
+        const __half* src = Vs + static_cast<size_t>(k0 + (tl & 1) * 8 + r) * kHd + nb + (tl >> 1) * 8;
+        uint32_t b0, b1, b2, b3;
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(b0), "=r"(b1), "=r"(b2), "=r"(b3)
+                     : "r"(smem_addr(src)));
+        mma_16816(acc0, a0, 0u, a2, 0u, b0, b1);
+        mma_16816(acc1, a0, 0u, a2, 0u, b2, b3);
+      }
+      if (g < G) {
+        part_o[g][nb + 2 * t] = acc0[0];
+        part_o[g][nb + 2 * t + 1] = acc0[1];
+        part_o[g][nb + 8 + 2 * t] = acc1[0];
+        part_o[g][nb + 8 + 2 * t + 1] = acc1[1];
+      }
     }
-#pragma unroll
-    for (int g = 0; g < G; ++g) part_o[g][d] = acc[g];
   }
 
   if (S == 1) {
@@ -270,7 +299,7 @@ extern "C" int dk_decode_attention(const void* qkv, void* k_cache, void* v_cache
   if (B > 65535 || nkv > 65535) return set_error(DK_ERR_INVALID, "decode_attention: grid too large");
   if (!qkv || !k_cache || !v_cache || !pos || !cos || !sin || !out)
     return set_error(DK_ERR_INVALID, "decode_attention: NULL pointer");
-  int S = splits > 0 ? splits : static_cast<int>(std::min<int64_t>(kMaxSplit, (max_len + 255) / 256));
+  int S = splits > 0 ? splits : static_cast<int>(std::min<int64_t>(kMaxSplit, (max_len + 127) / 128));
   S = std::max(1, std::min(S, kMaxSplit));
   AttnParams p;
   p.qkv = static_cast<const __half*>(qkv);
@@ -286,7 +315,8 @@ extern "C" int dk_decode_attention(const void* qkv, void* k_cache, void* v_cache
   p.scale = 1.0f / sqrtf(static_cast<float>(head_dim));
   p.err = device_info().err_word;
   const int G = static_cast<int>(nq / nkv);
-  const int slice_max = static_cast<int>((max_len + S - 1) / S);
+  // rows per CTA slice, rounded up to the 16-position MMA step (the P V loop reads whole steps)
+  const int slice_max = static_cast<int>(((max_len + S - 1) / S + 15) / 16 * 16);
   p.slice_max = slice_max;
   p.static_cache = (flags & DK_ATTN_STATIC_CACHE) ? 1 : 0;
   const size_t smem = 2 * static_cast<size_t>(slice_max) * head_dim * 2 + static_cast<size_t>(G) * slice_max * 4;
@@ -300,6 +330,7 @@ extern "C" int dk_decode_attention(const void* qkv, void* k_cache, void* v_cache
   case GG: {                                                                                             \
     auto k = head_dim == 128 ? decode_attention_kernel<GG, 128>                                          \
              : head_dim == 64 ? decode_attention_kernel<GG, 64> : decode_attention_kernel<GG, 32>;       \
+    cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);                             \
     if (opt_in_dynamic_smem(k) < static_cast<int>(smem))                                                   \
       return set_error(DK_ERR_UNSUPPORTED, "decode_attention: %zu bytes of shared memory do not fit", smem); \
     e = launch(k, grid, dim3(kThreads), smem, st, pdl_enabled(), dim3(1, 1, S), p);                       \
