@@ -75,8 +75,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const Att
   __shared__ __half knew[kHd], vnew[kHd];
   __shared__ float part_o[G][kHd];  // this CTA's unnormalized output
   __shared__ float part_m[G], part_l[G];
-  __shared__ float wq[G][kMaxSplit];  // combine weights exp(m_q - M) of every rank
-  __shared__ float inv_den[G];
+  // split-K combine, pushed by every rank of the cluster: softmax max / sum per head and the
+  // unnormalized output of the dims this rank owns
+  __shared__ float recv_ml[kMaxSplit][2][G];
+  __shared__ float recv_o[G * (kHd + kMaxSplit)];
   __shared__ __align__(8) uint64_t bar;
   extern __shared__ __align__(128) uint8_t dsm[];  // Ks[slice][hd] | Vs[slice][hd] | scores[G][slice]
 
@@ -139,10 +141,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const Att
   bool ok = true;
   if (n > 0) ok = mbar_wait(&bar, 0, p.err, DK_DEVERR_WAIT_FULL);
   if (__syncthreads_or(!ok)) {
-    if (S > 1) {
-      cluster_sync();
-      cluster_sync();
-    }
+    if (S > 1) cluster_sync();  // the one cluster barrier the other ranks pass as well
     return;
   }
   if (owner) {  // the slice copy holds the stale row at `pos`: replace it with the new k, v
@@ -249,36 +248,40 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const Att
     }
     return;
   }
-  // combine the S partials of the cluster: per head the weights exp(m_q - M) of every rank, then
-  // rank r writes the dims d with d % S == r
-  cluster_sync();
-  if (tid < G) {
-    const int g = tid;
-    float mq[kMaxSplit], lq[kMaxSplit];
-    float M = -FLT_MAX;
-    for (int q = 0; q < S; ++q) {
-      mq[q] = ld_shared_cluster_f32(map_shared_rank(&part_m[g], q));
-      lq[q] = ld_shared_cluster_f32(map_shared_rank(&part_l[g], q));
-      if (lq[q] > 0.f) M = fmaxf(M, mq[q]);
-    }
-    float den = 0.f;
-    for (int q = 0; q < S; ++q) {
-      const float w = lq[q] > 0.f ? __expf(mq[q] - M) : 0.f;
-      wq[g][q] = w;
-      den = fmaf(w, lq[q], den);
-    }
-    inv_den[g] = 1.0f / den;
-  }
+  // combine the S partials of the cluster: rank q owns dims [q*D, (q+1)*D); every rank pushes its
+  // (max, sum) per head and its partial output of rank q's dims into rank q's shared memory
+  // (remote stores, no round trips), one cluster barrier publishes them, and each rank combines
+  // its own dims from local shared memory.
   __syncthreads();
-  for (int e = tid; e < G * kHd; e += kThreads) {
-    const int g = e / kHd, d = e % kHd;
-    if (d % S != rank) continue;
-    float num = 0.f;
-    for (int q = 0; q < S; ++q)
-      if (wq[g][q] != 0.f) num = fmaf(wq[g][q], ld_shared_cluster_f32(map_shared_rank(&part_o[g][d], q)), num);
-    p.out[static_cast<int64_t>(b) * p.nq * kHd + (h * G + g) * kHd + d] = __float2half_rn(num * inv_den[g]);
+  const int D = (kHd + S - 1) / S;
+  for (int e = tid; e < S * G * D; e += kThreads) {
+    const int q = e / (G * D), g = (e / D) % G, dd = e % D;
+    const int d = q * D + dd;
+    if (d < kHd) st_shared_cluster_f32(map_shared_rank(&recv_o[(rank * G + g) * D + dd], q), part_o[g][d]);
   }
-  cluster_sync();  // keep partials alive until every rank has read them
+  for (int e = tid; e < S * G; e += kThreads) {
+    const int q = e / G, g = e % G;
+    st_shared_cluster_f32(map_shared_rank(&recv_ml[rank][0][g], q), part_m[g]);
+    st_shared_cluster_f32(map_shared_rank(&recv_ml[rank][1][g], q), part_l[g]);
+  }
+  cluster_sync();
+  for (int e = tid; e < G * D; e += kThreads) {
+    const int g = e / D, dd = e % D;
+    const int d = rank * D + dd;
+    if (d >= kHd) continue;
+    float M = -FLT_MAX;
+    for (int q = 0; q < S; ++q)
+      if (recv_ml[q][1][g] > 0.f) M = fmaxf(M, recv_ml[q][0][g]);
+    float num = 0.f, den = 0.f;
+    for (int q = 0; q < S; ++q) {
+      const float l = recv_ml[q][1][g];
+      if (l <= 0.f) continue;
+      const float w = __expf(recv_ml[q][0][g] - M);
+      num = fmaf(w, recv_o[(q * G + g) * D + dd], num);
+      den = fmaf(w, l, den);
+    }
+    p.out[static_cast<int64_t>(b) * p.nq * kHd + (h * G + g) * kHd + d] = __float2half_rn(num / den);
+  }
 }
 
 }  // namespace
