@@ -156,10 +156,13 @@ int dk_swiglu(const void* gate, int64_t ldg, const void* up, int64_t ldu, void* 
 #define DK_ATTN_STATIC_CACHE 1 /* flags: the cache rows before *pos and *pos itself were not written
                                   by the kernel immediately before this one (true inside a decode
                                   step): the cache slice is fetched before waiting for that kernel */
+/* rope_stride > 0: cos and sin are tables of at least max_len rows [positions, head_dim] (row stride
+ * rope_stride elements) and the kernel uses row *pos; rope_stride == 0: they already hold this
+ * position's [head_dim]. */
 int dk_decode_attention(const void* qkv, void* k_cache, void* v_cache, const int64_t* pos,
                         const void* cos, const void* sin, void* out, int64_t B, int64_t nq,
-                        int64_t nkv, int64_t head_dim, int64_t max_len, int32_t splits,
-                        int32_t flags, dk_stream_t stream);
+                        int64_t nkv, int64_t head_dim, int64_t max_len, int64_t rope_stride,
+                        int32_t splits, int32_t flags, dk_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -32,8 +32,9 @@ struct AttnParams {
   __half* k_cache;    // [B, nkv, max_len, hd]
   __half* v_cache;
   const int64_t* pos;  // [1]
-  const __half* cos;   // [hd]
-  const __half* sin;   // [hd]
+  const __half* cos;   // [hd], or a table [positions, hd] when rope_stride > 0
+  const __half* sin;
+  int64_t rope_stride;  // > 0: cos/sin rows are selected by *pos
   __half* out;         // [B, nq * hd]
   int nq, nkv, max_len;
   int slice_max;     // positions per CTA at most, a multiple of 16 (sizes the shared-memory slices)
@@ -119,6 +120,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const Att
   }
   if (p.static_cache) pdl_wait();  // qkv comes from the previous kernel
 
+  const __half* cosr = p.cos + (p.rope_stride > 0 ? pos64 * p.rope_stride : 0);
+  const __half* sinr = p.sin + (p.rope_stride > 0 ? pos64 * p.rope_stride : 0);
   const int row = (p.nq + 2 * p.nkv) * kHd;
   const __half* qrow = p.qkv + static_cast<int64_t>(b) * row;
   const __half* krow = qrow + p.nq * kHd + h * kHd;
@@ -126,8 +129,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(const Att
   for (int d = tid; d < kHd; d += kThreads) {
 #pragma unroll
     for (int g = 0; g < 8; ++g)
-      qs[g][d] = g < G ? rope_elem<kHd>(qrow + (h * G + g) * kHd, d, p.cos, p.sin) : __float2half(0.f);
-    knew[d] = rope_elem<kHd>(krow, d, p.cos, p.sin);
+      qs[g][d] = g < G ? rope_elem<kHd>(qrow + (h * G + g) * kHd, d, cosr, sinr) : __float2half(0.f);
+    knew[d] = rope_elem<kHd>(krow, d, cosr, sinr);
     vnew[d] = vrow[d];
   }
   __syncthreads();
@@ -291,8 +294,8 @@ using namespace dk;
 
 extern "C" int dk_decode_attention(const void* qkv, void* k_cache, void* v_cache, const int64_t* pos,
                                    const void* cos, const void* sin, void* out, int64_t B, int64_t nq,
-                                   int64_t nkv, int64_t head_dim, int64_t max_len, int32_t splits,
-                                   int32_t flags, dk_stream_t stream) {
+                                   int64_t nkv, int64_t head_dim, int64_t max_len, int64_t rope_stride,
+                                   int32_t splits, int32_t flags, dk_stream_t stream) {
   if (B <= 0 || nq <= 0 || nkv <= 0 || max_len <= 0) return set_error(DK_ERR_INVALID, "decode_attention: bad sizes");
   if (head_dim != 32 && head_dim != 64 && head_dim != 128)
     return set_error(DK_ERR_UNSUPPORTED, "decode_attention: head_dim %lld (32, 64 or 128)", (long long)head_dim);
@@ -311,6 +314,7 @@ extern "C" int dk_decode_attention(const void* qkv, void* k_cache, void* v_cache
   p.pos = pos;
   p.cos = static_cast<const __half*>(cos);
   p.sin = static_cast<const __half*>(sin);
+  p.rope_stride = rope_stride;
   p.out = static_cast<__half*>(out);
   p.nq = static_cast<int>(nq);
   p.nkv = static_cast<int>(nkv);

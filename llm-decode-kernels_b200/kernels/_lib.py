@@ -50,7 +50,7 @@ SIGNATURES = {
     "dk_w8a16_matmul": [P, I64, P, P, P, P, I64, I64, I64, I64, ctypes.POINTER(MatmulConfig), P],
     "dk_rmsnorm": [P, I64, P, I64, P, P, I64, P, I64, I64, I64, F32, P],
     "dk_swiglu": [P, I64, P, I64, P, I64, I64, I64, P],
-    "dk_decode_attention": [P, P, P, P, P, P, P, I64, I64, I64, I64, I64, I32, I32, P],
+    "dk_decode_attention": [P, P, P, P, P, P, P, I64, I64, I64, I64, I64, I64, I32, I32, P],
 }
 
 _lib = None

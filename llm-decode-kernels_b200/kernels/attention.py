@@ -11,7 +11,8 @@ from kernels import _lib
 
 def decode_attention(qkv, k_cache, v_cache, pos, cos, sin, n_heads, n_kv, splits=0, static_cache=False):
     """qkv [B, 1, (nq + 2 nkv) * hd] fp16; k_cache, v_cache [B, nkv, max_len, hd] fp16 (updated
-    in place at `pos`); pos int64 [1] (device); cos, sin [1, hd] fp16. Returns [B, 1, nq * hd].
+    in place at `pos`); pos int64 [1] (device); cos, sin [1, hd] fp16 for this position, or tables
+    [positions, hd] from which the kernel takes row `pos`. Returns [B, 1, nq * hd].
     static_cache: the cache and `pos` were not written by the kernel just before this one (true
     inside a decode step), so the kernel fetches its cache slice before waiting for that kernel."""
     B, T, width = qkv.shape
@@ -24,7 +25,12 @@ def decode_attention(qkv, k_cache, v_cache, pos, cos, sin, n_heads, n_kv, splits
     assert k_cache.is_contiguous() and v_cache.is_contiguous()
     qkv = qkv.contiguous()
     out = torch.empty((B, 1, n_heads * hd), dtype=qkv.dtype, device=qkv.device)
+    cos, sin = cos.contiguous(), sin.contiguous()
+    assert cos.shape == sin.shape and cos.shape[-1] == hd
+    if cos.shape[0] > 1 and cos.shape[0] < max_len:
+        raise RuntimeError("decode_attention: a RoPE table needs at least max_len rows")
+    stride = hd if cos.shape[0] > 1 else 0
     _lib.call("dk_decode_attention", _lib.ptr(qkv), _lib.ptr(k_cache), _lib.ptr(v_cache), _lib.ptr(pos),
-              _lib.ptr(cos.contiguous()), _lib.ptr(sin.contiguous()), _lib.ptr(out), B, n_heads, n_kv, hd,
-              max_len, splits, 1 if static_cache else 0, _lib.stream_of(qkv))
+              _lib.ptr(cos), _lib.ptr(sin), _lib.ptr(out), B, n_heads, n_kv, hd, max_len, stride, splits,
+              1 if static_cache else 0, _lib.stream_of(qkv))
     return out

@@ -246,6 +246,12 @@ class QwenRunner:
                 qkv=lin(a.q_proj, a.k_proj, a.v_proj), o=lin(a.o_proj),
                 gate_up=lin(mlp.gate_proj, mlp.up_proj), down=lin(mlp.down_proj),
             ))
+        # RoPE tables for the decode kernel, computed with the same ops as forward() does per step
+        if backend.fused_decode:
+            freqs = torch.arange(max_len, device=dev)[:, None].float() * self.inv_freq[None, :]
+            emb = torch.cat((freqs, freqs), dim=-1)
+            self.rope_cos = emb.cos().to(self.embed.dtype).contiguous()
+            self.rope_sin = emb.sin().to(self.embed.dtype).contiguous()
         shape = (len(self.layers), batch, self.n_kv, max_len, self.head_dim)
         self.k_cache = torch.zeros(shape, device=dev, dtype=self.embed.dtype)
         self.v_cache = torch.zeros(shape, device=dev, dtype=self.embed.dtype)
@@ -291,12 +297,14 @@ class QwenRunner:
         be, eps = self.backend, self.eps
         B, T = tokens.shape
         x = F.embedding(tokens, self.embed)
-        freqs = pos[:, None].float() * self.inv_freq[None, :]
-        emb = torch.cat((freqs, freqs), dim=-1)
-        cos, sin = emb.cos().to(x.dtype), emb.sin().to(x.dtype)
         decode = be.fused_decode and T == 1
         mask = None
-        if not decode:
+        if decode:  # the attention kernel reads row `pos` of the RoPE tables
+            cos, sin = self.rope_cos, self.rope_sin
+        else:
+            freqs = pos[:, None].float() * self.inv_freq[None, :]
+            emb = torch.cat((freqs, freqs), dim=-1)
+            cos, sin = emb.cos().to(x.dtype), emb.sin().to(x.dtype)
             keys = torch.arange(self.max_len, device=x.device)
             mask = keys[None, :] <= pos[:, None]  # [T, max_len], True = attend
 

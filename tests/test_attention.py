@@ -54,3 +54,23 @@ def test_bad_position_sets_device_error_and_writes_nothing():
     assert _lib.device_error() == 3  # DK_DEVERR_BAD_POSITION
     _lib.clear_device_error()
     assert np.array_equal(bits16(kc_t), bits16(kc))
+
+
+def test_rope_table_lookup_matches_per_position():
+    """cos/sin passed as [positions, hd] tables: the kernel takes row `pos` - same result as
+    passing that row."""
+    from kernels.attention import decode_attention
+
+    B, nq, nkv, max_len, pos = 1, 12, 2, 256, 100
+    qkv, kc, vc, cos, sin = _case(B, nq, nkv, max_len, pos)
+    tab_c = torch.zeros(max_len, 128, dtype=torch.float16)
+    tab_s = torch.zeros(max_len, 128, dtype=torch.float16)
+    tab_c[pos] = torch.from_numpy(cos)
+    tab_s[pos] = torch.from_numpy(sin)
+    args = (torch.from_numpy(qkv).cuda().view(B, 1, -1),)
+    p = torch.tensor([pos], device="cuda")
+    o1 = decode_attention(*args, torch.from_numpy(kc.copy()).cuda(), torch.from_numpy(vc.copy()).cuda(), p,
+                          torch.from_numpy(cos).cuda().view(1, -1), torch.from_numpy(sin).cuda().view(1, -1), nq, nkv)
+    o2 = decode_attention(*args, torch.from_numpy(kc.copy()).cuda(), torch.from_numpy(vc.copy()).cuda(), p,
+                          tab_c.cuda(), tab_s.cuda(), nq, nkv)
+    assert torch.equal(o1, o2)
