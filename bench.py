@@ -388,7 +388,10 @@ def run_ours(args, world, rank, local):
         if world == 1 and rank == 0:
             extras["cpu_baseline"] = cpu_decode_rate(model, steps=4)
     assert _lib.device_error() == 0, "a kernel recorded a device-side error"
-    per_step_launches = 7 * len(runner.layers) + 1 + (1 if runner.head_q is not None else 0)
+    # our kernels per token: per layer norm+qkv, attention, o_proj, norm+gate_up+SwiGLU, down (FP8:
+    # separate norm and SwiGLU kernels, 8 per layer), then the final norm and a quantized lm_head
+    per_layer = 8 if args.backend.startswith("ours_fp8") else 5
+    per_step_launches = per_layer * len(runner.layers) + 1 + (1 if runner.head_q is not None else 0)
     if rank != 0:
         return None
     return {"metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,

@@ -1,0 +1,129 @@
+"""Small, self-terminating workloads for profiler captures (ncu launch lists and single-kernel reports).
+
+    python llm-decode-kernels_b200/kernels/bench/profile_cases.py decode [ours|fp16] [steps]
+        Qwen2.5-1.5B (random init) batch-1 decode through the CUDA graph; the profiler range
+        (cudaProfilerStart/Stop) covers exactly `steps` graph replays at context 512.
+    python .../profile_cases.py gemv_layer
+        one decoder layer's four W4A16 launches at the Qwen2.5-1.5B shapes (M=1), as the runner
+        issues them (norm+qkv, o_proj, norm+gate_up+SwiGLU, down), 3 warm-up rounds + 1.
+    python .../profile_cases.py gemv N K [M]
+        five launches of one W4A16 GEMV of shape [M, K] x [K, N].
+    python .../profile_cases.py attention
+        28 decode-attention launches (one per layer, Qwen2.5-1.5B heads, position 767) eagerly,
+        then as a CUDA graph replayed 21 times.
+
+Every case allocates at most a few hundred MB and ends by itself.
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+
+sys.path.insert(0, os.path.abspath(os.path.join(os.path.dirname(__file__), "..", "..")))
+
+import torch  # noqa: E402
+
+from kernels import config  # noqa: E402
+from kernels.attention import decode_attention  # noqa: E402
+from kernels.quant import quantize_rtn  # noqa: E402
+from kernels.w4a16 import w4a16_matmul, w4a16_rmsnorm_matmul  # noqa: E402
+
+
+def _q(N, K):
+    return quantize_rtn((torch.randn(N, K, device="cuda") * 0.02).half(), config.GROUP_SIZE)
+
+
+def decode(backend="ours", steps="2"):
+    from kernels.e2e.model import QwenRunner, make_backend, random_qwen2
+    from kernels.e2e.run import GraphDecoder
+    steps = int(steps)
+    model = random_qwen2(config.QWEN15, dtype=torch.float16, device="cuda", seed=0)
+    ids = torch.randint(0, config.QWEN15["vocab_size"], (1, 512), device="cuda")
+    dec = GraphDecoder(QwenRunner(model, make_backend(backend), max_len=2048))
+    dec.capture(ids)
+    dec.prefill(ids)
+    for _ in range(5):
+        dec.graph.replay()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    for _ in range(steps):
+        dec.graph.replay()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    e0.record()
+    for _ in range(50):
+        dec.graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    print(f"{backend}: {e0.elapsed_time(e1) / 50:.4f} ms/step")
+
+
+def gemv_layer():
+    H, I, NQKV = 1536, 8960, 2048
+    qkv, o, gu, dn = _q(NQKV, H), _q(H, H), _q(2 * I, H), _q(H, I)
+    bias = (torch.randn(NQKV, device="cuda") * 0.1).half()
+    ln = torch.ones(H, device="cuda").half()
+    x, r, a = (torch.randn(1, H, device="cuda").half() for _ in range(3))
+    cfg = {"STATIC_WEIGHTS": True}
+
+    def layer():
+        w4a16_rmsnorm_matmul(x, ln, 1e-6, r, *qkv, bias=bias, config=cfg)
+        w4a16_matmul(a, *o, config=cfg)
+        act, _ = w4a16_rmsnorm_matmul(x, ln, 1e-6, r, *gu, swiglu=True, config=cfg)
+        w4a16_matmul(act, *dn, config=cfg)
+
+    for _ in range(4):
+        layer()
+    torch.cuda.synchronize()
+    print("gemv_layer ok")
+
+
+def gemv(N, K, M="1"):
+    N, K, M = int(N), int(K), int(M)
+    qw, s, z = _q(N, K)
+    x = torch.randn(M, K, device="cuda").half()
+    for _ in range(5):
+        y = w4a16_matmul(x, qw, s, z)
+    torch.cuda.synchronize()
+    print("gemv ok", y.float().abs().mean().item())
+
+
+def attention():
+    a = config.QWEN15
+    nq, nkv, hd = a["num_attention_heads"], a["num_key_value_heads"], a["head_dim"]
+    layers, max_len, pos = a["num_hidden_layers"], 2048, 767
+    qkv = torch.randn(1, 1, (nq + 2 * nkv) * hd, device="cuda").half()
+    kc = torch.randn(layers, 1, nkv, max_len, hd, device="cuda").half()
+    vc = torch.randn(layers, 1, nkv, max_len, hd, device="cuda").half()
+    p = torch.tensor([pos], device="cuda")
+    cos = torch.randn(1, hd, device="cuda").half()
+    sin = torch.randn(1, hd, device="cuda").half()
+
+    def run():
+        for i in range(layers):
+            decode_attention(qkv, kc[i], vc[i], p, cos, sin, nq, nkv, static_cache=True)
+
+    run()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        run()
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    e0.record()
+    for _ in range(20):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    print(f"attention: {e0.elapsed_time(e1) * 1e3 / (20 * layers):.2f} us/launch (position {pos})")
+
+
+CASES = {"decode": decode, "gemv_layer": gemv_layer, "gemv": gemv, "attention": attention}
+
+if __name__ == "__main__":
+    if len(sys.argv) < 2 or sys.argv[1] not in CASES:
+        sys.exit(f"usage: profile_cases.py {{{'|'.join(CASES)}}} [args]")
+    CASES[sys.argv[1]](*sys.argv[2:])
