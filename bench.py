@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--backend", default="ours", help="runner backend of our arm (ours, ours_lm, ours_fp8)")
     ap.add_argument("--no-extras", action="store_true", help="skip fp16 baseline, GEMV sweep and CPU baseline")
+    ap.add_argument("--l2-prefetch", action="store_true",
+                    help="runner with cross-launch L2 prefetch of the next projections' weights")
     return ap.parse_args()
 
 
@@ -176,9 +178,10 @@ def time_decode(dec, ids, steps: int, warmup: int, world: int) -> float:
 
 
 def gemv_roofline(runner, peak_gbs: float) -> dict:
-    """The dominant kernel (W4A16 GEMV): one decode step's linears (per layer qkv, o, gate_up with
-    fused SwiGLU, down; M = 1) captured back to back in one CUDA graph on the current stream and
-    timed with CUDA events; achieved = algorithmic bytes of those launches / their time."""
+    """The dominant kernel (W4A16 GEMV): one decode step's linears, issued exactly as the decode step
+    issues them (per layer norm+qkv, o, norm+gate_up+SwiGLU, down; M = 1; the runner's L2 prefetch
+    plan), captured back to back in one CUDA graph on the current stream and timed with CUDA events;
+    achieved = algorithmic bytes of those launches / their time."""
     from kernels.bench.harness import capture
     from kernels.quant import weight_bytes
 
@@ -189,11 +192,13 @@ def gemv_roofline(runner, peak_gbs: float) -> dict:
     a = torch.randn(1, 1, nq * hd, device="cuda", dtype=torch.float16)
     I = runner.layers[0].down.qweight.shape[0] * 8
 
+    r = torch.randn(1, 1, H, device="cuda", dtype=torch.float16)
+
     def chain():
         for L in runner.layers:
-            be.linear(x, L.qkv)
+            be.norm_linear(x, L.ln1, runner.eps, r, L.qkv)
             be.linear(a, L.o)
-            act = be.gate_up_act(x, L.gate_up)
+            act, _ = be.norm_gate_up_act(x, L.ln2, runner.eps, r, L.gate_up)
             be.linear(act, L.down)
 
     chain()
@@ -221,7 +226,7 @@ def gemv_roofline(runner, peak_gbs: float) -> dict:
     achieved = byts / launches / (sec / launches) / 1e9
     return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
             "frac": round(achieved / peak_gbs, 4), "traffic": traffic_per_launch(),
-            "kernel": "w4a16_gemv_kernel (28 x {qkv, o_proj, gate_up+SwiGLU, down}, M=1)",
+            "kernel": "w4a16_gemv_kernel (28 x {norm+qkv, o_proj, norm+gate_up+SwiGLU, down}, M=1)",
             "bytes_per_launch": round(byts / launches), "us_per_launch": round(sec / launches * 1e6, 3)}
 
 
@@ -333,7 +338,7 @@ def workload_config(args, world) -> dict:
     return {"workload": "BASELINE configs[3]: Qwen2.5-1.5B-architecture decode (28 layers, hidden 1536, 12/2 heads, "
                         "MLP 8960, vocab 151936, tied fp16 lm_head), random-init weights, W4A16 g128 linears, "
                         f"uniform random {PROMPT}-token prompt, greedy decode under CUDA graphs",
-            "backend": args.backend, "global_batch": args.batch * world, "seq_len": PROMPT, "max_len": MAX_LEN,
+            "backend": args.backend, "l2_prefetch": args.l2_prefetch, "global_batch": args.batch * world, "seq_len": PROMPT, "max_len": MAX_LEN,
             "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
             "l2": "inputs larger than L2: each step reads ~1.2 GB of weights"}
 
@@ -347,7 +352,8 @@ def run_ours(args, world, rank, local):
     model = build_model(args.batch)
     ids = prompt_ids(model.config.vocab_size, args.batch)
     assert PROMPT + args.warmup + args.steps + 8 < MAX_LEN, "steps + warmup exceed the cache"
-    runner = QwenRunner(model, make_backend(args.backend), max_len=MAX_LEN, batch=args.batch)
+    runner = QwenRunner(model, make_backend(args.backend), max_len=MAX_LEN, batch=args.batch,
+                        l2_prefetch=args.l2_prefetch)
     dec = GraphDecoder(runner)
     dec.capture(ids)
     with ClockSampler(local) as clocks:

@@ -25,7 +25,7 @@ extern "C" {
 
 typedef struct CUstream_st* dk_stream_t; /* same type as cudaStream_t */
 
-#define DK_ABI_VERSION 1
+#define DK_ABI_VERSION 2
 
 /* status codes */
 #define DK_OK 0
@@ -50,16 +50,27 @@ typedef struct CUstream_st* dk_stream_t; /* same type as cudaStream_t */
                                     of the default factored form s * sum(x * (q - z)) in fp32 (the
                                     reference's FACTORED path, kernels/w4a16.py:116-119) */
 
-/* Optional per-call tuning; zero fields mean "choose automatically". */
+#define DK_MAX_L2_PREFETCH 6
+
+/* Optional per-call tuning; zero fields mean "choose automatically".
+ * l2_prefetch: byte ranges of device memory (typically the weights of the launch after next) that
+ * the launch asks the L2 cache to fetch while it runs (cp.async.bulk.prefetch.L2), so that the later
+ * launch reads them from L2 instead of HBM. A hint only: it changes no result, and ranges are
+ * trimmed inward to 16-byte boundaries. No reference counterpart (the reference's Triton launches
+ * have no cross-launch prefetch). */
 typedef struct dk_matmul_config {
-  int32_t split_k; /* K slices reduced inside a thread-block cluster (1..8; clamped to what K allows) */
-  int32_t block_n; /* output columns per CTA tile: 32, 64, 128 or 256 (other values: automatic) */
-  int32_t flags;   /* DK_FLAG_* */
-  int32_t reserved;
+  int32_t split_k;    /* K slices reduced inside a thread-block cluster (1..8; clamped to what K allows) */
+  int32_t block_n;    /* output columns per CTA tile: 32, 64, 128 or 256 (other values: automatic) */
+  int32_t flags;      /* DK_FLAG_* */
+  int32_t n_prefetch; /* valid entries of l2_prefetch_ptr / l2_prefetch_bytes (0..DK_MAX_L2_PREFETCH) */
+  const void* l2_prefetch_ptr[DK_MAX_L2_PREFETCH];
+  uint64_t l2_prefetch_bytes[DK_MAX_L2_PREFETCH];
 } dk_matmul_config;
 
 /* ---- library ---------------------------------------------------------------------------- */
 int dk_abi_version(void);
+/* sizeof(dk_matmul_config) in this build, for FFI bindings that lay the struct out themselves. */
+int dk_matmul_config_size(void);
 /* Message of the last failing call on this host thread ("" if none). */
 const char* dk_last_error(void);
 /* Device error word of the current device (DK_DEVERR_*); reading it synchronizes the device.

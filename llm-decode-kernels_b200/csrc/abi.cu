@@ -103,6 +103,7 @@ const DeviceInfo& device_info() {
 extern "C" {
 
 int dk_abi_version(void) { return DK_ABI_VERSION; }
+int dk_matmul_config_size(void) { return static_cast<int>(sizeof(dk_matmul_config)); }
 
 const char* dk_last_error(void) { return dk::t_last_error; }
 

@@ -130,6 +130,50 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// ------------------------------------------------------------- L2 prefetch of later launches' data
+// Byte ranges (16-byte aligned start and size) that a launch asks L2 to fetch for a later launch.
+struct L2Prefetch {
+  const char* ptr[DK_MAX_L2_PREFETCH];
+  uint64_t bytes[DK_MAX_L2_PREFETCH];
+  int n;
+};
+
+// The ranges are cut into 32 KB pieces dealt round-robin to the threads (cta, lane) of one warp per
+// CTA, consecutive pieces on different CTAs (so on different SMs). Fire and forget: nothing waits
+// for the fetch, and L2 is the point of coherence, so a prefetch can never expose stale data.
+__device__ __forceinline__ void l2_prefetch_share(const L2Prefetch& pf, int cta, int nctas, int lane) {
+  constexpr uint64_t kPiece = 32768;
+  const uint64_t stride = static_cast<uint64_t>(nctas) * 32;
+  const uint64_t me = static_cast<uint64_t>(lane) * nctas + cta;
+  uint64_t base = 0;  // global index of this range's first piece
+  for (int r = 0; r < pf.n; ++r) {
+    const uint64_t pieces = (pf.bytes[r] + kPiece - 1) / kPiece;
+    for (uint64_t j = (me + stride - base % stride) % stride; j < pieces; j += stride) {
+      const uint64_t off = j * kPiece;
+      const uint32_t len = static_cast<uint32_t>(pf.bytes[r] - off < kPiece ? pf.bytes[r] - off : kPiece);
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(pf.ptr[r] + off), "r"(len) : "memory");
+    }
+    base += pieces;
+  }
+}
+
+// Host: the config's ranges trimmed inward to 16-byte boundaries (empty ones dropped).
+inline L2Prefetch l2_prefetch_from(const dk_matmul_config* cfg) {
+  L2Prefetch pf{};
+  const int n = cfg ? (cfg->n_prefetch < DK_MAX_L2_PREFETCH ? cfg->n_prefetch : DK_MAX_L2_PREFETCH) : 0;
+  for (int i = 0; i < n; ++i) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(cfg->l2_prefetch_ptr[i]);
+    if (!a) continue;
+    const uintptr_t lo = (a + 15) & ~uintptr_t(15);
+    const uintptr_t hi = (a + cfg->l2_prefetch_bytes[i]) & ~uintptr_t(15);
+    if (hi <= lo) continue;
+    pf.ptr[pf.n] = reinterpret_cast<const char*>(lo);
+    pf.bytes[pf.n] = hi - lo;
+    ++pf.n;
+  }
+  return pf;
+}
+
 // ------------------------------------------------------------- programmatic dependent launch
 // Wait until the preceding kernel on the stream (if it was launched as our PDL primary) has
 // completed and its writes are visible. A no-op when there is no such kernel.
@@ -151,6 +195,34 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::
                    : "memory");
+}
+
+// Split cluster barrier: arrive early, wait late (every thread of every CTA in the cluster takes
+// each arrive and each wait, in the same order).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+
+// Asynchronous 8-byte store into cluster CTA shared memory (addresses from map_shared_rank); the
+// bytes count against the transaction count of the mbarrier at `remote_bar` in the same CTA.
+__device__ __forceinline__ void st_async_v2_f32(uint32_t remote, float a, float b, uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(remote),
+               "f"(a), "f"(b), "r"(remote_bar)
+               : "memory");
+}
+
+// Four 8x8 b16 matrices from shared memory; lane i gives the row address of row (i % 8) of matrix
+// (i / 8). `trans` delivers each matrix transposed.
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void* row) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_addr(row)));
+}
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void* row) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_addr(row)));
 }
 
 // Address of `p` (a shared-memory address of this CTA) in the shared memory of cluster CTA `rank`.

@@ -73,6 +73,7 @@ struct GemvParams {
   int64_t ldro;
   float eps;
   int* err;
+  L2Prefetch pf;  // ranges to pull into L2 for a later launch (a hint)
 };
 
 struct SmemLayout {
@@ -333,6 +334,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 3 - NT)  // M <= 8: two CTA
   bool ok = true;
   if (warp == kWarps) {
     // ---------------------------------------------------------------- producer warp
+    if (p.pf.n) l2_prefetch_share(p.pf, blockIdx.x + gridDim.x * blockIdx.y, gridDim.x * gridDim.y, lane);
     if (!p.static_weights) pdl_wait();
     if (lane == 0) {
       prefetch_tensormap(&mq);
@@ -748,6 +750,7 @@ int run_fast(const void* x, int64_t ldx, const int32_t* qweight, const void* sca
     p.ldro = na.ldro;
     p.eps = na.eps;
     p.err = dev.err_word;
+    p.pf = l2_prefetch_from(m0 == 0 ? cfg : nullptr);
     const int rc = launch_gemv(mq, ms, mz, p, c, (flags & DK_FLAG_EXACT_DEQUANT) != 0, st);
     if (rc != DK_OK) return rc;
   }

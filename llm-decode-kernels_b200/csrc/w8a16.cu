@@ -43,6 +43,7 @@ struct W8Params {
   int M, N, K;
   int stages_total, split_stages, chunks, nbuf, xs_pitch, static_weights;
   int* err;
+  L2Prefetch pf;  // ranges to pull into L2 for a later launch (a hint)
 };
 
 struct Layout8 {
@@ -128,6 +129,7 @@ __global__ void __launch_bounds__((kWarps8 + 1) * 32, 3 - NT)
 
   bool ok = true;
   if (warp == kWarps8) {
+    if (p.pf.n) l2_prefetch_share(p.pf, blockIdx.x + gridDim.x * blockIdx.y, gridDim.x * gridDim.y, lane);
     if (!p.static_weights) pdl_wait();
     if (lane == 0) {
       prefetch_tensormap(&mw);
@@ -441,6 +443,7 @@ extern "C" int dk_w8a16_matmul(const void* x, int64_t ldx, const uint8_t* wq, co
     p.xs_pitch = xs_pitch8(p.split_stages);
     p.static_weights = (flags & DK_FLAG_STATIC_WEIGHTS) ? 1 : 0;
     p.err = dev.err_word;
+    p.pf = l2_prefetch_from(m0 == 0 ? cfg : nullptr);
     const dim3 grid(c.nctas, c.split, 1);
     cudaError_t e = launch(variant8(mc <= 8 ? 1 : 2, c.cw), grid, dim3((kWarps8 + 1) * 32), c.smem, st, pdl_enabled(),
                            dim3(1, c.split, 1), mw, p);

@@ -21,10 +21,16 @@ I32 = ctypes.c_int32
 F32 = ctypes.c_float
 
 
-class MatmulConfig(ctypes.Structure):
-    """dk_matmul_config: zero fields mean "choose automatically"."""
+MAX_L2_PREFETCH = 6
 
-    _fields_ = [("split_k", I32), ("block_n", I32), ("flags", I32), ("reserved", I32)]
+
+class MatmulConfig(ctypes.Structure):
+    """dk_matmul_config: zero fields mean "choose automatically"; n_prefetch ranges of device memory
+    the launch pulls into L2 for a later launch."""
+
+    _fields_ = [("split_k", I32), ("block_n", I32), ("flags", I32), ("n_prefetch", I32),
+                ("l2_prefetch_ptr", ctypes.c_void_p * MAX_L2_PREFETCH),
+                ("l2_prefetch_bytes", ctypes.c_uint64 * MAX_L2_PREFETCH)]
 
 
 FLAG_STATIC_WEIGHTS = 1
@@ -34,6 +40,7 @@ FLAG_EXACT_DEQUANT = 4
 # name -> argtypes; every function returns int status
 SIGNATURES = {
     "dk_abi_version": [],
+    "dk_matmul_config_size": [],
     "dk_device_error": [ctypes.POINTER(I32)],
     "dk_clear_device_error": [],
     "dk_set_pdl": [I32],

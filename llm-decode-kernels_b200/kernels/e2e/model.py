@@ -34,6 +34,8 @@ class Linear:
     scales: torch.Tensor | None = None
     zeros: torch.Tensor | None = None
     bias: torch.Tensor | None = None
+    # kernel backends: tensors this projection's launch pulls into L2 for a later launch
+    l2_next: tuple | None = None
 
 
 class Backend:
@@ -101,6 +103,9 @@ class OursBackend(Backend):
         self.decode_kernel = decode_kernel
         self.name = "ours" if decode_kernel == "triton" else f"ours_{decode_kernel}"
 
+    def cfg(self, p: Linear) -> dict:
+        return self.LINEAR_CFG if p.l2_next is None else {**self.LINEAR_CFG, "L2_PREFETCH": p.l2_next}
+
     def linear(self, x, p: Linear):
         from kernels.w4a16 import w4a16_matmul
 
@@ -109,7 +114,7 @@ class OursBackend(Backend):
             from kernels.cuda.w4a16_cuda import w4a16_decode_cuda
 
             return w4a16_decode_cuda(x, p.qweight, p.scales, p.zeros, bias=p.bias)
-        return w4a16_matmul(x, p.qweight, p.scales, p.zeros, bias=p.bias, config=self.LINEAR_CFG)
+        return w4a16_matmul(x, p.qweight, p.scales, p.zeros, bias=p.bias, config=self.cfg(p))
 
     def norm(self, x, w, eps, residual=None):
         from kernels.rmsnorm import rmsnorm
@@ -124,19 +129,19 @@ class OursBackend(Backend):
     def gate_up_act(self, x, p: Linear):
         from kernels.w4a16 import w4a16_swiglu
 
-        return w4a16_swiglu(x, p.qweight, p.scales, p.zeros, bias=p.bias, config=self.LINEAR_CFG)
+        return w4a16_swiglu(x, p.qweight, p.scales, p.zeros, bias=p.bias, config=self.cfg(p))
 
     def norm_linear(self, x, w, eps, residual, p: Linear):
         from kernels.w4a16 import w4a16_rmsnorm_matmul
 
         return w4a16_rmsnorm_matmul(x, w, eps, residual, p.qweight, p.scales, p.zeros, bias=p.bias,
-                                    config=self.LINEAR_CFG)
+                                    config=self.cfg(p))
 
     def norm_gate_up_act(self, x, w, eps, residual, p: Linear):
         from kernels.w4a16 import w4a16_rmsnorm_matmul
 
         return w4a16_rmsnorm_matmul(x, w, eps, residual, p.qweight, p.scales, p.zeros, bias=p.bias, swiglu=True,
-                                    config=self.LINEAR_CFG)
+                                    config=self.cfg(p))
 
 
 class OursFP8Backend(OursBackend):
@@ -158,7 +163,7 @@ class OursFP8Backend(OursBackend):
     def linear(self, x, p: Linear):
         from kernels.fp8 import w8a16_matmul
 
-        return w8a16_matmul(x, p.qweight, p.scales, bias=p.bias, config=self.LINEAR_CFG)
+        return w8a16_matmul(x, p.qweight, p.scales, bias=p.bias, config=self.cfg(p))
 
     def gate_up_act(self, x, p: Linear):
         return self.act(self.linear(x, p))
@@ -203,7 +208,8 @@ class Layer:
 class QwenRunner:
     """Qwen2 forward on a static KV cache (reference model.py:150-253)."""
 
-    def __init__(self, hf_model, backend: Backend, max_len: int = 2048, batch: int = 1):
+    def __init__(self, hf_model, backend: Backend, max_len: int = 2048, batch: int = 1,
+                 l2_prefetch: bool = False):
         cfg = hf_model.config
         self.backend = backend
         self.eps = cfg.rms_norm_eps
@@ -246,6 +252,8 @@ class QwenRunner:
                 qkv=lin(a.q_proj, a.k_proj, a.v_proj), o=lin(a.o_proj),
                 gate_up=lin(mlp.gate_proj, mlp.up_proj), down=lin(mlp.down_proj),
             ))
+        if backend.fused_decode and l2_prefetch:
+            self._plan_l2_prefetch()
         # RoPE tables for the decode kernel, computed with the same ops as forward() does per step
         if backend.fused_decode:
             freqs = torch.arange(max_len, device=dev)[:, None].float() * self.inv_freq[None, :]
@@ -255,6 +263,20 @@ class QwenRunner:
         shape = (len(self.layers), batch, self.n_kv, max_len, self.head_dim)
         self.k_cache = torch.zeros(shape, device=dev, dtype=self.embed.dtype)
         self.v_cache = torch.zeros(shape, device=dev, dtype=self.embed.dtype)
+
+    def _plan_l2_prefetch(self):
+        """Each projection's launch pulls the weights of the projection two launches ahead in the
+        decode chain (qkv, o, gate_up, down of layer 0, then layer 1, ...) into L2; the first one
+        also pulls the next. A layer's weights (25 MB for Qwen2.5-1.5B) then arrive while the
+        latency-bound launches before them run, and each GEMV reads L2 instead of HBM."""
+        chain = [p for L in self.layers for p in (L.qkv, L.o, L.gate_up, L.down)]
+
+        def tensors(p):
+            return tuple(t for t in (p.qweight, p.scales, p.zeros) if t is not None)
+
+        for j, p in enumerate(chain):
+            ahead = chain[j + 2: j + 3] + (chain[1:2] if j == 0 else [])
+            p.l2_next = tuple(t for q in ahead for t in tensors(q)) or None
 
     def weight_bytes(self) -> dict:
         """Bytes of the swapped layers vs the parts that stay fp16 (reference model.py:196-210)."""

@@ -28,7 +28,7 @@ _choices: dict[tuple, dict] = {}  # (m_key, N, K, bias) -> config used (export/i
 
 
 def _config(config: dict | None) -> _lib.MatmulConfig:
-    c = _lib.MatmulConfig(0, 0, 0, 0)
+    c = _lib.MatmulConfig()
     if not config:
         return c
     split = int(config.get("SPLIT_K", 0) or 0)
@@ -40,6 +40,17 @@ def _config(config: dict | None) -> _lib.MatmulConfig:
     exact = bool(config.get("EXACT")) or config.get("FACTORED") is False
     c.flags = (_lib.FLAG_STATIC_WEIGHTS if config.get("STATIC_WEIGHTS") else 0) | (
         _lib.FLAG_GENERIC if config.get("GENERIC") else 0) | (_lib.FLAG_EXACT_DEQUANT if exact else 0)
+    # L2_PREFETCH: CUDA tensors (e.g. the weights of the launch after next) this launch pulls into L2
+    pf = [t for t in (config.get("L2_PREFETCH") or ()) if t is not None and t.numel() > 0]
+    if len(pf) > _lib.MAX_L2_PREFETCH:
+        raise ValueError(f"L2_PREFETCH: at most {_lib.MAX_L2_PREFETCH} tensors, got {len(pf)}")
+    for i, t in enumerate(pf):
+        _lib.require_cuda("L2_PREFETCH", t)
+        if not t.is_contiguous():
+            raise ValueError("L2_PREFETCH: tensors must be contiguous")
+        c.l2_prefetch_ptr[i] = t.data_ptr()
+        c.l2_prefetch_bytes[i] = t.numel() * t.element_size()
+    c.n_prefetch = len(pf)
     return c
 
 

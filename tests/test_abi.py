@@ -37,7 +37,7 @@ def test_library_loads_and_reports_version():
     from kernels import _lib
 
     h = _lib.lib()
-    assert h.dk_abi_version() == 1
+    assert h.dk_abi_version() == 2
     for name in declared_symbols():
         assert hasattr(h, name)
     # every declared symbol has a ctypes signature in the Python mirror
@@ -56,8 +56,8 @@ def test_errors_come_back_as_status_without_a_gpu():
     assert rc == -1 and b"group_size" in h.dk_last_error()
     rc = h.dk_pack_int4(None, None, 12, 4, None)
     assert rc == -1 and b"multiple of 8" in h.dk_last_error()
-    cfg = _lib.MatmulConfig(0, 0, 0, 0)
-    assert ctypes.sizeof(cfg) == 16
+    cfg = _lib.MatmulConfig()
+    assert ctypes.sizeof(cfg) == h.dk_matmul_config_size() == 16 + 16 * _lib.MAX_L2_PREFETCH
 
 
 def test_package_has_no_oracle_or_cpu_path():
