@@ -48,6 +48,10 @@ def parse():
     ap.add_argument("--no-extras", action="store_true", help="skip fp16 baseline, GEMV sweep and CPU baseline")
     ap.add_argument("--l2-prefetch", action="store_true",
                     help="runner with cross-launch L2 prefetch of the next projections' weights")
+    ap.add_argument("--tp7b", choices=["auto", "on", "off"], default="auto",
+                    help="Qwen2.5-7B tensor-parallel decode over the N ranks (BASELINE configs[4]); "
+                         "auto = on when N > 1")
+    ap.add_argument("--tp-batches", default="1,8", help="batch sizes of the 7B tensor-parallel decode")
     return ap.parse_args()
 
 
@@ -62,7 +66,7 @@ def dist_setup():
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     elif torch.cuda.is_available():
         torch.cuda.set_device(0)
@@ -264,6 +268,62 @@ def gemv_sweep(peak_gbs: float) -> dict:
     return out
 
 
+# ------------------------------------------------------------------------------ 7B tensor parallel
+TP_PROMPT = 1024
+
+
+def run_tp7b(args, world, rank) -> dict:
+    """Qwen2.5-7B-architecture decode (28 layers, hidden 3584, 28/4 heads, MLP
+    18944, vocab 152064, untied lm_head), random-init weights, all linears W4A16 g128 including
+    lm_head, tensor-parallel over the N ranks (column-sharded qkv/gate_up/lm_head, row-sharded
+    o_proj/down), synthetic 1024-token prompts, greedy decode under CUDA graphs. Each batch size is
+    timed with the fused GEMV+allreduce kernel and with the plain GEMV followed by an NCCL allreduce.
+    Strong scaling: the model is the same at every N."""
+    from kernels import _lib, config
+    from kernels.e2e.model import QwenRunner, make_backend, random_qwen2
+    from kernels.e2e.run import GraphDecoder
+    from kernels.tp import TensorParallel
+
+    t0 = time.perf_counter()
+    model = random_qwen2(config.QWEN7, dtype=torch.float16, device="cuda", seed=0)
+    tp = TensorParallel(mode="fused")
+    base = QwenRunner(model, make_backend("ours_lm"), max_len=MAX_LEN, batch=1, tp=tp)
+    del model
+    torch.cuda.empty_cache()
+    setup_s = time.perf_counter() - t0
+    res = {"workload": "BASELINE configs[4]: Qwen2.5-7B-architecture decode, random-init weights, W4A16 g128 "
+                       "linears incl. lm_head, tensor parallel (column: qkv, gate_up, lm_head; row: o_proj, down), "
+                       f"uniform random {TP_PROMPT}-token prompts, greedy decode under CUDA graphs",
+           "tp": world, "scaling": "strong", "unit": "tok/s", "steps": args.steps, "warmup": max(args.warmup, 3),
+           "plan": {"q_heads": base.n_heads, "kv_heads": base.n_kv, "mlp_cols": base.plan.mlp[1] - base.plan.mlp[0],
+                    "vocab_rows": base.plan.vocab[1] - base.plan.vocab[0]},
+           "setup_s": round(setup_s, 1), "batches": {}}
+    n_layers = len(base.layers)
+    for B in [int(b) for b in args.tp_batches.split(",") if b]:
+        runner = base if B == 1 else base.with_batch(B)
+        ids = torch.randint(0, config.QWEN7["vocab_size"], (B, TP_PROMPT),
+                            generator=torch.Generator().manual_seed(3)).cuda()
+        row = {}
+        for mode in ("fused", "nccl"):
+            tp.mode = mode
+            dec = GraphDecoder(runner)
+            dec.capture(ids)
+            sec = max_over_ranks(time_decode(dec, ids, args.steps, max(args.warmup, 3), world), world)
+            row[mode] = {"tok_s": round(B * args.steps / sec, 2), "ms_per_step": round(sec / args.steps * 1e3, 4),
+                         "us_per_layer": round(sec / args.steps / n_layers * 1e6, 2)}
+            del dec
+        tp.mode = "fused"
+        row["fused_vs_nccl"] = round(row["fused"]["tok_s"] / row["nccl"]["tok_s"], 3)
+        res["batches"][str(B)] = row
+        del runner
+        torch.cuda.empty_cache()
+    res["device_error"] = _lib.device_error()
+    tp.close()
+    del base
+    torch.cuda.empty_cache()
+    return res
+
+
 # ------------------------------------------------------------------------------ CPU baseline
 def cpu_decode_rate(model, steps: int, threads: int | None = None) -> dict:
     """The reference's CPU path on the same model: OracleRunner (dequantize-then-fp32-matmul
@@ -394,10 +454,14 @@ def run_ours(args, world, rank, local):
         if world == 1 and rank == 0:
             extras["cpu_baseline"] = cpu_decode_rate(model, steps=4)
     assert _lib.device_error() == 0, "a kernel recorded a device-side error"
+    if args.tp7b == "on" or (args.tp7b == "auto" and world > 1):
+        del dec, runner
+        torch.cuda.empty_cache()
+        extras["tp7b"] = run_tp7b(args, world, rank)
     # our kernels per token: per layer norm+qkv, attention, o_proj, norm+gate_up+SwiGLU, down (FP8:
     # separate norm and SwiGLU kernels, 8 per layer), then the final norm and a quantized lm_head
     per_layer = 8 if args.backend.startswith("ours_fp8") else 5
-    per_step_launches = per_layer * len(runner.layers) + 1 + (1 if runner.head_q is not None else 0)
+    per_step_launches = per_layer * 28 + 1 + (1 if args.backend.endswith("_lm") else 0)
     if rank != 0:
         return None
     return {"metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,

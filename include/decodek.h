@@ -25,7 +25,7 @@ extern "C" {
 
 typedef struct CUstream_st* dk_stream_t; /* same type as cudaStream_t */
 
-#define DK_ABI_VERSION 2
+#define DK_ABI_VERSION 3
 
 /* status codes */
 #define DK_OK 0
@@ -39,6 +39,7 @@ typedef struct CUstream_st* dk_stream_t; /* same type as cudaStream_t */
 #define DK_DEVERR_WAIT_FULL 1  /* a consumer gave up waiting for a stage's copies */
 #define DK_DEVERR_WAIT_EMPTY 2 /* the producer gave up waiting for a stage to be released */
 #define DK_DEVERR_BAD_POSITION 3 /* decode attention: position outside [0, max_len) (no write done) */
+#define DK_DEVERR_TP_WAIT 4      /* a fused-allreduce CTA gave up waiting for a peer's partial sums */
 
 /* dk_matmul_config.flags */
 #define DK_FLAG_STATIC_WEIGHTS 1 /* weights are not written by any kernel still in flight on the
@@ -174,6 +175,48 @@ int dk_decode_attention(const void* qkv, void* k_cache, void* v_cache, const int
                         const void* cos, const void* sin, void* out, int64_t B, int64_t nq,
                         int64_t nkv, int64_t head_dim, int64_t max_len, int64_t rope_stride,
                         int32_t splits, int32_t flags, dk_stream_t stream);
+
+/* ---- tensor parallelism: row-sharded W4A16 projection fused with its allreduce ------------
+ * No reference counterpart: the reference runs on one GPU (README.md:249). These entry points serve
+ * the tensor-parallel runner (column-sharded qkv/gate_up/lm_head, row-sharded o_proj/down), one
+ * process per GPU of one node. Each rank owns one exchange buffer, allocated once at set-up and
+ * mapped into every peer with CUDA IPC; a row-sharded projection then pushes its fp32 partial sums
+ * into every peer's buffer over NVLink from the GEMV epilogue and sums the ranks' partials of its own
+ * output columns in rank order, so the matmul and the allreduce are one kernel and every rank ends
+ * with the same bits. No TMA multicast is used on peer memory. */
+#define DK_TP_MAX_WORLD 8
+#define DK_TP_IPC_HANDLE_BYTES 64 /* sizeof(cudaIpcMemHandle_t) */
+
+typedef struct dk_tp_comm dk_tp_comm;
+
+/* Bytes of one rank's exchange buffer for launches of up to max_m rows (max 16) and max_n columns. */
+int dk_tp_buffer_bytes(int32_t world, int64_t max_m, int64_t max_n, uint64_t* bytes);
+/* Set-up only (allocates and synchronizes): cudaMalloc `bytes` on the current device, zero them,
+ * return the pointer and its IPC handle (DK_TP_IPC_HANDLE_BYTES bytes written to ipc_handle). */
+int dk_tp_buffer_alloc(uint64_t bytes, void** ptr, void* ipc_handle);
+int dk_tp_buffer_free(void* ptr);
+/* Set-up only: map a peer process's buffer from its IPC handle (peer access over NVLink). */
+int dk_tp_buffer_open(const void* ipc_handle, void** ptr);
+int dk_tp_buffer_close(void* ptr);
+/* A communicator over the exchange buffers of all ranks: bufs[rank] is this rank's own buffer
+ * (dk_tp_buffer_alloc), bufs[q] the mapping of rank q's (dk_tp_buffer_open). Host object only;
+ * destroying it frees and unmaps nothing. */
+int dk_tp_comm_create(dk_tp_comm** comm, int32_t rank, int32_t world, void* const* bufs, int64_t max_m,
+                      int64_t max_n);
+int dk_tp_comm_destroy(dk_tp_comm* comm);
+
+/* Row-sharded w4a16_matmul with the allreduce fused in:
+ *   y[M, N] = fp16( sum over ranks r, in rank order, of x_r[M, K] @ dequant(W_r).T  + bias )
+ * where each rank passes its own K-shard x_r and W_r (qweight [K/8, N], scales/zeros [K/128, N]) and
+ * receives the full y. Every rank must make the same sequence of calls on one communicator with the
+ * same M, N and K (the kernels of different ranks meet per CTA; a CTA that waits more than ~2 s for
+ * a peer gives up, leaves its columns of y unwritten and sets DK_DEVERR_TP_WAIT). Needs the fast
+ * path's conditions (group_size 128, N % 8 == 0, 16-byte aligned operands), N <= max_n, and runs
+ * M in launches of up to min(16, max_m) rows. */
+int dk_w4a16_matmul_allreduce(const void* x, int64_t ldx, const int32_t* qweight, const void* scales,
+                              const void* zeros, const void* bias, void* y, int64_t ldy, int64_t M, int64_t N,
+                              int64_t K, int64_t group_size, const dk_matmul_config* cfg,
+                              const dk_tp_comm* comm, dk_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -480,7 +480,9 @@ extern "C" int dk_decode_attention(const void* qkv, void* k_cache, void* v_cache
   switch (G) {
     DK_ATTN(1)
     DK_ATTN(2)
+    DK_ATTN(3)
     DK_ATTN(4)
+    DK_ATTN(5)
     DK_ATTN(6)
     DK_ATTN(7)
     DK_ATTN(8)

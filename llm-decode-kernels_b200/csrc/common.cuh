@@ -174,6 +174,36 @@ inline L2Prefetch l2_prefetch_from(const dk_matmul_config* cfg) {
   return pf;
 }
 
+// ------------------------------------------------------------------- tensor-parallel exchange
+// One rank's exchange buffer (allocated by dk_tp_buffer_alloc, zeroed, mapped into every peer):
+//   [0, 256)                 header: launch epoch (u64), CTA arrival count (u32)
+//   [256, 256 + kTpFlagBytes) flags[src rank][CTA] (u64): the epoch at which CTA `CTA` of rank `src`
+//                            finished pushing its partial sums into this buffer
+//   [kTpDataOff, ...)        data[slot 0..1][src rank][max_m][max_n] fp32 partial sums
+constexpr int kTpMaxCtas = 1024;
+constexpr size_t kTpHeaderBytes = 256;
+constexpr size_t kTpFlagBytes = static_cast<size_t>(DK_TP_MAX_WORLD) * kTpMaxCtas * 8;
+constexpr size_t kTpDataOff = kTpHeaderBytes + kTpFlagBytes;
+
+// What a fused-allreduce launch needs; world == 0 means a plain launch.
+struct TPArgs {
+  float* data[DK_TP_MAX_WORLD];                 // data region of each rank's buffer (peer mappings)
+  unsigned long long* flags[DK_TP_MAX_WORLD];   // flag region of each rank's buffer
+  unsigned long long* epoch;                    // this rank's header
+  unsigned int* arrive;
+  int rank, world, max_m, max_n;
+};
+
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
 // ------------------------------------------------------------- programmatic dependent launch
 // Wait until the preceding kernel on the stream (if it was launched as our PDL primary) has
 // completed and its writes are visible. A no-op when there is no such kernel.

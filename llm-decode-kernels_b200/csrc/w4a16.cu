@@ -34,6 +34,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstring>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -74,6 +75,7 @@ struct GemvParams {
   float eps;
   int* err;
   L2Prefetch pf;  // ranges to pull into L2 for a later launch (a hint)
+  TPArgs tp;      // tp.world > 0: row-sharded launch with the allreduce fused in (see tp_finish)
 };
 
 struct SmemLayout {
@@ -204,6 +206,97 @@ __device__ __forceinline__ void consume_chunk_stage(const uint8_t* __restrict__ 
   }
 }
 
+// ------------------------------------------------------------------ fused allreduce (row sharding)
+// A row-sharded launch computes this rank's partial sums of y. Instead of storing them, the
+// epilogue pushes them (fp32, no bias) into slot (epoch & 1), row `rank`, of every rank's exchange
+// buffer over NVLink; tp_finish then publishes this CTA's flag in every buffer, waits for the flags
+// of the same CTA on the other ranks (each rank launches the same grid, so CTA i covers the same
+// columns everywhere), and adds the ranks' partials of its own columns in rank order. Two slots
+// suffice: a rank starts launch e + 2 only after its launch e + 1 finished, and every CTA of that
+// launch waited for all ranks' launch e + 1, which start after their launch e finished reading.
+__device__ __forceinline__ float* tp_cell(const TPArgs& tp, int q, unsigned long long ep, int src, int m, int n) {
+  return tp.data[q] + ((static_cast<size_t>(ep & 1) * tp.world + src) * tp.max_m + m) * static_cast<size_t>(tp.max_n) + n;
+}
+
+__device__ __forceinline__ void tp_push(const TPArgs& tp, unsigned long long ep, int m, int n, float v) {
+  for (int q = 0; q < tp.world; ++q) *tp_cell(tp, q, ep, tp.rank, m, n) = v;
+}
+
+__device__ __forceinline__ void tp_push4(const TPArgs& tp, unsigned long long ep, int m, int n, float4 v) {
+  for (int q = 0; q < tp.world; ++q) *reinterpret_cast<float4*>(tp_cell(tp, q, ep, tp.rank, m, n)) = v;
+}
+
+// Called by every thread of the CTA after its last push. Columns: [c_begin*32, min(c_end*32, N)) with
+// split 1; with a cluster split S the elements e = m*ncols + col with e % S == cluster rank.
+__device__ void tp_finish(const GemvParams& p, unsigned long long ep, bool ok, int c_begin, int c_end, int upt,
+                          int S, int crank) {
+  const TPArgs& tp = p.tp;
+  const int cta = blockIdx.x + gridDim.x * blockIdx.y;
+  __syncthreads();  // every push of this CTA has been issued
+  if (threadIdx.x == 0) {
+    fence_acq_rel_sys();  // the CTA's pushes (ordered before this by the barrier) precede the flags
+    for (int q = 0; q < tp.world; ++q) st_release_sys_u64(tp.flags[q] + tp.rank * kTpMaxCtas + cta, ep);
+  }
+  bool bad = false;
+  if (threadIdx.x < tp.world) {
+    const unsigned long long* f = tp.flags[tp.rank] + threadIdx.x * kTpMaxCtas + cta;
+    if (ld_acquire_sys_u64(f) != ep) {
+      const uint64_t t0 = globaltimer_ns();
+      while (ld_acquire_sys_u64(f) != ep) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          record_device_error(p.err, DK_DEVERR_TP_WAIT);
+          bad = true;
+          break;
+        }
+      }
+    }
+  }
+  bad = __syncthreads_or(bad);
+  if (ok && !bad) {
+    const float* own = tp.data[tp.rank] + static_cast<size_t>(ep & 1) * tp.world * tp.max_m * static_cast<size_t>(tp.max_n);
+    const size_t row_stride = static_cast<size_t>(tp.max_m) * tp.max_n;  // between source ranks
+    if (S == 1) {
+      const int n_lo = c_begin * 32, n_hi = min(c_end * 32, p.N);
+      const int nq = (n_hi - n_lo) / 4;  // N % 8 == 0 on this path
+      for (int e = threadIdx.x; e < p.M * nq; e += blockDim.x) {
+        const int m = e / nq, n = n_lo + 4 * (e % nq);
+        const float* src = own + static_cast<size_t>(m) * tp.max_n + n;
+        float4 a = __ldcg(reinterpret_cast<const float4*>(src));
+        for (int q = 1; q < tp.world; ++q) {
+          const float4 b = __ldcg(reinterpret_cast<const float4*>(src + q * row_stride));
+          a.x += b.x;
+          a.y += b.y;
+          a.z += b.z;
+          a.w += b.w;
+        }
+        float v[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          if (p.bias != nullptr) v[c] += __half2float(p.bias[n + c]);
+          p.y[m * p.ldy + n + c] = __float2half_rn(v[c]);
+        }
+      }
+    } else {
+      const int ncols = min(upt, c_end - c_begin) * 32;
+      for (int e = threadIdx.x; e < p.M * ncols; e += blockDim.x) {
+        if (e % S != crank) continue;
+        const int m = e / ncols, n = c_begin * 32 + e % ncols;
+        if (n >= p.N) continue;
+        const float* src = own + static_cast<size_t>(m) * tp.max_n + n;
+        float a = __ldcg(src);
+        for (int q = 1; q < tp.world; ++q) a += __ldcg(src + q * row_stride);
+        if (p.bias != nullptr) a += __half2float(p.bias[n]);
+        p.y[m * p.ldy + n] = __float2half_rn(a);
+      }
+    }
+  }
+  if (threadIdx.x == 0 && atomicAdd(tp.arrive, 1u) == gridDim.x * gridDim.y - 1) {
+    // last CTA of the launch: the next launch on this communicator uses epoch ep + 1
+    *tp.arrive = 0;
+    *reinterpret_cast<volatile unsigned long long*>(tp.epoch) = ep;
+  }
+}
+
 // Stage x[:, K slice of this CTA] into shared memory, each 8-element block permuted to
 // (0,4,1,5,2,6,3,7) for the MMA fragments. With `norm_w` the staged rows are the fused residual
 // add + RMSNorm of the input, with the rounding of kernels/rmsnorm.py:28-37 (and the rmsnorm kernel
@@ -304,6 +397,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 3 - NT)  // M <= 8: two CTA
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int rank = blockIdx.y;  // cluster dims (1, S, 1)
+  __shared__ unsigned long long s_ep;  // fused allreduce: this launch's epoch
   const int s_begin = rank * p.split_stages;
   const int s_end = min(s_begin + p.split_stages, p.stages_total);
   const int nst = max(0, s_end - s_begin);
@@ -365,7 +459,9 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 3 - NT)  // M <= 8: two CTA
   } else {
     // ---------------------------------------------------------------- consumer warps
     pdl_wait();  // x (and the residual) come from the previous kernels
-    stage_x(p, smem + L.xs_off, s_begin, nst, blockIdx.x == 0 && blockIdx.y == 0);
+    if (p.tp.world > 0 && threadIdx.x == 0) s_ep = *reinterpret_cast<volatile unsigned long long*>(p.tp.epoch) + 1;
+    stage_x(p, smem + L.xs_off, s_begin, nst, blockIdx.x == 0 && blockIdx.y == 0);  // ends with a barrier
+    const unsigned long long ep = s_ep;
     const int g = lane >> 2;  // MMA group: A rows g, g+8 ; B column g
     const int t = lane & 3;   // thread in group: K slots 2t.., 2t+8..
     const int slot = warp % CW;  // chunk of the tile this warp works on
@@ -409,6 +505,10 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 3 - NT)  // M <= 8: two CTA
               const int m = nt * 8 + 2 * t + e;
               if (m >= p.M) continue;
               float v[4] = {acc[0][nt][e], acc[0][nt][2 + e], acc[1][nt][e], acc[1][nt][2 + e]};
+              if (p.tp.world > 0) {  // N % 8 == 0: the 4 columns are all inside or all outside
+                if (n0 < p.N) tp_push4(p.tp, ep, m, n0, make_float4(v[0], v[1], v[2], v[3]));
+                continue;
+              }
 #pragma unroll
               for (int c = 0; c < 4; ++c)
                 if (n0 + c < p.N) {
@@ -450,6 +550,10 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 3 - NT)  // M <= 8: two CTA
             const int n = tile * 32 + col;
             if (!swiglu && n < p.N) {
               float a = v[0];
+              if (p.tp.world > 0) {
+                tp_push(p.tp, ep, m, n, a);
+                continue;
+              }
               if (p.bias != nullptr) a += __half2float(p.bias[n]);
               p.y[m * p.ldy + n] = __float2half_rn(a);
             } else if (swiglu && n < p.swiglu_i) {
@@ -479,6 +583,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 3 - NT)  // M <= 8: two CTA
       cluster_sync();
       cluster_sync();
     }
+    if (p.tp.world > 0) tp_finish(p, s_ep, false, c_begin, c_end, UPT, S, rank);
     return;
   }
   if (S > 1) {
@@ -497,6 +602,8 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 3 - NT)  // M <= 8: two CTA
       }
       if (swiglu) {
         p.y[m * p.ldy + n] = swiglu_out(v[0], v[1], p.bias, n, p.swiglu_i);
+      } else if (p.tp.world > 0) {
+        tp_push(p.tp, s_ep, m, n, v[0]);
       } else {
         if (p.bias != nullptr) v[0] += __half2float(p.bias[n]);
         p.y[m * p.ldy + n] = __float2half_rn(v[0]);
@@ -504,6 +611,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 3 - NT)  // M <= 8: two CTA
     }
     cluster_sync();  // keep this CTA's partial sums alive until every rank has read them
   }
+  if (p.tp.world > 0) tp_finish(p, s_ep, true, c_begin, c_end, UPT, S, rank);
 }
 
 // Any-alignment fallback: one thread per (row, column), plain loads, the reference's fp16 weight
@@ -711,7 +819,8 @@ struct NormArgs {
 
 int run_fast(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const void* zeros,
              const void* bias, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group_size,
-             const dk_matmul_config* cfg, int swiglu_i, const NormArgs& na, cudaStream_t st) {
+             const dk_matmul_config* cfg, int swiglu_i, const NormArgs& na, cudaStream_t st,
+             const TPArgs* tp = nullptr) {
   const int flags = cfg ? cfg->flags : 0;
   CUtensorMap mq, ms, mz;
   if (!make_tensor_map_2d(&mq, qweight, CU_TENSOR_MAP_DATA_TYPE_INT32, N, K / 8, N * 4, 32, kStageRows,
@@ -723,10 +832,14 @@ int run_fast(const void* x, int64_t ldx, const int32_t* qweight, const void* sca
     return DK_ERR_CUDA;
   const DeviceInfo& dev = device_info();
   const int units = swiglu_i > 0 ? (swiglu_i + 31) / 32 : static_cast<int>((N + 31) / 32);
-  for (int64_t m0 = 0; m0 < M; m0 += 16) {
-    const int mc = static_cast<int>(std::min<int64_t>(16, M - m0));
+  const int64_t rows_per_launch = tp != nullptr ? std::min<int64_t>(16, tp->max_m) : 16;
+  for (int64_t m0 = 0; m0 < M; m0 += rows_per_launch) {
+    const int mc = static_cast<int>(std::min<int64_t>(rows_per_launch, M - m0));
     const Choice c = choose(mc, units, static_cast<int>(K), swiglu_i > 0, cfg);
     if (c.cw == 0) return set_error(DK_ERR_UNSUPPORTED, "w4a16: no tile fits (M=%d, K=%lld)", mc, (long long)K);
+    if (tp != nullptr && (mc > tp->max_m || c.nctas * c.split > kTpMaxCtas))
+      return set_error(DK_ERR_UNSUPPORTED, "w4a16_matmul_allreduce: %d rows or %d CTAs exceed the communicator",
+                       mc, c.nctas * c.split);
     GemvParams p;
     p.x = static_cast<const __half*>(x) + m0 * ldx;
     p.ldx = ldx;
@@ -751,6 +864,10 @@ int run_fast(const void* x, int64_t ldx, const int32_t* qweight, const void* sca
     p.eps = na.eps;
     p.err = dev.err_word;
     p.pf = l2_prefetch_from(m0 == 0 ? cfg : nullptr);
+    if (tp != nullptr)
+      p.tp = *tp;
+    else
+      std::memset(&p.tp, 0, sizeof(p.tp));
     const int rc = launch_gemv(mq, ms, mz, p, c, (flags & DK_FLAG_EXACT_DEQUANT) != 0, st);
     if (rc != DK_OK) return rc;
   }
@@ -851,4 +968,29 @@ extern "C" int dk_w4a16_rmsnorm_matmul(const void* x, int64_t ldx, const void* r
   na.eps = eps;
   return run_fast(x, ldx, qweight, scales, zeros, bias, y, ldy, M, N, K, group_size, cfg,
                   swiglu ? static_cast<int>(N / 2) : 0, na, reinterpret_cast<cudaStream_t>(stream));
+}
+
+namespace dk {
+bool tp_args_from(const dk_tp_comm* c, TPArgs* a);
+}
+
+extern "C" int dk_w4a16_matmul_allreduce(const void* x, int64_t ldx, const int32_t* qweight, const void* scales,
+                                         const void* zeros, const void* bias, void* y, int64_t ldy, int64_t M,
+                                         int64_t N, int64_t K, int64_t group_size, const dk_matmul_config* cfg,
+                                         const dk_tp_comm* comm, dk_stream_t stream) {
+  using namespace dk;
+  int rc = check_w4a16_args("w4a16_matmul_allreduce", x, ldx, qweight, scales, zeros, y, ldy, M, N, N, K, group_size);
+  if (rc != DK_OK) return rc;
+  TPArgs tp;
+  if (!tp_args_from(comm, &tp)) return set_error(DK_ERR_INVALID, "w4a16_matmul_allreduce: comm is NULL");
+  if (N > tp.max_n)
+    return set_error(DK_ERR_INVALID, "w4a16_matmul_allreduce: N=%lld exceeds the communicator's max_n=%d",
+                     (long long)N, tp.max_n);
+  if (M == 0 || N == 0) return DK_OK;
+  const int flags = cfg ? cfg->flags : 0;
+  if (!fast_ok(x, ldx, qweight, scales, zeros, N, K, group_size, flags))
+    return set_error(DK_ERR_UNSUPPORTED,
+                     "w4a16_matmul_allreduce: needs group_size 128, N %% 8 == 0 and 16-byte aligned operands");
+  return run_fast(x, ldx, qweight, scales, zeros, bias, y, ldy, M, N, K, group_size, cfg, 0, NormArgs(),
+                  reinterpret_cast<cudaStream_t>(stream), &tp);
 }

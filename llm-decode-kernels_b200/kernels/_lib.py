@@ -58,6 +58,15 @@ SIGNATURES = {
     "dk_rmsnorm": [P, I64, P, I64, P, P, I64, P, I64, I64, I64, F32, P],
     "dk_swiglu": [P, I64, P, I64, P, I64, I64, I64, P],
     "dk_decode_attention": [P, P, P, P, P, P, P, I64, I64, I64, I64, I64, I64, I32, I32, P],
+    "dk_tp_buffer_bytes": [I32, I64, I64, ctypes.POINTER(ctypes.c_uint64)],
+    "dk_tp_buffer_alloc": [ctypes.c_uint64, ctypes.POINTER(P), P],
+    "dk_tp_buffer_free": [P],
+    "dk_tp_buffer_open": [P, ctypes.POINTER(P)],
+    "dk_tp_buffer_close": [P],
+    "dk_tp_comm_create": [ctypes.POINTER(P), I32, I32, ctypes.POINTER(P), I64, I64],
+    "dk_tp_comm_destroy": [P],
+    "dk_w4a16_matmul_allreduce": [P, I64, P, P, P, P, P, I64, I64, I64, I64, I64, ctypes.POINTER(MatmulConfig), P,
+                                  P],
 }
 
 _lib = None

@@ -209,7 +209,9 @@ class QwenRunner:
     """Qwen2 forward on a static KV cache (reference model.py:150-253)."""
 
     def __init__(self, hf_model, backend: Backend, max_len: int = 2048, batch: int = 1,
-                 l2_prefetch: bool = False):
+                 l2_prefetch: bool = False, tp=None):
+        """tp: a kernels.tp.TensorParallel to hold only this rank's shards (column-sharded qkv,
+        gate_up and lm_head; row-sharded o_proj and down, reduced over the group), or None."""
         cfg = hf_model.config
         self.backend = backend
         self.eps = cfg.rms_norm_eps
@@ -221,18 +223,37 @@ class QwenRunner:
         m = hf_model.model
         dev = m.embed_tokens.weight.device
         self.embed = m.embed_tokens.weight
-        self.lm_head = hf_model.lm_head.weight
+        self.tp = tp
+        hd = self.head_dim
+        full = (0, 1 << 62)
+        if tp is not None:
+            self.plan = tp.plan(cfg)
+            self.n_heads, self.n_kv = self.plan.n_q, self.plan.n_kv
+            qh, kvh, mlp, voc = self.plan.q_heads, self.plan.kv_heads, self.plan.mlp, self.plan.vocab
+        else:
+            self.plan = None
+            qh, kvh, mlp, voc = full, full, full, full
+        self.vocab_start = voc[0] if tp is not None else 0
+        qc, kvc = (qh[0] * hd, qh[1] * hd), (kvh[0] * hd, kvh[1] * hd)
+        self.lm_head = hf_model.lm_head.weight[voc[0]:voc[1]]
         self.final_norm = m.norm.weight
         rope = getattr(cfg, "rope_parameters", None) or {}
         theta = rope.get("rope_theta", getattr(cfg, "rope_theta", 10000.0))
         d = self.head_dim
         self.inv_freq = 1.0 / (theta ** (torch.arange(0, d, 2, device=dev, dtype=torch.float) / d))
 
-        def lin(*mods) -> Linear:
-            w = torch.cat([mm.weight.data for mm in mods], 0)
+        def part(mod, rows=full, cols=full):
+            """(weight, bias) of a module restricted to output rows / input columns (a shard)."""
+            w = mod.weight.data[rows[0]:rows[1], cols[0]:cols[1]]
+            b = None if mod.bias is None else mod.bias.data[rows[0]:rows[1]]
+            return w, b
+
+        def lin(*parts) -> Linear:
+            parts = [p if isinstance(p, tuple) else part(p) for p in parts]
+            w = torch.cat([pw for pw, _ in parts], 0).contiguous()
             b = None
-            if mods[0].bias is not None:
-                b = torch.cat([mm.bias.data for mm in mods], 0)
+            if parts[0][1] is not None:
+                b = torch.cat([pb for _, pb in parts], 0).contiguous()
             if not backend.quantized:
                 return Linear(w=w, bias=b)
             if hasattr(backend, "quantize"):  # formats other than int4 RTN (FP8)
@@ -243,15 +264,20 @@ class QwenRunner:
             return Linear(qweight=qw, scales=s, zeros=z, bias=b)
 
         # Optional quantized copy of lm_head (the fp16 table stays for the embedding lookup).
-        self.head_q = lin(hf_model.lm_head) if getattr(backend, "quant_lm_head", False) else None
+        self.head_q = (lin(part(hf_model.lm_head, rows=voc)) if getattr(backend, "quant_lm_head", False)
+                       else None)
         self.layers = []
         for layer in m.layers:
-            a, mlp = layer.self_attn, layer.mlp
+            a, f = layer.self_attn, layer.mlp
             self.layers.append(Layer(
                 ln1=layer.input_layernorm.weight, ln2=layer.post_attention_layernorm.weight,
-                qkv=lin(a.q_proj, a.k_proj, a.v_proj), o=lin(a.o_proj),
-                gate_up=lin(mlp.gate_proj, mlp.up_proj), down=lin(mlp.down_proj),
+                qkv=lin(part(a.q_proj, rows=qc), part(a.k_proj, rows=kvc), part(a.v_proj, rows=kvc)),
+                o=lin(part(a.o_proj, cols=qc)),
+                gate_up=lin(part(f.gate_proj, rows=mlp), part(f.up_proj, rows=mlp)),
+                down=lin(part(f.down_proj, cols=mlp)),
             ))
+        if tp is not None:
+            tp.setup(cfg.hidden_size, dev)
         if backend.fused_decode and l2_prefetch:
             self._plan_l2_prefetch()
         # RoPE tables for the decode kernel, computed with the same ops as forward() does per step
@@ -263,6 +289,17 @@ class QwenRunner:
         shape = (len(self.layers), batch, self.n_kv, max_len, self.head_dim)
         self.k_cache = torch.zeros(shape, device=dev, dtype=self.embed.dtype)
         self.v_cache = torch.zeros(shape, device=dev, dtype=self.embed.dtype)
+
+    def with_batch(self, batch: int) -> "QwenRunner":
+        """A runner for another batch size that shares this one's weights (new, empty KV caches)."""
+        import copy
+
+        r = copy.copy(self)
+        r.batch = batch
+        shape = (len(self.layers), batch, self.n_kv, self.max_len, self.head_dim)
+        r.k_cache = torch.zeros(shape, device=self.k_cache.device, dtype=self.k_cache.dtype)
+        r.v_cache = torch.zeros(shape, device=self.v_cache.device, dtype=self.v_cache.dtype)
+        return r
 
     def _plan_l2_prefetch(self):
         """Each projection's launch pulls the weights of the projection two launches ahead in the
@@ -294,6 +331,21 @@ class QwenRunner:
         return {"linear_layers": layers, "embed": nbytes(self.embed), "lm_head_read": head,
                 "lm_head_quantized": self.head_q is not None,
                 "lm_head_shared_with_embed": self.lm_head.data_ptr() == self.embed.data_ptr()}
+
+    def _row_linear(self, x, p: Linear):
+        """o_proj / down: the plain projection, or under tensor parallelism this rank's K-shard
+        reduced over the group (fused NVLink allreduce or NCCL)."""
+        if self.tp is None:
+            return self.backend.linear(x, p)
+        return self.tp.reduce_linear(self.backend, x, p)
+
+    def greedy(self, logits: torch.Tensor) -> torch.Tensor:
+        """Greedy next token [B] from forward()'s logits [B, T, V] (this rank's vocabulary shard
+        under tensor parallelism: the argmax then spans all ranks)."""
+        last = logits[:, -1]
+        if self.tp is None:
+            return last.argmax(-1)
+        return self.tp.argmax(last, self.vocab_start)
 
     def _rope(self, x, cos, sin):
         x1, x2 = x[..., : self.head_dim // 2], x[..., self.head_dim // 2:]
@@ -342,9 +394,9 @@ class QwenRunner:
                     qkv, residual = be.norm_linear(h, L.ln1, eps, residual, L.qkv)
                 attn = decode_attention(qkv, self.k_cache[i], self.v_cache[i], pos, cos, sin,
                                         self.n_heads, self.n_kv, static_cache=True)
-                o = be.linear(attn, L.o)
+                o = self._row_linear(attn, L.o)
                 act, residual = be.norm_gate_up_act(o, L.ln2, eps, residual, L.gate_up)
-                h = be.linear(act, L.down)
+                h = self._row_linear(act, L.down)
                 continue
             if h is None:
                 h = be.norm(x, L.ln1, eps)
@@ -352,9 +404,9 @@ class QwenRunner:
                 h, residual = be.norm(h, L.ln1, eps, residual=residual)
             qkv = be.linear(h, L.qkv)
             attn = self._attention_sdpa(i, qkv, pos, cos, sin, mask, B, T)
-            o = be.linear(attn, L.o)
+            o = self._row_linear(attn, L.o)
             h, residual = be.norm(o, L.ln2, eps, residual=residual)
-            h = be.linear(be.gate_up_act(h, L.gate_up), L.down)
+            h = self._row_linear(be.gate_up_act(h, L.gate_up), L.down)
         h, _ = be.norm(h, self.final_norm, eps, residual=residual)
         if not all_logits:
             h = h[:, -1:]

@@ -39,7 +39,7 @@ class GraphDecoder:
 
     def _step(self):
         logits = self.r.forward(self.tok, self.pos)
-        nxt = logits[:, -1].argmax(-1)
+        nxt = self.r.greedy(logits)
         self.out.index_copy_(1, self.pos, nxt.view(-1, 1))
         self.tok.copy_(nxt.view(-1, 1))
         self.pos.add_(1)
@@ -48,7 +48,7 @@ class GraphDecoder:
         """ids [B, P] on the device. Fills the cache, sets the first generated token."""
         P = ids.shape[1]
         logits = self.r.forward(ids, torch.arange(P, device=ids.device))
-        self.tok.copy_(logits[:, -1].argmax(-1).view(-1, 1))
+        self.tok.copy_(self.r.greedy(logits).view(-1, 1))
         self.pos.fill_(P)
         self.out.zero_()
         self.out[:, P - 1] = self.tok.view(-1)  # position P-1 holds the first new token

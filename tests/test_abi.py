@@ -37,7 +37,7 @@ def test_library_loads_and_reports_version():
     from kernels import _lib
 
     h = _lib.lib()
-    assert h.dk_abi_version() == 2
+    assert h.dk_abi_version() == 3
     for name in declared_symbols():
         assert hasattr(h, name)
     # every declared symbol has a ctypes signature in the Python mirror
@@ -66,3 +66,24 @@ def test_package_has_no_oracle_or_cpu_path():
     for py in pkg.rglob("*.py"):
         text = py.read_text()
         assert "import oracle" not in text and "from oracle" not in text, py
+
+
+def test_tp_entry_points_validate_without_a_gpu():
+    """The tensor-parallel set-up calls check their arguments before touching the device."""
+    import ctypes
+
+    from kernels import _lib
+
+    h = _lib.lib()
+    n = ctypes.c_uint64(0)
+    assert h.dk_tp_buffer_bytes(2, 16, 3584, ctypes.byref(n)) == 0
+    assert n.value == 256 + 8 * 1024 * 8 + 2 * 2 * 16 * 3584 * 4
+    assert h.dk_tp_buffer_bytes(9, 16, 3584, ctypes.byref(n)) == -1
+    assert h.dk_tp_buffer_bytes(2, 17, 3584, ctypes.byref(n)) == -1
+    assert h.dk_tp_buffer_bytes(2, 16, 3585, ctypes.byref(n)) == -1
+    comm = ctypes.c_void_p()
+    bufs = (ctypes.c_void_p * 2)(None, None)
+    assert h.dk_tp_comm_create(ctypes.byref(comm), 0, 2, bufs, 16, 3584) == -1
+    assert b"NULL" in h.dk_last_error()
+    rc = h.dk_w4a16_matmul_allreduce(None, 128, None, None, None, None, None, 8, 1, 8, 128, 128, None, None, None)
+    assert rc == -1

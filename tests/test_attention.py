@@ -25,6 +25,9 @@ def _case(B, nq, nkv, max_len, pos, seed=0, hd=128, theta=1e6):
     (1, 12, 2, 2048, 0, 0), (1, 12, 2, 2048, 511, 0), (1, 12, 2, 2048, 767, 0), (1, 12, 2, 2048, 2047, 0),
     (16, 12, 2, 1024, 300, 0), (1, 28, 4, 1024, 777, 0), (2, 8, 8, 64, 33, 3), (1, 4, 2, 96, 95, 1),
     (3, 12, 2, 512, 200, 8),
+    # tensor-parallel shards of Qwen2.5-7B (28 query / 4 kv heads): 14/2 at 2 ranks, 7/1 at 4, 3/1 and 4/1 at 8
+    (1, 14, 2, 2048, 1100, 0), (8, 7, 1, 2048, 1030, 0), (1, 3, 1, 2048, 1024, 0), (32, 4, 1, 2048, 1025, 0),
+    (2, 5, 1, 128, 70, 0),
 ])
 def test_decode_attention(B, nq, nkv, max_len, pos, splits):
     from kernels.attention import decode_attention
