@@ -50,6 +50,9 @@ typedef struct CUstream_st* dk_stream_t; /* same type as cudaStream_t */
                                     reference's dequantize-then-matmul ((q - z) * s in fp16) instead
                                     of the default factored form s * sum(x * (q - z)) in fp32 (the
                                     reference's FACTORED path, kernels/w4a16.py:116-119) */
+#define DK_FLAG_GEMV 8           /* run M in launches of up to 16 rows of the decode GEMV even where
+                                    the tensor-core GEMM would take the shape (M >= 128, N >= 128);
+                                    for tests and comparisons */
 
 #define DK_MAX_L2_PREFETCH 6
 
@@ -97,7 +100,10 @@ int dk_dequantize_int4(const int32_t* qweight, const void* scales, const void* z
 /* ---- W4A16 matmul: kernels/w4a16.py, kernels/cuda/w4a16_decode.cu ---------------------- */
 /* w4a16_matmul (kernels/w4a16.py:301-330) and w4a16_decode (kernels/cuda/w4a16_decode.cu:136-181):
  * y[M, N] fp16 = x[M, K] fp16 @ dequant(W).T (+ bias[N]), fp32 accumulation.
- * x rows have stride ldx, y rows stride ldy (elements). bias may be NULL. cfg may be NULL. */
+ * x rows have stride ldx, y rows stride ldy (elements). bias may be NULL. cfg may be NULL.
+ * M <= 16 rows per launch run the decode GEMV; M >= 128 and N >= 128 (aligned, group_size 128) run the
+ * tcgen05 tensor-core GEMM (kernels/w4a16.py:31-97), which always rounds every dequantized weight to
+ * fp16 like the reference's dequantize-then-matmul; other shapes loop the GEMV over 16-row blocks. */
 int dk_w4a16_matmul(const void* x, int64_t ldx, const int32_t* qweight, const void* scales,
                     const void* zeros, const void* bias, void* y, int64_t ldy, int64_t M,
                     int64_t N, int64_t K, int64_t group_size, const dk_matmul_config* cfg,
@@ -180,10 +186,11 @@ int dk_decode_attention(const void* qkv, void* k_cache, void* v_cache, const int
  * No reference counterpart: the reference runs on one GPU (README.md:249). These entry points serve
  * the tensor-parallel runner (column-sharded qkv/gate_up/lm_head, row-sharded o_proj/down), one
  * process per GPU of one node. Each rank owns one exchange buffer, allocated once at set-up and
- * mapped into every peer with CUDA IPC; a row-sharded projection then pushes its fp32 partial sums
- * into every peer's buffer over NVLink from the GEMV epilogue and sums the ranks' partials of its own
- * output columns in rank order, so the matmul and the allreduce are one kernel and every rank ends
- * with the same bits. No TMA multicast is used on peer memory. */
+ * mapped into every peer with CUDA IPC; a row-sharded projection then pushes its fp32 partial sums,
+ * each tagged with the launch's epoch in the same 8-byte store, into every peer's buffer over NVLink
+ * from the GEMV epilogue, and sums the ranks' partials of its own output columns in rank order once
+ * their tags match, so the matmul and the allreduce are one kernel and every rank ends with the same
+ * bits. No TMA multicast is used on peer memory. */
 #define DK_TP_MAX_WORLD 8
 #define DK_TP_IPC_HANDLE_BYTES 64 /* sizeof(cudaIpcMemHandle_t) */
 

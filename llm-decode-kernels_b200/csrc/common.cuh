@@ -176,33 +176,40 @@ inline L2Prefetch l2_prefetch_from(const dk_matmul_config* cfg) {
 
 // ------------------------------------------------------------------- tensor-parallel exchange
 // One rank's exchange buffer (allocated by dk_tp_buffer_alloc, zeroed, mapped into every peer):
-//   [0, 256)                 header: launch epoch (u64), CTA arrival count (u32)
-//   [256, 256 + kTpFlagBytes) flags[src rank][CTA] (u64): the epoch at which CTA `CTA` of rank `src`
-//                            finished pushing its partial sums into this buffer
-//   [kTpDataOff, ...)        data[slot 0..1][src rank][max_m][max_n] fp32 partial sums
-constexpr int kTpMaxCtas = 1024;
+//   [0, 256)           header: launch epoch (u64), CTA arrival count (u32)
+//   [256, ...)         cells[slot 0..1][src rank][max_m][max_n]: 8 bytes each, {fp32 partial sum bits,
+//                      low 32 bits of the epoch of the launch that wrote it}
+// A receiver polls a cell until its epoch word matches: value and epoch travel in one 8-byte store,
+// so no fence or separate flag is needed (the "LL" idea of NCCL's low-latency protocol).
 constexpr size_t kTpHeaderBytes = 256;
-constexpr size_t kTpFlagBytes = static_cast<size_t>(DK_TP_MAX_WORLD) * kTpMaxCtas * 8;
-constexpr size_t kTpDataOff = kTpHeaderBytes + kTpFlagBytes;
 
 // What a fused-allreduce launch needs; world == 0 means a plain launch.
 struct TPArgs {
-  float* data[DK_TP_MAX_WORLD];                 // data region of each rank's buffer (peer mappings)
-  unsigned long long* flags[DK_TP_MAX_WORLD];   // flag region of each rank's buffer
-  unsigned long long* epoch;                    // this rank's header
+  uint32_t* cells[DK_TP_MAX_WORLD];  // cell region of each rank's buffer (peer mappings)
+  unsigned long long* epoch;         // this rank's header
   unsigned int* arrive;
   int rank, world, max_m, max_n;
 };
 
-__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+__device__ __forceinline__ void st_volatile_v4(uint32_t* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
 }
-__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+__device__ __forceinline__ void st_volatile_v2(uint32_t* p, uint32_t a, uint32_t b) {
+  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(a), "r"(b) : "memory");
+}
+__device__ __forceinline__ uint4 ld_volatile_v4(const uint32_t* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
   return v;
 }
-__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ uint2 ld_volatile_v2(const uint32_t* p) {
+  uint2 v;
+  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+  return v;
+}
 
 // ------------------------------------------------------------- programmatic dependent launch
 // Wait until the preceding kernel on the stream (if it was launched as our PDL primary) has

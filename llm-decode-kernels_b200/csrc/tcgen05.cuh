@@ -1,0 +1,89 @@
+// 5th-generation tensor-core helpers (sm_100a): tcgen05.mma with operands in shared memory described
+// by matrix descriptors, the fp32 accumulator in tensor memory (TMEM), and the TMEM allocator.
+//
+// Written from the PTX ISA's description of tcgen05 (instruction descriptor, shared-memory matrix
+// descriptor, 32x32b TMEM loads). Only the forms the GEMM kernels here use: cta_group::1,
+// kind::f16 with fp16 A and B (both operands the same type), fp32 accumulation, K-major operands in
+// the 128-byte-swizzled canonical layout.
+#pragma once
+
+#include "common.cuh"
+
+namespace dk {
+namespace tc {
+
+// Instruction descriptor of tcgen05.mma.kind::f16: D fp32 (bits 4-5 = 1), A and B fp16 (bits 7-9,
+// 10-12 = 0), both K-major (bits 15, 16 = 0), N >> 3 in bits 17-22, M >> 4 in bits 24-28.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
+  return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// Shared-memory matrix descriptor for a K-major operand in the 128-byte swizzle layout: rows of 128
+// bytes (64 fp16 along K), 8-row swizzle atoms of 1024 bytes stacked along M/N (stride byte offset
+// 1024), 16-byte chunk c of row r stored at chunk c ^ (r % 8) - the pattern a TMA load with
+// CU_TENSOR_MAP_SWIZZLE_128B writes. Start address >> 4 in bits 0-13, leading byte offset (unused
+// for swizzled K-major; 16 bytes) in 16-29, stride byte offset >> 4 in 32-45, version 1 in 46-47,
+// layout type 2 (128-byte swizzle) in 61-63. Atoms must be 1024-byte aligned; the start address may
+// move along K inside an atom in 32-byte steps (one K=16 slice of fp16).
+__device__ __forceinline__ uint64_t sdesc_k_sw128(uint32_t smem_byte_addr) {
+  return static_cast<uint64_t>((smem_byte_addr >> 4) & 0x3FFF) | (static_cast<uint64_t>(16 >> 4) << 16) |
+         (static_cast<uint64_t>(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T for one K = 16 slice; `accumulate` = 0 overwrites D.
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive (once) on an mbarrier of this CTA when every tcgen05 operation this thread issued so far
+// has completed.
+__device__ __forceinline__ void commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+// Allocate `ncols` TMEM columns (a power of two >= 32) for this CTA; a whole warp executes it and
+// the base address lands in shared memory at `dst`.
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Generic-proxy writes to shared memory become visible to the async proxy (tcgen05.mma operand reads).
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// 32 consecutive fp32 columns of one TMEM lane per thread: the warp reads lanes [32*(warp%4), +32)
+// (address lane field = that base) and columns col..col+31.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
+      "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");  // the wait is in the same statement: no use of r[] can move above it
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+}  // namespace tc
+}  // namespace dk

@@ -2,8 +2,9 @@
 // IPC, and the host-side communicator that the fused row-sharded GEMV + allreduce launches read.
 //
 // No reference counterpart: the reference is single-GPU (README.md:249). The data path lives in
-// w4a16.cu (the GEMV epilogue pushes fp32 partial sums into every rank's buffer and sums the ranks'
-// partials of its own columns); this file only allocates, maps and describes the buffers. Every
+// w4a16.cu (the GEMV epilogue pushes fp32 partial sums, each tagged with the launch's epoch, into
+// every rank's buffer and sums the ranks' partials of its own columns); this file only allocates,
+// maps and describes the buffers. Every
 // function here is set-up code: it may allocate, synchronize and call the driver, and must not be
 // called inside a CUDA-graph capture.
 #include <cstring>
@@ -21,11 +22,8 @@ namespace dk {
 bool tp_args_from(const dk_tp_comm* c, TPArgs* a) {
   if (c == nullptr) return false;
   std::memset(a, 0, sizeof(*a));
-  for (int q = 0; q < c->world; ++q) {
-    char* base = static_cast<char*>(c->bufs[q]);
-    a->data[q] = reinterpret_cast<float*>(base + kTpDataOff);
-    a->flags[q] = reinterpret_cast<unsigned long long*>(base + kTpHeaderBytes);
-  }
+  for (int q = 0; q < c->world; ++q)
+    a->cells[q] = reinterpret_cast<uint32_t*>(static_cast<char*>(c->bufs[q]) + kTpHeaderBytes);
   char* own = static_cast<char*>(c->bufs[c->rank]);
   a->epoch = reinterpret_cast<unsigned long long*>(own);
   a->arrive = reinterpret_cast<unsigned int*>(own + 8);
@@ -51,13 +49,13 @@ int dk_tp_buffer_bytes(int32_t world, int64_t max_m, int64_t max_n, uint64_t* by
     return set_error(DK_ERR_INVALID,
                      "dk_tp_buffer_bytes: need 1 <= world <= %d, 1 <= max_m <= 16, max_n a positive multiple of 8",
                      DK_TP_MAX_WORLD);
-  *bytes = kTpDataOff + 2ull * static_cast<uint64_t>(world) * max_m * max_n * sizeof(float);
+  *bytes = kTpHeaderBytes + 2ull * static_cast<uint64_t>(world) * max_m * max_n * 8;
   return DK_OK;
 }
 
 int dk_tp_buffer_alloc(uint64_t bytes, void** ptr, void* ipc_handle) {
   using namespace dk;
-  if (ptr == nullptr || ipc_handle == nullptr || bytes < kTpDataOff)
+  if (ptr == nullptr || ipc_handle == nullptr || bytes < kTpHeaderBytes)
     return set_error(DK_ERR_INVALID, "dk_tp_buffer_alloc: NULL argument or buffer smaller than its header");
   static_assert(sizeof(cudaIpcMemHandle_t) == DK_TP_IPC_HANDLE_BYTES, "IPC handle size");
   void* p = nullptr;

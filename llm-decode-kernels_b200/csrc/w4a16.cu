@@ -208,22 +208,73 @@ __device__ __forceinline__ void consume_chunk_stage(const uint8_t* __restrict__ 
 
 // ------------------------------------------------------------------ fused allreduce (row sharding)
 // A row-sharded launch computes this rank's partial sums of y. Instead of storing them, the
-// epilogue pushes them (fp32, no bias) into slot (epoch & 1), row `rank`, of every rank's exchange
-// buffer over NVLink; tp_finish then publishes this CTA's flag in every buffer, waits for the flags
-// of the same CTA on the other ranks (each rank launches the same grid, so CTA i covers the same
-// columns everywhere), and adds the ranks' partials of its own columns in rank order. Two slots
-// suffice: a rank starts launch e + 2 only after its launch e + 1 finished, and every CTA of that
-// launch waited for all ranks' launch e + 1, which start after their launch e finished reading.
-__device__ __forceinline__ float* tp_cell(const TPArgs& tp, int q, unsigned long long ep, int src, int m, int n) {
-  return tp.data[q] + ((static_cast<size_t>(ep & 1) * tp.world + src) * tp.max_m + m) * static_cast<size_t>(tp.max_n) + n;
+// epilogue pushes each one, tagged with the low 32 bits of the launch's epoch, into slot
+// (epoch & 1), row `rank`, of every rank's exchange buffer over NVLink (one 8-byte {value, epoch}
+// store per value, so a value is valid exactly when its tag matches: no fence, no flag). tp_finish
+// then polls the cells of this CTA's own columns from every rank (each rank launches the same grid,
+// so CTA i covers the same columns everywhere) and adds them in rank order. Two slots suffice: a rank
+// starts launch e + 2 only after its launch e + 1 finished, and every CTA of that launch read all
+// ranks' launch e + 1 values, which they wrote after their launch e had finished reading.
+__device__ __forceinline__ uint32_t* tp_cell(const TPArgs& tp, int q, unsigned long long ep, int src, int m, int n) {
+  return tp.cells[q] +
+         2 * (((static_cast<size_t>(ep & 1) * tp.world + src) * tp.max_m + m) * static_cast<size_t>(tp.max_n) + n);
 }
 
 __device__ __forceinline__ void tp_push(const TPArgs& tp, unsigned long long ep, int m, int n, float v) {
-  for (int q = 0; q < tp.world; ++q) *tp_cell(tp, q, ep, tp.rank, m, n) = v;
+  const uint32_t tag = static_cast<uint32_t>(ep);
+  for (int q = 0; q < tp.world; ++q) st_volatile_v2(tp_cell(tp, q, ep, tp.rank, m, n), __float_as_uint(v), tag);
 }
 
 __device__ __forceinline__ void tp_push4(const TPArgs& tp, unsigned long long ep, int m, int n, float4 v) {
-  for (int q = 0; q < tp.world; ++q) *reinterpret_cast<float4*>(tp_cell(tp, q, ep, tp.rank, m, n)) = v;
+  const uint32_t tag = static_cast<uint32_t>(ep);
+  for (int q = 0; q < tp.world; ++q) {
+    uint32_t* c = tp_cell(tp, q, ep, tp.rank, m, n);  // n % 4 == 0: 32-byte aligned
+    st_volatile_v4(c, __float_as_uint(v.x), tag, __float_as_uint(v.y), tag);
+    st_volatile_v4(c + 4, __float_as_uint(v.z), tag, __float_as_uint(v.w), tag);
+  }
+}
+
+// Bounded polling: false once the CTA gave up (another thread timed out) or this wait passed the
+// limit (then it records the device error and makes the CTA give up).
+__device__ __forceinline__ bool tp_keep_waiting(int it, uint64_t& t0, volatile int* give_up, int* err) {
+  if (*give_up) return false;
+  if (it == 0) {
+    t0 = globaltimer_ns();
+  } else if ((it & 63) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+    record_device_error(err, DK_DEVERR_TP_WAIT);
+    *give_up = 1;
+    return false;
+  }
+  return true;
+}
+
+// The four values of cells c[0..3] (32 bytes) once all four carry `tag`.
+__device__ __forceinline__ bool tp_poll4(const uint32_t* c, uint32_t tag, float (&out)[4], volatile int* give_up,
+                                         int* err) {
+  uint64_t t0 = 0;
+  for (int it = 0;; ++it) {
+    const uint4 a = ld_volatile_v4(c), b = ld_volatile_v4(c + 4);
+    if (a.y == tag && a.w == tag && b.y == tag && b.w == tag) {
+      out[0] = __uint_as_float(a.x);
+      out[1] = __uint_as_float(a.z);
+      out[2] = __uint_as_float(b.x);
+      out[3] = __uint_as_float(b.z);
+      return true;
+    }
+    if (!tp_keep_waiting(it, t0, give_up, err)) return false;
+  }
+}
+
+__device__ __forceinline__ bool tp_poll1(const uint32_t* c, uint32_t tag, float& out, volatile int* give_up, int* err) {
+  uint64_t t0 = 0;
+  for (int it = 0;; ++it) {
+    const uint2 a = ld_volatile_v2(c);
+    if (a.y == tag) {
+      out = __uint_as_float(a.x);
+      return true;
+    }
+    if (!tp_keep_waiting(it, t0, give_up, err)) return false;
+  }
 }
 
 // Called by every thread of the CTA after its last push. Columns: [c_begin*32, min(c_end*32, N)) with
@@ -231,49 +282,30 @@ __device__ __forceinline__ void tp_push4(const TPArgs& tp, unsigned long long ep
 __device__ void tp_finish(const GemvParams& p, unsigned long long ep, bool ok, int c_begin, int c_end, int upt,
                           int S, int crank) {
   const TPArgs& tp = p.tp;
-  const int cta = blockIdx.x + gridDim.x * blockIdx.y;
-  __syncthreads();  // every push of this CTA has been issued
-  if (threadIdx.x == 0) {
-    fence_acq_rel_sys();  // the CTA's pushes (ordered before this by the barrier) precede the flags
-    for (int q = 0; q < tp.world; ++q) st_release_sys_u64(tp.flags[q] + tp.rank * kTpMaxCtas + cta, ep);
-  }
-  bool bad = false;
-  if (threadIdx.x < tp.world) {
-    const unsigned long long* f = tp.flags[tp.rank] + threadIdx.x * kTpMaxCtas + cta;
-    if (ld_acquire_sys_u64(f) != ep) {
-      const uint64_t t0 = globaltimer_ns();
-      while (ld_acquire_sys_u64(f) != ep) {
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
-          record_device_error(p.err, DK_DEVERR_TP_WAIT);
-          bad = true;
-          break;
-        }
-      }
-    }
-  }
-  bad = __syncthreads_or(bad);
-  if (ok && !bad) {
-    const float* own = tp.data[tp.rank] + static_cast<size_t>(ep & 1) * tp.world * tp.max_m * static_cast<size_t>(tp.max_n);
-    const size_t row_stride = static_cast<size_t>(tp.max_m) * tp.max_n;  // between source ranks
+  const uint32_t tag = static_cast<uint32_t>(ep);
+  __shared__ int s_give_up;
+  if (threadIdx.x == 0) s_give_up = ok ? 0 : 1;
+  __syncthreads();
+  if (ok) {
+    volatile int* give_up = &s_give_up;
     if (S == 1) {
       const int n_lo = c_begin * 32, n_hi = min(c_end * 32, p.N);
       const int nq = (n_hi - n_lo) / 4;  // N % 8 == 0 on this path
       for (int e = threadIdx.x; e < p.M * nq; e += blockDim.x) {
         const int m = e / nq, n = n_lo + 4 * (e % nq);
-        const float* src = own + static_cast<size_t>(m) * tp.max_n + n;
-        float4 a = __ldcg(reinterpret_cast<const float4*>(src));
-        for (int q = 1; q < tp.world; ++q) {
-          const float4 b = __ldcg(reinterpret_cast<const float4*>(src + q * row_stride));
-          a.x += b.x;
-          a.y += b.y;
-          a.z += b.z;
-          a.w += b.w;
+        float sum[4] = {0.f, 0.f, 0.f, 0.f};
+        bool good = true;
+        for (int q = 0; q < tp.world && good; ++q) {
+          float v[4];
+          good = tp_poll4(tp_cell(tp, tp.rank, ep, q, m, n), tag, v, give_up, p.err);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) sum[c] += v[c];
         }
-        float v[4] = {a.x, a.y, a.z, a.w};
+        if (!good) continue;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          if (p.bias != nullptr) v[c] += __half2float(p.bias[n + c]);
-          p.y[m * p.ldy + n + c] = __float2half_rn(v[c]);
+          if (p.bias != nullptr) sum[c] += __half2float(p.bias[n + c]);
+          p.y[m * p.ldy + n + c] = __float2half_rn(sum[c]);
         }
       }
     } else {
@@ -282,14 +314,20 @@ __device__ void tp_finish(const GemvParams& p, unsigned long long ep, bool ok, i
         if (e % S != crank) continue;
         const int m = e / ncols, n = c_begin * 32 + e % ncols;
         if (n >= p.N) continue;
-        const float* src = own + static_cast<size_t>(m) * tp.max_n + n;
-        float a = __ldcg(src);
-        for (int q = 1; q < tp.world; ++q) a += __ldcg(src + q * row_stride);
+        float a = 0.f;
+        bool good = true;
+        for (int q = 0; q < tp.world && good; ++q) {
+          float v = 0.f;
+          good = tp_poll1(tp_cell(tp, tp.rank, ep, q, m, n), tag, v, give_up, p.err);
+          a += v;
+        }
+        if (!good) continue;
         if (p.bias != nullptr) a += __half2float(p.bias[n]);
         p.y[m * p.ldy + n] = __float2half_rn(a);
       }
     }
   }
+  __syncthreads();
   if (threadIdx.x == 0 && atomicAdd(tp.arrive, 1u) == gridDim.x * gridDim.y - 1) {
     // last CTA of the launch: the next launch on this communicator uses epoch ep + 1
     *tp.arrive = 0;
@@ -837,9 +875,8 @@ int run_fast(const void* x, int64_t ldx, const int32_t* qweight, const void* sca
     const int mc = static_cast<int>(std::min<int64_t>(rows_per_launch, M - m0));
     const Choice c = choose(mc, units, static_cast<int>(K), swiglu_i > 0, cfg);
     if (c.cw == 0) return set_error(DK_ERR_UNSUPPORTED, "w4a16: no tile fits (M=%d, K=%lld)", mc, (long long)K);
-    if (tp != nullptr && (mc > tp->max_m || c.nctas * c.split > kTpMaxCtas))
-      return set_error(DK_ERR_UNSUPPORTED, "w4a16_matmul_allreduce: %d rows or %d CTAs exceed the communicator",
-                       mc, c.nctas * c.split);
+    if (tp != nullptr && mc > tp->max_m)
+      return set_error(DK_ERR_UNSUPPORTED, "w4a16_matmul_allreduce: %d rows exceed the communicator", mc);
     GemvParams p;
     p.x = static_cast<const __half*>(x) + m0 * ldx;
     p.ldx = ldx;
@@ -898,6 +935,13 @@ bool fast_ok(const void* x, int64_t ldx, const int32_t* qweight, const void* sca
 }  // namespace
 }  // namespace dk
 
+namespace dk {
+bool gemm_tc_ok(const void* x, int64_t ldx, const void* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
+                int64_t group_size);
+int launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const void* zeros,
+                   const void* bias, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, cudaStream_t st);
+}  // namespace dk
+
 extern "C" int dk_w4a16_matmul(const void* x, int64_t ldx, const int32_t* qweight, const void* scales,
                                const void* zeros, const void* bias, void* y, int64_t ldy, int64_t M,
                                int64_t N, int64_t K, int64_t group_size, const dk_matmul_config* cfg,
@@ -918,6 +962,8 @@ extern "C" int dk_w4a16_matmul(const void* x, int64_t ldx, const int32_t* qweigh
     if (e != cudaSuccess) return set_error(DK_ERR_CUDA, "w4a16 generic launch: %s", cudaGetErrorString(e));
     return DK_OK;
   }
+  if (!(flags & DK_FLAG_GEMV) && gemm_tc_ok(x, ldx, y, ldy, M, N, K, group_size))
+    return launch_gemm_tc(x, ldx, qweight, scales, zeros, bias, y, ldy, M, N, K, st);
   return run_fast(x, ldx, qweight, scales, zeros, bias, y, ldy, M, N, K, group_size, cfg, 0, NormArgs(), st);
 }
 
@@ -994,3 +1040,4 @@ extern "C" int dk_w4a16_matmul_allreduce(const void* x, int64_t ldx, const int32
   return run_fast(x, ldx, qweight, scales, zeros, bias, y, ldy, M, N, K, group_size, cfg, 0, NormArgs(),
                   reinterpret_cast<cudaStream_t>(stream), &tp);
 }
+

@@ -1,0 +1,283 @@
+// W4A16 GEMM for prefill-sized inputs (M >= 128 rows) on the 5th-generation tensor cores:
+// y[M, N] = x[M, K] @ dequant(W).T (+ bias), fp16 operands, fp32 accumulation in tensor memory.
+//
+// Replaces the reference's Triton tensor-core tile kernel for large M (kernels/w4a16.py:31-97,
+// the `direct` path of w4a16_matmul) with tcgen05.mma. One CTA computes a 128 x 128 tile of y:
+// * warp 0 (one lane) streams, per 64-wide K step, the x tile [128 rows x 64] with TMA into the
+//   128-byte-swizzled K-major layout, and the packed weights of the tile (8 rows of qweight x 128
+//   columns, int32) plus the step's scale and zero rows, into a 4-stage ring;
+// * warps 2-5 dequantize: thread t owns output column n0 + t and turns its 8 packed words (64 K
+//   values) into one 128-byte row of the fp16 B tile, (q - z) * s with the reference's rounding
+//   (kernels/reference.py:35: q - z is exact in fp16, one fp16 multiply by s), written straight
+//   into the swizzled K-major layout that tcgen05 reads (16-byte chunk c of row t at c ^ (t % 8));
+// * warp 1 allocates 128 TMEM columns (the 128 x 128 fp32 accumulator) and one lane issues four
+//   K = 16 tcgen05.mma per step, releasing each stage with tcgen05.commit;
+// * warps 2-5 then read the accumulator back (tcgen05.ld, one 32-lane quarter of TMEM per warp),
+//   add the bias, round to fp16 and store.
+// Nibble pairs become fp16 with the LOP3 "magic number" conversion (0x6400 exponent; Kim et al.,
+// "Who Says Elephants Can't Run?"), after a PRMT that puts K values 2j and 2j+1 of a word into the
+// low nibble of byte 0 and the high nibble of byte 2; one fp16x2 FMA with (1, 1/16) and
+// (-(1024 + z), -(64 + z)) leaves (q_2j - z, q_2j+1 - z) exactly.
+// Every mbarrier wait is bounded; a CTA whose wait gives up records a device error, waits (bounded)
+// for its in-flight copies and MMAs, frees its TMEM and skips its stores.
+#include <cstdio>
+#include <mutex>
+
+#include "common.cuh"
+#include "tcgen05.cuh"
+
+namespace dk {
+namespace {
+
+constexpr int kBM = 128, kBN = 128, kBK = 64;
+constexpr int kStages = 4;
+constexpr int kThreads = 192;                  // warp 0 TMA, warp 1 TMEM + MMA, warps 2-5 dequant + epilogue
+constexpr int kABytes = kBM * kBK * 2;         // 16 KB x tile
+constexpr int kBBytes = kBN * kBK * 2;         // 16 KB dequantized weight tile
+constexpr int kWBytes = (kBK / 8) * kBN * 4;   // 4 KB packed weights
+constexpr int kSZBytes = kBN * 2;              // one scale (or zero) row
+constexpr uint32_t kStageTx = kABytes + kWBytes + 2 * kSZBytes;
+constexpr int kOffB = kStages * kABytes;
+constexpr int kOffW = kOffB + kStages * kBBytes;
+constexpr int kOffS = kOffW + kStages * kWBytes;
+constexpr int kOffZ = kOffS + kStages * kSZBytes;
+constexpr int kOffBar = kOffZ + kStages * kSZBytes;
+constexpr int kSmemBytes = kOffBar + (3 * kStages + 1) * 8 + 16 + 1024;  // + barriers, TMEM slot, alignment
+
+struct GemmParams {
+  __half* y;
+  int64_t ldy;
+  const __half* bias;
+  int M, N, K;
+  int ktiles;
+  int* err;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    w4a16_gemm_tc_kernel(const __grid_constant__ CUtensorMap mx, const __grid_constant__ CUtensorMap mq,
+                         const __grid_constant__ CUtensorMap ms, const __grid_constant__ CUtensorMap mz,
+                         const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kOffB;
+  uint8_t* sW = smem + kOffW;
+  uint8_t* sS = smem + kOffS;
+  uint8_t* sZ = smem + kOffZ;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* deq = full + kStages;
+  uint64_t* empty = deq + kStages;
+  uint64_t* done = empty + kStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  __shared__ int s_fail;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * kBN, m0 = blockIdx.y * kBM;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&deq[s], 128);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    s_fail = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, kBN);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  pdl_trigger();
+  pdl_wait();  // x comes from the previous kernel; y may alias memory it still reads
+
+  bool ok = true;
+  int issued = 0;  // producer: K steps whose copies were issued
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tensormap(&mx);
+      prefetch_tensormap(&mq);
+      prefetch_tensormap(&ms);
+      prefetch_tensormap(&mz);
+      for (int kt = 0; kt < p.ktiles; ++kt) {
+        const int s = kt % kStages;
+        if (kt >= kStages && !mbar_wait(&empty[s], ((kt / kStages) - 1) & 1, p.err, DK_DEVERR_WAIT_EMPTY)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[s], kStageTx);
+        tma_load_2d(sA + s * kABytes, &mx, kt * kBK, m0, &full[s]);
+        tma_load_2d(sW + s * kWBytes, &mq, n0, kt * (kBK / 8), &full[s]);
+        tma_load_2d(sS + s * kSZBytes, &ms, n0, (kt * kBK) / 128, &full[s]);
+        tma_load_2d(sZ + s * kSZBytes, &mz, n0, (kt * kBK) / 128, &full[s]);
+        issued = kt + 1;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = tc::idesc_f16_f32(kBM, kBN);
+      for (int kt = 0; kt < p.ktiles; ++kt) {
+        const int s = kt % kStages;
+        const uint32_t par = (kt / kStages) & 1;
+        if (!mbar_wait(&full[s], par, p.err, DK_DEVERR_WAIT_FULL) ||
+            !mbar_wait(&deq[s], par, p.err, DK_DEVERR_WAIT_FULL)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+        const uint32_t a0 = smem_addr(sA + s * kABytes), b0 = smem_addr(sB + s * kBBytes);
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk)
+          tc::mma_f16(tmem, tc::sdesc_k_sw128(a0 + 32 * kk), tc::sdesc_k_sw128(b0 + 32 * kk), idesc,
+                      (kt | kk) != 0 ? 1u : 0u);
+        tc::commit(&empty[s]);  // the stage is free once these MMAs have read it
+      }
+      tc::commit(done);  // the accumulator is final once every MMA issued above has completed
+    }
+  } else {
+    // ------------------------------------------------------------------ dequantization (warps 2-5)
+    const int t = threadIdx.x - 64;  // output column n0 + t, row t of the B tile
+    const uint32_t mul2 = 0x2C003C00u;  // (1.0, 1/16)
+    for (int kt = 0; kt < p.ktiles; ++kt) {
+      const int s = kt % kStages;
+      if (!mbar_wait(&full[s], (kt / kStages) & 1, p.err, DK_DEVERR_WAIT_FULL)) {
+        ok = false;
+        break;
+      }
+      const uint32_t* w = reinterpret_cast<const uint32_t*>(sW + s * kWBytes);
+      const __half sc = reinterpret_cast<const __half*>(sS + s * kSZBytes)[t];
+      const __half zc = reinterpret_cast<const __half*>(sZ + s * kSZBytes)[t];
+      const __half lo = __hneg(__hadd(__float2half_rn(1024.f), zc));  // -(1024 + z), exact
+      const __half hi = __hneg(__hadd(__float2half_rn(64.f), zc));    // -(64 + z), exact
+      const uint32_t add2 = half2_bits(lo, hi);
+      const uint32_t sc2 = half2_bits(sc, sc);
+      uint8_t* brow = sB + s * kBBytes + (t >> 3) * 1024 + (t & 7) * 128;
+#pragma unroll
+      for (int c = 0; c < kBK / 8; ++c) {  // packed row c = K values 8c..8c+7 = 16-byte chunk c of row t
+        const uint32_t word = w[c * kBN + t];
+        uint32_t h[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t v = prmt(word, 0u, static_cast<uint32_t>(j | (4 << 4) | (j << 8) | (4 << 12)));
+          const uint32_t u = lop3_and_or(v, 0x00F0000Fu, 0x64006400u);  // (1024 + q_2j, 1024 + 16 q_2j+1)
+          h[j] = hmul2_rn(hfma2_rn(u, mul2, add2), sc2);                   // ((q - z) * s) for both
+        }
+        *reinterpret_cast<uint4*>(brow + ((c ^ (t & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
+      }
+      tc::fence_proxy_async_smem();  // these generic-proxy writes feed tcgen05.mma (async proxy)
+      mbar_arrive(&deq[s]);
+    }
+  }
+
+  if (!ok) atomicOr(&s_fail, 1);
+  __syncthreads();
+  const bool failed = s_fail != 0;
+  if (failed && warp == 0 && lane == 0) {
+    // wait (bounded) for the copies still in flight before the shared memory goes away
+    const uint64_t t0 = globaltimer_ns();
+    for (int it = issued > kStages ? issued - kStages : 0; it < issued; ++it)
+      while (!mbar_try_wait(&full[it % kStages], (it / kStages) & 1) && globaltimer_ns() - t0 < 500000000ull) {
+      }
+  }
+
+  // ------------------------------------------------------------------ epilogue (warps 2-5)
+  if (warp >= 2) {
+    const bool have = mbar_wait(done, 0, p.err, DK_DEVERR_WAIT_FULL) && !failed;
+    __syncwarp();  // tcgen05.ld is warp-collective: reconverge after the spin above
+    tc::fence_after_sync();
+    const int q = warp & 3;  // this warp's TMEM lane quarter: accumulator rows 32q..32q+31
+    const int row = m0 + 32 * q + lane;
+#pragma unroll 1
+    for (int c0 = 0; c0 < kBN; c0 += 32) {
+      float v[32];
+      tc::tmem_ld32(tmem + (static_cast<uint32_t>(32 * q) << 16) + c0, v);
+      const int n = n0 + c0;
+      if (!have || row >= p.M || n >= p.N) continue;
+      if (p.bias != nullptr) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (n + i < p.N) v[i] += __half2float(p.bias[n + i]);
+      }
+      __half* dst = p.y + static_cast<int64_t>(row) * p.ldy + n;
+      if (n + 32 <= p.N && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          uint4 o;
+          o.x = half2_bits(__float2half_rn(v[i]), __float2half_rn(v[i + 1]));
+          o.y = half2_bits(__float2half_rn(v[i + 2]), __float2half_rn(v[i + 3]));
+          o.z = half2_bits(__float2half_rn(v[i + 4]), __float2half_rn(v[i + 5]));
+          o.w = half2_bits(__float2half_rn(v[i + 6]), __float2half_rn(v[i + 7]));
+          *reinterpret_cast<uint4*>(dst + i) = o;
+        }
+      } else {
+        for (int i = 0; i < 32 && n + i < p.N; ++i) dst[i] = __float2half_rn(v[i]);
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, kBN);
+  }
+}
+
+bool smem_ready() {
+  static std::mutex mu;
+  static bool done[64] = {};
+  static bool okv[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev < 64 && !done[dev]) {
+    okv[dev] = opt_in_dynamic_smem(w4a16_gemm_tc_kernel) >= kSmemBytes;
+    done[dev] = true;
+  }
+  return dev < 64 && okv[dev];
+}
+
+}  // namespace
+
+// True when the tensor-core GEMM takes this shape: M >= 128 and N >= 128 (whole TMA boxes start
+// inside the tensors), 16-byte aligned operands, x rows 16-byte aligned; group_size 128.
+bool gemm_tc_ok(const void* x, int64_t ldx, const void* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
+                int64_t group_size) {
+  return M >= kBM && N >= kBN && N % 8 == 0 && K % 128 == 0 && group_size == 128 && aligned16(x) && ldx % 8 == 0 &&
+         y != nullptr && M <= INT32_MAX && N <= INT32_MAX;
+}
+
+int launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const void* zeros,
+                   const void* bias, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, cudaStream_t st) {
+  if (!smem_ready())
+    return set_error(DK_ERR_UNSUPPORTED, "w4a16 gemm: %d bytes of shared memory do not fit", kSmemBytes);
+  CUtensorMap mx, mq, ms, mz;
+  if (!make_tensor_map_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, K, M, ldx * 2, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_tensor_map_2d(&mq, qweight, CU_TENSOR_MAP_DATA_TYPE_INT32, N, K / 8, N * 4, kBN, kBK / 8,
+                          CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !make_tensor_map_2d(&ms, scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, N, K / 128, N * 2, kBN, 1,
+                          CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !make_tensor_map_2d(&mz, zeros, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, N, K / 128, N * 2, kBN, 1,
+                          CU_TENSOR_MAP_SWIZZLE_NONE))
+    return DK_ERR_CUDA;
+  GemmParams p;
+  p.y = static_cast<__half*>(y);
+  p.ldy = ldy;
+  p.bias = static_cast<const __half*>(bias);
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.ktiles = static_cast<int>(K / kBK);
+  p.err = device_info().err_word;
+  const dim3 grid(static_cast<unsigned>((N + kBN - 1) / kBN), static_cast<unsigned>((M + kBM - 1) / kBM), 1);
+  cudaError_t e = launch(w4a16_gemm_tc_kernel, grid, dim3(kThreads, 1, 1), kSmemBytes, st, pdl_enabled(),
+                         dim3(1, 1, 1), mx, mq, ms, mz, p);
+  if (e != cudaSuccess) return set_error(DK_ERR_CUDA, "w4a16 gemm launch: %s", cudaGetErrorString(e));
+  return DK_OK;
+}
+
+}  // namespace dk

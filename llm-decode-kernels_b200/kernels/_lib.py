@@ -36,6 +36,7 @@ class MatmulConfig(ctypes.Structure):
 FLAG_STATIC_WEIGHTS = 1
 FLAG_GENERIC = 2
 FLAG_EXACT_DEQUANT = 4
+FLAG_GEMV = 8
 
 # name -> argtypes; every function returns int status
 SIGNATURES = {

@@ -8,6 +8,8 @@
         issues them (norm+qkv, o_proj, norm+gate_up+SwiGLU, down), 3 warm-up rounds + 1.
     python .../profile_cases.py gemv N K [M]
         five launches of one W4A16 GEMV of shape [M, K] x [K, N].
+    python .../profile_cases.py gemm M N K
+        three launches of the tcgen05 W4A16 GEMM of shape [M, K] x [K, N], then 20 timed ones.
     python .../profile_cases.py attention
         28 decode-attention launches (one per layer, Qwen2.5-1.5B heads, position 767) eagerly,
         then as a CUDA graph replayed 21 times.
@@ -90,6 +92,23 @@ def gemv(N, K, M="1"):
     print("gemv ok", y.float().abs().mean().item())
 
 
+def gemm(M, N, K):
+    M, N, K = int(M), int(N), int(K)
+    qw, s, z = _q(N, K)
+    x = torch.randn(M, K, device="cuda").half()
+    for _ in range(3):
+        w4a16_matmul(x, qw, s, z)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    e0.record()
+    for _ in range(20):
+        w4a16_matmul(x, qw, s, z)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / 20
+    print(f"gemm M={M} N={N} K={K}: {ms * 1e3:.1f} us, {2 * M * N * K / ms / 1e9:.1f} TFLOP/s")
+
+
 def attention():
     a = config.QWEN15
     nq, nkv, hd = a["num_attention_heads"], a["num_key_value_heads"], a["head_dim"]
@@ -121,7 +140,7 @@ def attention():
     print(f"attention: {e0.elapsed_time(e1) * 1e3 / (20 * layers):.2f} us/launch (position {pos})")
 
 
-CASES = {"decode": decode, "gemv_layer": gemv_layer, "gemv": gemv, "attention": attention}
+CASES = {"decode": decode, "gemv_layer": gemv_layer, "gemv": gemv, "attention": attention, "gemm": gemm}
 
 if __name__ == "__main__":
     if len(sys.argv) < 2 or sys.argv[1] not in CASES:

@@ -12,8 +12,13 @@ here and are accepted and ignored. `FACTORED` keeps the reference's meaning: the
 computes s * sum(x * (q - z)) per group in fp32 by default (the reference's FACTORED numerics);
 `FACTORED=False` (or `EXACT=True`) rounds every dequantized weight to fp16 first, exactly like the
 reference's dequantize-then-matmul. Extra keys: `STATIC_WEIGHTS` (the weights are constant, so the
-kernel may prefetch them before the previous kernel finishes) and `GENERIC` (force the
-any-alignment kernel, which always rounds like the reference).
+kernel may prefetch them before the previous kernel finishes), `GENERIC` (force the
+any-alignment kernel, which always rounds like the reference) and `DECODE_GEMV` (run large M as
+16-row launches of the decode kernel instead of the tensor-core GEMM).
+
+Inputs of 128 rows or more (prefill) run the tcgen05 tensor-core GEMM, which dequantizes with the
+reference's fp16 rounding; the fused SwiGLU and RMSNorm variants then run as the GEMM plus the
+separate norm / activation kernels.
 """
 
 from __future__ import annotations
@@ -25,6 +30,7 @@ import torch
 from kernels import _lib
 
 _choices: dict[tuple, dict] = {}  # (m_key, N, K, bias) -> config used (export/import_choices)
+TC_MIN_ROWS = 128  # rows from which dk_w4a16_matmul runs the tensor-core GEMM
 
 
 def _config(config: dict | None) -> _lib.MatmulConfig:
@@ -39,7 +45,8 @@ def _config(config: dict | None) -> _lib.MatmulConfig:
     c.block_n = bn if bn in (32, 64, 128, 256) else 0
     exact = bool(config.get("EXACT")) or config.get("FACTORED") is False
     c.flags = (_lib.FLAG_STATIC_WEIGHTS if config.get("STATIC_WEIGHTS") else 0) | (
-        _lib.FLAG_GENERIC if config.get("GENERIC") else 0) | (_lib.FLAG_EXACT_DEQUANT if exact else 0)
+        _lib.FLAG_GENERIC if config.get("GENERIC") else 0) | (_lib.FLAG_EXACT_DEQUANT if exact else 0) | (
+        _lib.FLAG_GEMV if config.get("DECODE_GEMV") else 0)
     # L2_PREFETCH: CUDA tensors (e.g. the weights of the launch after next) this launch pulls into L2
     pf = [t for t in (config.get("L2_PREFETCH") or ()) if t is not None and t.numel() > 0]
     if len(pf) > _lib.MAX_L2_PREFETCH:
@@ -96,7 +103,8 @@ def w4a16_swiglu(x, qweight, scales, zeros, group_size=128, bias=None, config=No
         x2 = x2.contiguous()
     aligned = all(t.data_ptr() % 16 == 0 for t in (x2, qweight, scales, zeros)) and x2.stride(0) % 8 == 0
     cfg = _config(config)
-    if I % 32 != 0 or group_size != 128 or not aligned or cfg.flags & _lib.FLAG_GENERIC:
+    big = x2.shape[0] >= TC_MIN_ROWS and not cfg.flags & _lib.FLAG_GEMV
+    if I % 32 != 0 or group_size != 128 or not aligned or cfg.flags & _lib.FLAG_GENERIC or big:
         from kernels.swiglu import swiglu_fused
 
         return swiglu_fused(w4a16_matmul(x, qweight, scales, zeros, group_size, bias, config))
@@ -134,7 +142,9 @@ def w4a16_rmsnorm_matmul(x, norm_weight, eps, residual, qweight, scales, zeros, 
     cfg = _config(config)
     I = N // 2
     tensors = [x2, qweight, scales, zeros, norm_weight] + ([r2] if r2 is not None else [])
+    big = M >= TC_MIN_ROWS and not cfg.flags & _lib.FLAG_GEMV
     fast = (group_size == 128 and N % 8 == 0 and (not swiglu or I % 32 == 0) and not cfg.flags & _lib.FLAG_GENERIC
+            and not big
             and all(t.data_ptr() % 16 == 0 for t in tensors) and x2.stride(0) % 8 == 0
             and (r2 is None or r2.stride(0) % 8 == 0) and norm_weight.is_contiguous())
     if not fast:

@@ -77,7 +77,7 @@ def test_tp_entry_points_validate_without_a_gpu():
     h = _lib.lib()
     n = ctypes.c_uint64(0)
     assert h.dk_tp_buffer_bytes(2, 16, 3584, ctypes.byref(n)) == 0
-    assert n.value == 256 + 8 * 1024 * 8 + 2 * 2 * 16 * 3584 * 4
+    assert n.value == 256 + 2 * 2 * 16 * 3584 * 8
     assert h.dk_tp_buffer_bytes(9, 16, 3584, ctypes.byref(n)) == -1
     assert h.dk_tp_buffer_bytes(2, 17, 3584, ctypes.byref(n)) == -1
     assert h.dk_tp_buffer_bytes(2, 16, 3585, ctypes.byref(n)) == -1

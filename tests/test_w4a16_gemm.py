@@ -1,0 +1,96 @@
+"""W4A16 tensor-core GEMM (tcgen05 + TMEM; dk_w4a16_matmul with M >= 128 and N >= 128) vs the oracle's
+dequantize-then-fp32-matmul (reference kernels/reference.py:39-45), rtol 2e-2 / atol 2e-3, and vs the
+decode GEMV run over 16-row blocks. The GEMM rounds every dequantized weight to fp16 like the
+reference, so the only differences are fp32 summation order and the final fp16 rounding."""
+
+import numpy as np
+import pytest
+import torch
+
+from _util import assert_matmul_close, to_cuda, w4_case, w4_ref
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("M,N,K,bias", [
+    (128, 128, 128, False), (200, 200, 256, True), (256, 1536, 1536, True), (512, 2048, 1536, False),
+    (130, 17920, 1536, False), (384, 1536, 8960, False), (129, 256, 4096, True), (640, 4608, 3584, True),
+])
+def test_gemm_matches_oracle(M, N, K, bias):
+    from kernels.w4a16 import w4a16_matmul
+
+    x, qw, s, z, b = w4_case(M, N, K, seed=M + N, bias=bias)
+    xc, qc, sc, zc, bc = to_cuda(x, qw, s, z, b)
+    out = w4a16_matmul(xc, qc, sc, zc, 128, bias=bc)
+    assert_matmul_close(out, w4_ref(x, qw, s, z, b))
+    again = w4a16_matmul(xc, qc, sc, zc, 128, bias=bc)
+    assert torch.equal(out, again)  # deterministic
+    from kernels import _lib
+
+    assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 2048, 1536), (1024, 1536, 8960)])
+def test_gemm_matches_decode_gemv(M, N, K):
+    from kernels.w4a16 import w4a16_matmul
+
+    x, qw, s, z, _ = w4_case(M, N, K, seed=3)
+    xc, qc, sc, zc = to_cuda(x, qw, s, z)
+    tc = w4a16_matmul(xc, qc, sc, zc).float()
+    gemv = w4a16_matmul(xc, qc, sc, zc, config={"DECODE_GEMV": True, "FACTORED": False}).float()
+    torch.testing.assert_close(tc, gemv, rtol=2e-2, atol=2e-3)
+
+
+def test_gemm_strided_and_3d_input():
+    from kernels.w4a16 import w4a16_matmul
+
+    M, N, K = 256, 1024, 1024
+    x, qw, s, z, _ = w4_case(M, N, K, seed=5)
+    xc, qc, sc, zc = to_cuda(x, qw, s, z)
+    wide = torch.zeros(M, K + 64, dtype=torch.float16, device="cuda")
+    wide[:, :K] = xc
+    out = w4a16_matmul(wide[:, :K], qc, sc, zc)  # row stride K + 64
+    assert_matmul_close(out, w4_ref(x, qw, s, z, None))
+    out3 = w4a16_matmul(xc.view(2, 128, K), qc, sc, zc)
+    assert out3.shape == (2, 128, N) and torch.equal(out3.view(M, N), out)
+
+
+def test_gemm_in_cuda_graph():
+    from kernels.bench.harness import capture
+    from kernels.w4a16 import w4a16_matmul
+
+    x, qw, s, z, b = w4_case(256, 2048, 1536, seed=9, bias=True)
+    xc, qc, sc, zc, bc = to_cuda(x, qw, s, z, b)
+    ref = w4a16_matmul(xc, qc, sc, zc, bias=bc)
+    res = {}
+
+    def step():
+        res["y"] = w4a16_matmul(xc, qc, sc, zc, bias=bc)
+
+    step()
+    torch.cuda.synchronize()
+    graph, _ = capture(step)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(res["y"], ref)
+    del graph
+
+
+def test_prefill_swiglu_and_norm_paths():
+    """M >= 128 through the fused entry points runs the GEMM plus the separate kernels: same
+    results as those ops called one by one."""
+    from kernels.rmsnorm import rmsnorm
+    from kernels.swiglu import swiglu_fused
+    from kernels.w4a16 import w4a16_matmul, w4a16_rmsnorm_matmul, w4a16_swiglu
+
+    M, I, K = 256, 1024, 1536
+    x, qw, s, z, _ = w4_case(M, 2 * I, K, seed=4)
+    xc, qc, sc, zc = to_cuda(x, qw, s, z)
+    assert torch.equal(w4a16_swiglu(xc, qc, sc, zc), swiglu_fused(w4a16_matmul(xc, qc, sc, zc)))
+    r = torch.randn(M, K, device="cuda").half()
+    nw = (1 + 0.05 * torch.randn(K, device="cuda")).half()
+    y, res = w4a16_rmsnorm_matmul(xc, nw, 1e-6, r, qc, sc, zc, swiglu=True)
+    h, res2 = rmsnorm(xc, nw, 1e-6, residual=r)
+    assert torch.equal(res, res2)
+    assert torch.equal(y, swiglu_fused(w4a16_matmul(h, qc, sc, zc)))
