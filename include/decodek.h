@@ -225,6 +225,26 @@ int dk_w4a16_matmul_allreduce(const void* x, int64_t ldx, const int32_t* qweight
                               int64_t K, int64_t group_size, const dk_matmul_config* cfg,
                               const dk_tp_comm* comm, dk_stream_t stream);
 
+/* ---- allocation-free variant ---------------------------------------------------------------
+ * No counterpart in the reference. dk_w4a16_matmul_allreduce needs an exchange buffer from
+ * dk_tp_buffer_alloc (cudaMalloc). Some callers cannot allocate device memory: a plugin loaded into a
+ * serving process that owns the CUDA allocator and hands the plugin only its input and output
+ * buffers, or a runtime that forbids raw cudaMalloc (it synchronizes the device and fragments a pool
+ * it manages). For them this entry point runs the same fused matmul + reduce kernel on one GPU
+ * (world 1: y = fp16(x @ dequant(W).T + bias), the result of dk_w4a16_matmul_allreduce with a
+ * one-rank communicator) with its scratch - launch epoch, arrival count and the epoch-tagged
+ * partial-sum cells - in a fixed array inside the library: 2 MiB + 256 bytes per GPU that loads the
+ * library, held until the process exits. The caller passes inputs and outputs only. Limits: N <= 8192
+ * (larger N returns DK_ERR_INVALID), M in launches of up to 16 rows, and the fast path's conditions
+ * (group_size 128, N % 8 == 0, 16-byte aligned operands). It calls no cudaMalloc, cudaFree or
+ * allocating library routine. Its first call on a device looks up the array's device address
+ * (set-up): make that first call before any stream capture. Every call shares the one array and
+ * clears its 16-byte header on `stream` first; calls that overlap on the GPU (other streams, other
+ * host threads) race on it. */
+int dk_w4a16_matmul_reduce_static(const void* x, int64_t ldx, const int32_t* qweight, const void* scales,
+                                  const void* zeros, const void* bias, void* y, int64_t ldy, int64_t M, int64_t N,
+                                  int64_t K, int64_t group_size, const dk_matmul_config* cfg, dk_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

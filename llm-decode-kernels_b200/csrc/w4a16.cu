@@ -1041,3 +1041,82 @@ extern "C" int dk_w4a16_matmul_allreduce(const void* x, int64_t ldx, const int32
                   reinterpret_cast<cudaStream_t>(stream), &tp);
 }
 
+// ---------------------------------------------------------------- allocation-free single-GPU variant
+// dk_w4a16_matmul_reduce_static: the fused matmul + reduce launch of dk_w4a16_matmul_allreduce on one
+// GPU (world 1), for callers that cannot allocate device memory themselves (see decodek.h). Its
+// scratch - the header (launch epoch, CTA arrival count) and the tagged partial-sum cells - lives in
+// the file-scope array below instead of a buffer from dk_tp_buffer_alloc.
+namespace dk {
+namespace {
+
+constexpr int kStaticMaxM = 16;
+constexpr int kStaticMaxN = 8192;
+constexpr size_t kStaticScratchBytes = kTpHeaderBytes + 2ull * kStaticMaxM * kStaticMaxN * 8;  // 2 MiB + 256 B
+
+// One copy per device that loads the library, held until the process exits. Host code must not use
+// the name as an address: static_scratch_address() gets the device address.
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+// Device address of g_static_scratch on the current device, looked up once per device (set-up done
+// by the entry point's first call on that device). nullptr with dk_last_error set on failure.
+void* static_scratch_address() {
+  static std::mutex mu;
+  static void* addr[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    set_error(DK_ERR_CUDA, "w4a16_matmul_reduce_static: no current CUDA device");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      set_error(DK_ERR_CUDA, "w4a16_matmul_reduce_static: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      return nullptr;
+    }
+    addr[dev] = p;
+  }
+  return addr[dev];
+}
+
+}  // namespace
+}  // namespace dk
+
+extern "C" int dk_w4a16_matmul_reduce_static(const void* x, int64_t ldx, const int32_t* qweight, const void* scales,
+                                             const void* zeros, const void* bias, void* y, int64_t ldy, int64_t M,
+                                             int64_t N, int64_t K, int64_t group_size, const dk_matmul_config* cfg,
+                                             dk_stream_t stream) {
+  using namespace dk;
+  int rc = check_w4a16_args("w4a16_matmul_reduce_static", x, ldx, qweight, scales, zeros, y, ldy, M, N, N, K,
+                            group_size);
+  if (rc != DK_OK) return rc;
+  if (N > kStaticMaxN)
+    return set_error(DK_ERR_INVALID,
+                     "w4a16_matmul_reduce_static: N=%lld exceeds the static scratch limit of %d columns",
+                     (long long)N, kStaticMaxN);
+  if (M == 0 || N == 0) return DK_OK;
+  const int flags = cfg ? cfg->flags : 0;
+  if (!fast_ok(x, ldx, qweight, scales, zeros, N, K, group_size, flags))
+    return set_error(DK_ERR_UNSUPPORTED,
+                     "w4a16_matmul_reduce_static: needs group_size 128, N %% 8 == 0 and 16-byte aligned operands");
+  char* base = static_cast<char*>(static_scratch_address());
+  if (base == nullptr) return DK_ERR_CUDA;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // The header must start at zero (epoch 0: the first launch uses tag 1; no CTA has arrived). The
+  // cells need no clearing: a CTA only reads cells its own threads wrote earlier in the same launch.
+  cudaError_t e = cudaMemsetAsync(base, 0, 16, st);
+  if (e != cudaSuccess)
+    return set_error(DK_ERR_CUDA, "w4a16_matmul_reduce_static: clearing the scratch header: %s", cudaGetErrorString(e));
+  TPArgs tp;
+  std::memset(&tp, 0, sizeof(tp));
+  tp.cells[0] = reinterpret_cast<uint32_t*>(base + kTpHeaderBytes);
+  tp.epoch = reinterpret_cast<unsigned long long*>(base);
+  tp.arrive = reinterpret_cast<unsigned int*>(base + 8);
+  tp.rank = 0;
+  tp.world = 1;
+  tp.max_m = kStaticMaxM;
+  tp.max_n = kStaticMaxN;
+  return run_fast(x, ldx, qweight, scales, zeros, bias, y, ldy, M, N, K, group_size, cfg, 0, NormArgs(), st, &tp);
+}

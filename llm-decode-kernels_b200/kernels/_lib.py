@@ -68,6 +68,8 @@ SIGNATURES = {
     "dk_tp_comm_destroy": [P],
     "dk_w4a16_matmul_allreduce": [P, I64, P, P, P, P, P, I64, I64, I64, I64, I64, ctypes.POINTER(MatmulConfig), P,
                                   P],
+    "dk_w4a16_matmul_reduce_static": [P, I64, P, P, P, P, P, I64, I64, I64, I64, I64, ctypes.POINTER(MatmulConfig),
+                                      P],
 }
 
 _lib = None
