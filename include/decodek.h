@@ -144,7 +144,9 @@ int dk_dequantize_fp8(const uint8_t* wq, const void* scale, void* w, int64_t N, 
 
 /* w8a16_matmul (kernels/fp8.py:200-223): y[M, N] fp16 = (x[M, K] @ fp16(wq)) * scale (+ bias),
  * wq e4m3 [K, N] (N contiguous), scale fp16 [N], fp32 accumulation, the scale applied to the
- * fp32 sum (kernels/fp8.py:81-82). cfg as for dk_w4a16_matmul (split_k, block_n, flags). */
+ * fp32 sum (kernels/fp8.py:81-82). cfg as for dk_w4a16_matmul (split_k, block_n, flags).
+ * M >= 128 and N >= 128 (N % 16 == 0, K % 64 == 0, aligned) run the tcgen05 tensor-core GEMM
+ * (kernels/fp8.py:42-127 for large M); DK_FLAG_GEMV keeps the 16-row decode kernel. */
 int dk_w8a16_matmul(const void* x, int64_t ldx, const uint8_t* wq, const void* scale, const void* bias,
                     void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, const dk_matmul_config* cfg,
                     dk_stream_t stream);

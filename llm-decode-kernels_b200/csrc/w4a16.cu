@@ -63,6 +63,7 @@ struct GemvParams {
   int split_stages;  // stages per cluster rank
   int chunks;        // ceil(N / 32)
   int nbuf;          // ring depth
+  uint32_t nbuf_rcp; // ceil(2^32 / nbuf): it / nbuf == __umulhi(it, nbuf_rcp) for the small it used here
   int xs_pitch;      // bytes per staged x row
   int static_weights;
   int swiglu_i;      // > 0: fused SwiGLU over gate columns [0, I) and up columns [I, 2I); y is [M, I]
@@ -79,7 +80,7 @@ struct GemvParams {
 };
 
 struct SmemLayout {
-  int w_off, sz_off, xs_off, red_off, bar_off, total;
+  int w_off, sz_off, xs_off, cx_off, red_off, bar_off, total;
 };
 
 constexpr int kWarps = 8;  // consumer warps per CTA (plus one producer warp)
@@ -91,7 +92,9 @@ __host__ __device__ inline SmemLayout smem_layout(int cw, int nbuf, int M, int x
   L.w_off = 0;
   L.sz_off = nbuf * cw * kBoxBytes;
   L.xs_off = L.sz_off + nbuf * cw * 2 * kSZBytes;
-  L.red_off = L.xs_off + ((M * xs_pitch + 15) / 16) * 16;
+  // per (group, row) corrections of the factored path: {C, X} fp32 for 16 rows = 128 bytes a group
+  L.cx_off = L.xs_off + ((M * xs_pitch + 15) / 16) * 16;
+  L.red_off = L.cx_off + 2 * ((xs_pitch - kXsPad) / (kStageRows * 16)) * 128;
   // reduction scratch, always present: the fused-SwiGLU and split-K epilogues use it at any wpc
   L.bar_off = L.red_off + wpc * M * cw * 32 * 4;
   L.total = L.bar_off + 2 * nbuf * 8;
@@ -335,13 +338,108 @@ __device__ void tp_finish(const GemvParams& p, unsigned long long ep, bool ok, i
   }
 }
 
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
+
+// The default (factored) path without a per-weight zero subtraction. A word's nibble pairs become
+// fp16 by LOP3 with the 0x6400 exponent alone: 1024 + q for the low nibble of a byte (even K) and
+// 1024 + 16 q for the high nibble (odd K), whose x values were staged divided by 16. The MMA then
+// sums x'(1024 + q') = C + sum(x q) over a group, where C = 1024 * sum(x') is a per-(group, row)
+// constant computed once per CTA from the staged x, and X = sum over the group of the x each weight
+// is effectively multiplied by; the group's result is s * (mma - C - z * X), the reference's
+// FACTORED numerics (kernels/w4a16.py:116-119) with the zero point applied once per group.
+// Shared-memory operands come by 32-bit address: wbox (the chunk-stage's swizzled weight box), szb
+// (its scale and zero boxes), xrow (this stage's staged x), cxg (the stage's two {C, X} groups).
+template <int NT>
+__device__ __forceinline__ void consume_chunk_stage_f(uint32_t wbox, uint32_t szb, uint32_t xrow, uint32_t cxg,
+                                                      int xs_pitch, int M, int g, int t, float (&acc)[2][NT][4]) {
+  const uint32_t k1024 = 0x64006400u;
+  // a lane reads packed rows r = 8 * (st / 2) + 2t + (st % 2): two lane-dependent bases
+  const uint32_t w_even = wbox + (2 * t) * 128 + ((g ^ (2 * t)) << 4);
+  const uint32_t w_odd = wbox + (2 * t + 1) * 128 + ((g ^ (2 * t + 1)) << 4);
+  const uint32_t x_even = xrow + (2 * t) * 16, x_odd = xrow + (2 * t + 1) * 16;
+#pragma unroll
+  for (int half = 0; half < kGroupsPerStage; ++half) {
+    const uint2 s4 = lds64(szb + half * 64 + g * 8);
+    const uint2 z4 = lds64(szb + kSZBytes + half * 64 + g * 8);
+    float accg[2][NT][4];
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+      for (int b = 0; b < NT; ++b)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) accg[a][b][c] = 0.f;
+#pragma unroll
+    for (int st4 = 0; st4 < 4; ++st4) {
+      const int st = half * 4 + st4;
+      const uint4 wv = lds128(((st & 1) ? w_odd : w_even) + 1024 * (st >> 1));
+      uint32_t bx[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const int m = nt * 8 + g;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (m < M) v = lds128(((st & 1) ? x_odd : x_even) + 128 * (st >> 1) + m * xs_pitch);
+        bx[nt][0] = v.x;
+        bx[nt][1] = v.y;
+        bx[nt][2] = v.z;
+        bx[nt][3] = v.w;
+      }
+      const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
+      uint32_t W[4][4];  // [column][nibble pair]
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint32_t w = words[c];
+        const uint32_t w8 = w >> 8;
+        W[c][0] = lop3_and_or(w, 0x000F000Fu, k1024);   // 1024 + q0, 1024 + q4
+        W[c][1] = lop3_and_or(w, 0x00F000F0u, k1024);   // 1024 + 16 q1, 1024 + 16 q5
+        W[c][2] = lop3_and_or(w8, 0x000F000Fu, k1024);  // q2, q6
+        W[c][3] = lop3_and_or(w8, 0x00F000F0u, k1024);  // q3, q7
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        mma_16816(accg[0][nt], W[0][0], W[1][0], W[0][1], W[1][1], bx[nt][0], bx[nt][1]);
+        mma_16816(accg[0][nt], W[0][2], W[1][2], W[0][3], W[1][3], bx[nt][2], bx[nt][3]);
+        mma_16816(accg[1][nt], W[2][0], W[3][0], W[2][1], W[3][1], bx[nt][0], bx[nt][1]);
+        mma_16816(accg[1][nt], W[2][2], W[3][2], W[2][3], W[3][3], bx[nt][2], bx[nt][3]);
+      }
+    }
+    const __half2 s01 = *reinterpret_cast<const __half2*>(&s4.x), s23 = *reinterpret_cast<const __half2*>(&s4.y);
+    const __half2 z01 = *reinterpret_cast<const __half2*>(&z4.x), z23 = *reinterpret_cast<const __half2*>(&z4.y);
+    const float sc[4] = {__low2float(s01), __high2float(s01), __low2float(s23), __high2float(s23)};
+    const float zc[4] = {__low2float(z01), __high2float(z01), __low2float(z23), __high2float(z23)};
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      // {C, X} of rows nt*8 + 2t and nt*8 + 2t + 1 (the D fragment's two batch rows)
+      const uint4 cxr = lds128(cxg + half * 128 + (nt * 8 + 2 * t) * 8);
+      const float cx[2][2] = {{__uint_as_float(cxr.x), __uint_as_float(cxr.y)},
+                              {__uint_as_float(cxr.z), __uint_as_float(cxr.w)}};
+#pragma unroll
+      for (int tile = 0; tile < 2; ++tile)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int col = 2 * tile + (e >> 1), r = e & 1;
+          acc[tile][nt][e] = fmaf(sc[col], accg[tile][nt][e] - fmaf(zc[col], cx[r][1], cx[r][0]), acc[tile][nt][e]);
+        }
+    }
+  }
+}
+
 // Stage x[:, K slice of this CTA] into shared memory, each 8-element block permuted to
 // (0,4,1,5,2,6,3,7) for the MMA fragments. With `norm_w` the staged rows are the fused residual
 // add + RMSNorm of the input, with the rounding of kernels/rmsnorm.py:28-37 (and the rmsnorm kernel
 // of this library): h = x + residual (fp16 add), var = sum(h^2)/K in fp32, out = w * fp16(h / sqrt(
 // var + eps)); every CTA reads the whole row for the sum of squares (per-warp partials added in a
 // fixed order: deterministic), and `writer` (one CTA) stores h as the new residual stream.
-__device__ __forceinline__ void stage_x(const GemvParams& p, uint8_t* xs, int s_begin, int nst, bool writer) {
+__device__ __forceinline__ void stage_x(const GemvParams& p, uint8_t* xs, float* cx, int s_begin, int nst, bool writer,
+                                        bool factored) {
   constexpr int kThr = kWarps * 32;
   const int tid = threadIdx.x;
   const int kb0 = s_begin * kStageRows;  // first packed row (block of 8 K values)
@@ -384,7 +482,11 @@ __device__ __forceinline__ void stage_x(const GemvParams& p, uint8_t* xs, int s_
     }
     asm volatile("bar.sync 1, %0;" ::"r"(kThr) : "memory");
   }
-  for (int i = tid; i < p.M * nblk; i += kThr) {
+  // One item = 8 K values of one row. nblk is a multiple of 32, so every warp iteration has 32 items
+  // in range and the 16 lanes of a half-warp hold the 16 blocks of one 128-group: the factored path
+  // reduces its {C, X} with shuffles in a fixed order (deterministic) - no second pass.
+  for (int base = (tid & ~31); base < p.M * nblk; base += kThr) {
+    const int i = base + (tid & 31);
     const int m = i / nblk, b = i % nblk;
     const int k = (kb0 + b) * 8;
     uint4 v = make_uint4(0, 0, 0, 0);
@@ -413,6 +515,28 @@ __device__ __forceinline__ void stage_x(const GemvParams& p, uint8_t* xs, int s_
     o.y = prmt(v.x, v.z, 0x7632);  // (x1, x5)
     o.z = prmt(v.y, v.w, 0x5410);  // (x2, x6)
     o.w = prmt(v.y, v.w, 0x7632);  // (x3, x7)
+    if (factored) {  // odd K meets 1024 + 16 q: stage x / 16 (exact, a power of two)
+      o.y = hmul2_rn(o.y, 0x2C002C00u);
+      o.w = hmul2_rn(o.w, 0x2C002C00u);
+      // {C, X} of this 128-group and row: C = 1024 * sum of the staged values, X = the sum of the x
+      // each weight is multiplied by (odd K: 16 * staged)
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&o.x));
+      const float2 bb = __half22float2(*reinterpret_cast<const __half2*>(&o.y));
+      const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&o.z));
+      const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&o.w));
+      const float even = (a.x + a.y) + (c.x + c.y), odd = (bb.x + bb.y) + (d.x + d.y);
+      float C = even + odd, X = fmaf(16.f, odd, even);
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) {
+        C += __shfl_xor_sync(0xffffffffu, C, off);
+        X += __shfl_xor_sync(0xffffffffu, X, off);
+      }
+      if ((tid & 15) == 0) {
+        float* dst = cx + 2 * ((b >> 4) * 16 + m);  // [group in slice][16 rows]{C, X}
+        dst[0] = 1024.f * C;
+        dst[1] = X;
+      }
+    }
     *reinterpret_cast<uint4*>(xs + m * p.xs_pitch + b * 16) = o;
   }
   asm volatile("bar.sync 1, %0;" ::"r"(kThr) : "memory");
@@ -426,7 +550,8 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 3 - NT)  // M <= 8: two CTA
                       const __grid_constant__ CUtensorMap mz, const GemvParams p) {
   constexpr int WPC = kWarps / CW;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte aligned base, derived from smem_raw by pointer arithmetic so accesses stay shared-space
+  uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   const int S = gridDim.y;
   const SmemLayout L = smem_layout(CW, p.nbuf, p.M, p.xs_pitch, S);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
@@ -476,8 +601,9 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 3 - NT)  // M <= 8: two CTA
       for (int tile = c_begin; tile < c_end && ok; tile += UPT) {
         const int nch = min(UPT, c_end - tile);
         for (int s = s_begin; s < s_end; ++s, ++it) {
-          const int buf = it % p.nbuf;
-          if (it >= p.nbuf && !mbar_wait(&empty[buf], ((it / p.nbuf) - 1) & 1, p.err, DK_DEVERR_WAIT_EMPTY)) {
+          const int round = static_cast<int>(__umulhi(static_cast<uint32_t>(it), p.nbuf_rcp));
+          const int buf = it - round * p.nbuf;
+          if (it >= p.nbuf && !mbar_wait(&empty[buf], (round - 1) & 1, p.err, DK_DEVERR_WAIT_EMPTY)) {
             ok = false;
             break;
           }
@@ -498,7 +624,8 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 3 - NT)  // M <= 8: two CTA
     // ---------------------------------------------------------------- consumer warps
     pdl_wait();  // x (and the residual) come from the previous kernels
     if (p.tp.world > 0 && threadIdx.x == 0) s_ep = *reinterpret_cast<volatile unsigned long long*>(p.tp.epoch) + 1;
-    stage_x(p, smem + L.xs_off, s_begin, nst, blockIdx.x == 0 && blockIdx.y == 0);  // ends with a barrier
+    stage_x(p, smem + L.xs_off, reinterpret_cast<float*>(smem + L.cx_off), s_begin, nst,
+            blockIdx.x == 0 && blockIdx.y == 0, !EXACT);  // ends with a barrier
     const unsigned long long ep = s_ep;
     const int g = lane >> 2;  // MMA group: A rows g, g+8 ; B column g
     const int t = lane & 3;   // thread in group: K slots 2t.., 2t+8..
@@ -519,15 +646,24 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 3 - NT)  // M <= 8: two CTA
 
       for (int ls = phase; ls < nst && ok; ls += WPC) {
         const int it = tile_idx * nst + ls;
-        const int buf = it % p.nbuf;
-        if (!mbar_wait(&full[buf], (it / p.nbuf) & 1, p.err, DK_DEVERR_WAIT_FULL)) {
+        const int round = static_cast<int>(__umulhi(static_cast<uint32_t>(it), p.nbuf_rcp));
+        const int buf = it - round * p.nbuf;
+        if (!mbar_wait(&full[buf], round & 1, p.err, DK_DEVERR_WAIT_FULL)) {
           ok = false;
           break;
         }
-        if (active)
-          consume_chunk_stage<NT, EXACT>(smem + L.w_off + (buf * CW + slot) * kBoxBytes,
-                                         smem + L.sz_off + (buf * CW + slot) * 2 * kSZBytes,
-                                         smem + L.xs_off + ls * kStageRows * 16, p.xs_pitch, p.M, g, t, acc);
+        if (active) {
+          if constexpr (EXACT)
+            consume_chunk_stage<NT, true>(smem + L.w_off + (buf * CW + slot) * kBoxBytes,
+                                          smem + L.sz_off + (buf * CW + slot) * 2 * kSZBytes,
+                                          smem + L.xs_off + ls * kStageRows * 16, p.xs_pitch, p.M, g, t, acc);
+          else
+            consume_chunk_stage_f<NT>(smem_addr(smem + L.w_off + (buf * CW + slot) * kBoxBytes),
+                                      smem_addr(smem + L.sz_off + (buf * CW + slot) * 2 * kSZBytes),
+                                      smem_addr(smem + L.xs_off + ls * kStageRows * 16),
+                                      smem_addr(smem + L.cx_off + ls * kGroupsPerStage * 128), p.xs_pitch, p.M, g, t,
+                                      acc);
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[buf]);
       }
@@ -890,6 +1026,7 @@ int run_fast(const void* x, int64_t ldx, const int32_t* qweight, const void* sca
     p.split_stages = (p.stages_total + c.split - 1) / c.split;
     p.chunks = units;
     p.nbuf = c.nbuf;
+    p.nbuf_rcp = static_cast<uint32_t>((0x100000000ull + c.nbuf - 1) / c.nbuf);
     p.xs_pitch = xs_pitch_for(p.split_stages);
     p.static_weights = (flags & DK_FLAG_STATIC_WEIGHTS) ? 1 : 0;
     p.swiglu_i = swiglu_i;

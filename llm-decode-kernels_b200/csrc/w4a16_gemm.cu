@@ -1,5 +1,7 @@
-// W4A16 GEMM for prefill-sized inputs (M >= 128 rows) on the 5th-generation tensor cores:
+// W4A16 (and W8A16) GEMM for prefill-sized inputs (M >= 128 rows) on the 5th-generation tensor cores:
 // y[M, N] = x[M, K] @ dequant(W).T (+ bias), fp16 operands, fp32 accumulation in tensor memory.
+// The e4m3 variant (kFp8) differs only in the weight tile and its conversion (see below) and applies
+// the per-column scale to the fp32 accumulator in the epilogue.
 //
 // Replaces the reference's Triton tensor-core tile kernel for large M (kernels/w4a16.py:31-97,
 // the `direct` path of w4a16_matmul) with tcgen05.mma. One CTA computes a 128 x 128 tile of y:
@@ -34,29 +36,48 @@ constexpr int kStages = 4;
 constexpr int kThreads = 192;                  // warp 0 TMA, warp 1 TMEM + MMA, warps 2-5 dequant + epilogue
 constexpr int kABytes = kBM * kBK * 2;         // 16 KB x tile
 constexpr int kBBytes = kBN * kBK * 2;         // 16 KB dequantized weight tile
-constexpr int kWBytes = (kBK / 8) * kBN * 4;   // 4 KB packed weights
-constexpr int kSZBytes = kBN * 2;              // one scale (or zero) row
-constexpr uint32_t kStageTx = kABytes + kWBytes + 2 * kSZBytes;
-constexpr int kOffB = kStages * kABytes;
-constexpr int kOffW = kOffB + kStages * kBBytes;
-constexpr int kOffS = kOffW + kStages * kWBytes;
-constexpr int kOffZ = kOffS + kStages * kSZBytes;
-constexpr int kOffBar = kOffZ + kStages * kSZBytes;
-constexpr int kSmemBytes = kOffBar + (3 * kStages + 1) * 8 + 16 + 1024;  // + barriers, TMEM slot, alignment
+constexpr int kSZBytes = kBN * 2;              // one scale (or zero) row (int4 format)
+
+// Shared-memory layout per weight format: int4 (packed rows [8][128] int32 + scale and zero rows) or
+// e4m3 (the raw [64 K][128 N] byte tile).
+template <bool kFp8>
+struct Layout {
+  static constexpr int kWBytes = kFp8 ? kBK * kBN : (kBK / 8) * kBN * 4;  // 8 KB e4m3 / 4 KB int4
+  static constexpr uint32_t kStageTx = kABytes + kWBytes + (kFp8 ? 0 : 2 * kSZBytes);
+  static constexpr int kOffB = kStages * kABytes;
+  static constexpr int kOffW = kOffB + kStages * kBBytes;
+  static constexpr int kOffS = kOffW + kStages * kWBytes;
+  static constexpr int kOffZ = kOffS + kStages * kSZBytes;
+  static constexpr int kOffBar = kOffZ + kStages * kSZBytes;
+  static constexpr int kSmemBytes = kOffBar + (3 * kStages + 1) * 8 + 16 + 1024;  // + barriers, TMEM slot, alignment
+};
 
 struct GemmParams {
   __half* y;
   int64_t ldy;
   const __half* bias;
+  const __half* scale;  // e4m3 format: per-column scale applied to the fp32 sum (kernels/fp8.py:81-82)
   int M, N, K;
   int ktiles;
   int* err;
 };
 
+// Convert the two e4m3 bytes of each 16-bit half of `v` to fp16 pairs (exact: every e4m3 value is an fp16).
+__device__ __forceinline__ void e4m3x4_to_f16(uint32_t v, uint32_t& lo, uint32_t& hi) {
+  asm("{\n.reg .b16 a, b;\nmov.b32 {a, b}, %2;\ncvt.rn.f16x2.e4m3x2 %0, a;\ncvt.rn.f16x2.e4m3x2 %1, b;\n}\n"
+      : "=r"(lo), "=r"(hi)
+      : "r"(v));
+}
+
+template <bool kFp8>
 __global__ void __launch_bounds__(kThreads, 1)
     w4a16_gemm_tc_kernel(const __grid_constant__ CUtensorMap mx, const __grid_constant__ CUtensorMap mq,
                          const __grid_constant__ CUtensorMap ms, const __grid_constant__ CUtensorMap mz,
                          const GemmParams p) {
+  using Lay = Layout<kFp8>;
+  constexpr int kWBytes = Lay::kWBytes, kOffB = Lay::kOffB, kOffW = Lay::kOffW, kOffS = Lay::kOffS,
+                kOffZ = Lay::kOffZ, kOffBar = Lay::kOffBar;
+  constexpr uint32_t kStageTx = Lay::kStageTx;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -101,8 +122,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       prefetch_tensormap(&mx);
       prefetch_tensormap(&mq);
-      prefetch_tensormap(&ms);
-      prefetch_tensormap(&mz);
+      if (!kFp8) {
+        prefetch_tensormap(&ms);
+        prefetch_tensormap(&mz);
+      }
       for (int kt = 0; kt < p.ktiles; ++kt) {
         const int s = kt % kStages;
         if (kt >= kStages && !mbar_wait(&empty[s], ((kt / kStages) - 1) & 1, p.err, DK_DEVERR_WAIT_EMPTY)) {
@@ -111,9 +134,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_arrive_expect_tx(&full[s], kStageTx);
         tma_load_2d(sA + s * kABytes, &mx, kt * kBK, m0, &full[s]);
-        tma_load_2d(sW + s * kWBytes, &mq, n0, kt * (kBK / 8), &full[s]);
-        tma_load_2d(sS + s * kSZBytes, &ms, n0, (kt * kBK) / 128, &full[s]);
-        tma_load_2d(sZ + s * kSZBytes, &mz, n0, (kt * kBK) / 128, &full[s]);
+        if (kFp8) {
+          tma_load_2d(sW + s * kWBytes, &mq, n0, kt * kBK, &full[s]);  // e4m3 [64 K rows][128 N]
+        } else {
+          tma_load_2d(sW + s * kWBytes, &mq, n0, kt * (kBK / 8), &full[s]);
+          tma_load_2d(sS + s * kSZBytes, &ms, n0, (kt * kBK) / 128, &full[s]);
+          tma_load_2d(sZ + s * kSZBytes, &mz, n0, (kt * kBK) / 128, &full[s]);
+        }
         issued = kt + 1;
       }
     }
@@ -137,6 +164,47 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::commit(&empty[s]);  // the stage is free once these MMAs have read it
       }
       tc::commit(done);  // the accumulator is final once every MMA issued above has completed
+    }
+  } else if (kFp8) {
+    // ------------------------------------------------------------ e4m3 -> fp16 (warps 2-5), transposing
+    // Lane c owns columns 4c..4c+3; of the stage's 8 K-blocks (8 rows each) warp w takes the pair
+    // 2 * ((w + c / 2) % 4) + {0, 1}, so the 4 warps cover all 8 and the lanes of one store spread
+    // over the bank groups. A K-block: 8 row words (4 columns each) -> PRMT pairs rows (2i, 2i+1)
+    // per column -> cvt gives fp16 (k even, k odd) -> one 16-byte chunk per column.
+    const int c = lane, w = warp - 2;
+    for (int kt = 0; kt < p.ktiles; ++kt) {
+      const int s = kt % kStages;
+      if (!mbar_wait(&full[s], (kt / kStages) & 1, p.err, DK_DEVERR_WAIT_FULL)) {
+        ok = false;
+        break;
+      }
+      const uint32_t* raw = reinterpret_cast<const uint32_t*>(sW + s * kWBytes);  // row k: 32 words
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int kb = 2 * ((w + (c >> 1)) & 3) + i;
+        uint32_t r[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) r[j] = raw[(kb * 8 + j) * (kBN / 4) + c];
+        uint32_t h[4][4];  // [column][k pair]
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t lo, hi;
+          e4m3x4_to_f16(prmt(r[2 * j], r[2 * j + 1], 0x5140u), lo, hi);  // columns 0, 1 of rows 2j, 2j+1
+          h[0][j] = lo;
+          h[1][j] = hi;
+          e4m3x4_to_f16(prmt(r[2 * j], r[2 * j + 1], 0x7362u), lo, hi);  // columns 2, 3
+          h[2][j] = lo;
+          h[3][j] = hi;
+        }
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          const int n = 4 * c + cc;  // row n of the B tile, chunk kb
+          *reinterpret_cast<uint4*>(sB + s * kBBytes + (n >> 3) * 1024 + (n & 7) * 128 + ((kb ^ (n & 7)) << 4)) =
+              make_uint4(h[cc][0], h[cc][1], h[cc][2], h[cc][3]);
+        }
+      }
+      tc::fence_proxy_async_smem();
+      mbar_arrive(&deq[s]);
     }
   } else {
     // ------------------------------------------------------------------ dequantization (warps 2-5)
@@ -197,6 +265,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::tmem_ld32(tmem + (static_cast<uint32_t>(32 * q) << 16) + c0, v);
       const int n = n0 + c0;
       if (!have || row >= p.M || n >= p.N) continue;
+      if (kFp8) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (n + i < p.N) v[i] *= __half2float(p.scale[n + i]);
+      }
       if (p.bias != nullptr) {
 #pragma unroll
         for (int i = 0; i < 32; ++i)
@@ -227,6 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+template <bool kFp8>
 bool smem_ready() {
   static std::mutex mu;
   static bool done[64] = {};
@@ -235,7 +309,7 @@ bool smem_ready() {
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lock(mu);
   if (dev < 64 && !done[dev]) {
-    okv[dev] = opt_in_dynamic_smem(w4a16_gemm_tc_kernel) >= kSmemBytes;
+    okv[dev] = opt_in_dynamic_smem(w4a16_gemm_tc_kernel<kFp8>) >= Layout<kFp8>::kSmemBytes;
     done[dev] = true;
   }
   return dev < 64 && okv[dev];
@@ -253,7 +327,8 @@ bool gemm_tc_ok(const void* x, int64_t ldx, const void* y, int64_t ldy, int64_t 
 
 int launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const void* zeros,
                    const void* bias, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, cudaStream_t st) {
-  if (!smem_ready())
+  constexpr int kSmemBytes = Layout<false>::kSmemBytes;
+  if (!smem_ready<false>())
     return set_error(DK_ERR_UNSUPPORTED, "w4a16 gemm: %d bytes of shared memory do not fit", kSmemBytes);
   CUtensorMap mx, mq, ms, mz;
   if (!make_tensor_map_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, K, M, ldx * 2, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -268,15 +343,50 @@ int launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight, const voi
   p.y = static_cast<__half*>(y);
   p.ldy = ldy;
   p.bias = static_cast<const __half*>(bias);
+  p.scale = nullptr;
   p.M = static_cast<int>(M);
   p.N = static_cast<int>(N);
   p.K = static_cast<int>(K);
   p.ktiles = static_cast<int>(K / kBK);
   p.err = device_info().err_word;
   const dim3 grid(static_cast<unsigned>((N + kBN - 1) / kBN), static_cast<unsigned>((M + kBM - 1) / kBM), 1);
-  cudaError_t e = launch(w4a16_gemm_tc_kernel, grid, dim3(kThreads, 1, 1), kSmemBytes, st, pdl_enabled(),
+  cudaError_t e = launch(w4a16_gemm_tc_kernel<false>, grid, dim3(kThreads, 1, 1), kSmemBytes, st, pdl_enabled(),
                          dim3(1, 1, 1), mx, mq, ms, mz, p);
   if (e != cudaSuccess) return set_error(DK_ERR_CUDA, "w4a16 gemm launch: %s", cudaGetErrorString(e));
+  return DK_OK;
+}
+
+// W8A16 (e4m3 weights [K, N], fp16 per-column scale) on the same tensor-core GEMM: kernels/fp8.py:42-127
+// for large M. Same shape conditions as the int4 GEMM (M >= 128, N >= 128, N % 16 == 0 for the byte
+// tile's 16-byte rows, K % 64 == 0, aligned operands).
+bool gemm_tc_fp8_ok(const void* x, int64_t ldx, const void* wq, int64_t M, int64_t N, int64_t K) {
+  return M >= kBM && N >= kBN && N % 16 == 0 && K % kBK == 0 && K > 0 && aligned16(x) && ldx % 8 == 0 &&
+         aligned16(wq) && M <= INT32_MAX && N <= INT32_MAX;
+}
+
+int launch_gemm_tc_fp8(const void* x, int64_t ldx, const uint8_t* wq, const void* scale, const void* bias, void* y,
+                       int64_t ldy, int64_t M, int64_t N, int64_t K, cudaStream_t st) {
+  constexpr int kSmemBytes = Layout<true>::kSmemBytes;
+  if (!smem_ready<true>())
+    return set_error(DK_ERR_UNSUPPORTED, "w8a16 gemm: %d bytes of shared memory do not fit", kSmemBytes);
+  CUtensorMap mx, mw;
+  if (!make_tensor_map_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, K, M, ldx * 2, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_tensor_map_2d(&mw, wq, CU_TENSOR_MAP_DATA_TYPE_UINT8, N, K, N, kBN, kBK, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return DK_ERR_CUDA;
+  GemmParams p;
+  p.y = static_cast<__half*>(y);
+  p.ldy = ldy;
+  p.bias = static_cast<const __half*>(bias);
+  p.scale = static_cast<const __half*>(scale);
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.ktiles = static_cast<int>(K / kBK);
+  p.err = device_info().err_word;
+  const dim3 grid(static_cast<unsigned>((N + kBN - 1) / kBN), static_cast<unsigned>((M + kBM - 1) / kBM), 1);
+  cudaError_t e = launch(w4a16_gemm_tc_kernel<true>, grid, dim3(kThreads, 1, 1), kSmemBytes, st, pdl_enabled(),
+                         dim3(1, 1, 1), mx, mw, mw, mw, p);
+  if (e != cudaSuccess) return set_error(DK_ERR_CUDA, "w8a16 gemm launch: %s", cudaGetErrorString(e));
   return DK_OK;
 }
 

@@ -397,6 +397,12 @@ Choice8 choose8(int M, int N, int K, const dk_matmul_config* cfg) {
 }  // namespace
 }  // namespace dk
 
+namespace dk {
+bool gemm_tc_fp8_ok(const void* x, int64_t ldx, const void* wq, int64_t M, int64_t N, int64_t K);
+int launch_gemm_tc_fp8(const void* x, int64_t ldx, const uint8_t* wq, const void* scale, const void* bias, void* y,
+                       int64_t ldy, int64_t M, int64_t N, int64_t K, cudaStream_t st);
+}  // namespace dk
+
 extern "C" int dk_w8a16_matmul(const void* x, int64_t ldx, const uint8_t* wq, const void* scale, const void* bias,
                                void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, const dk_matmul_config* cfg,
                                dk_stream_t stream) {
@@ -418,6 +424,8 @@ extern "C" int dk_w8a16_matmul(const void* x, int64_t ldx, const uint8_t* wq, co
     if (e != cudaSuccess) return set_error(DK_ERR_CUDA, "w8a16 generic launch: %s", cudaGetErrorString(e));
     return DK_OK;
   }
+  if (!(flags & DK_FLAG_GEMV) && gemm_tc_fp8_ok(x, ldx, wq, M, N, K))
+    return launch_gemm_tc_fp8(x, ldx, wq, scale, bias, y, ldy, M, N, K, st);
   CUtensorMap mw;
   if (!make_tensor_map_2d(&mw, wq, CU_TENSOR_MAP_DATA_TYPE_UINT8, N, K, N, 32, kRows, CU_TENSOR_MAP_SWIZZLE_NONE))
     return DK_ERR_CUDA;

@@ -106,3 +106,21 @@ def test_fp8_golden(golden):
     wc = torch.from_numpy(g["w8_wq"]).cuda().view(FP8)
     out = w8a16_matmul(xc, wc, sc, bias=bc)
     np.testing.assert_allclose(out.float().cpu().numpy(), g["w8_ref"], **MATMUL_TOL)
+
+
+@pytest.mark.parametrize("M,N,K,bias", [(128, 128, 64, False), (200, 208, 192, True), (256, 1536, 1536, True),
+                                        (512, 17920, 1536, False), (130, 1536, 8960, False)])
+def test_w8a16_tensor_core_gemm(M, N, K, bias):
+    """M >= 128 runs the tcgen05 GEMM (e4m3 tile converted to fp16 in shared memory, scale on the
+    fp32 accumulator): same tolerance against the oracle, deterministic, and close to the 16-row
+    decode kernel (DECODE_GEMV)."""
+    from kernels.fp8 import FP8, w8a16_matmul
+
+    x, _, wq, s, b = _case(M, N, K, seed=M + K, bias=bias)
+    xc, sc, bc = to_cuda(x, s, b)
+    wc = torch.from_numpy(wq).cuda().view(FP8)
+    out = w8a16_matmul(xc, wc, sc, bias=bc)
+    np.testing.assert_allclose(out.float().cpu().numpy(), ref.w8a16_ref(x, wq, s, b), **MATMUL_TOL)
+    assert torch.equal(out, w8a16_matmul(xc, wc, sc, bias=bc))
+    gemv = w8a16_matmul(xc, wc, sc, bias=bc, config={"DECODE_GEMV": True})
+    torch.testing.assert_close(out.float(), gemv.float(), **MATMUL_TOL)
