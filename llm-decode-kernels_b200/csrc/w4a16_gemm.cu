@@ -31,19 +31,23 @@
 namespace dk {
 namespace {
 
-constexpr int kBM = 128, kBN = 128, kBK = 64;
-constexpr int kStages = 4;
-constexpr int kThreads = 192;                  // warp 0 TMA, warp 1 TMEM + MMA, warps 2-5 dequant + epilogue
-constexpr int kABytes = kBM * kBK * 2;         // 16 KB x tile
+constexpr int kBM = 256, kBN = 128, kBK = 64;  // CTA tile: two 128-row accumulators share one B tile
+constexpr int kHalfRows = 128;                 // rows per tcgen05.mma (M = 128, cta_group::1)
+constexpr int kThreads = 320;                  // warp 0 TMA, warp 1 TMEM + MMA, warps 2-9 dequant + epilogue
+constexpr int kDeqThreads = 256;
+constexpr int kTmemCols = 2 * kBN;             // two fp32 128 x 128 accumulators
+constexpr int kAHalfBytes = kHalfRows * kBK * 2;  // 16 KB: one 128-row x 64 box of x
+constexpr int kABytes = 2 * kAHalfBytes;
 constexpr int kBBytes = kBN * kBK * 2;         // 16 KB dequantized weight tile
 constexpr int kSZBytes = kBN * 2;              // one scale (or zero) row (int4 format)
 
-// Shared-memory layout per weight format: int4 (packed rows [8][128] int32 + scale and zero rows) or
-// e4m3 (the raw [64 K][128 N] byte tile).
+// Shared-memory layout per weight format: int4 (packed rows [8][128] int32 + scale and zero rows, 4
+// stages) or e4m3 (the raw [64 K][128 N] byte tile, 3 stages).
 template <bool kFp8>
 struct Layout {
+  static constexpr int kStages = kFp8 ? 3 : 4;
   static constexpr int kWBytes = kFp8 ? kBK * kBN : (kBK / 8) * kBN * 4;  // 8 KB e4m3 / 4 KB int4
-  static constexpr uint32_t kStageTx = kABytes + kWBytes + (kFp8 ? 0 : 2 * kSZBytes);
+  static constexpr uint32_t kWTx = kWBytes + (kFp8 ? 0 : 2 * kSZBytes);
   static constexpr int kOffB = kStages * kABytes;
   static constexpr int kOffW = kOffB + kStages * kBBytes;
   static constexpr int kOffS = kOffW + kStages * kWBytes;
@@ -75,11 +79,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                          const __grid_constant__ CUtensorMap ms, const __grid_constant__ CUtensorMap mz,
                          const GemmParams p) {
   using Lay = Layout<kFp8>;
+  constexpr int kStages = Lay::kStages;
   constexpr int kWBytes = Lay::kWBytes, kOffB = Lay::kOffB, kOffW = Lay::kOffW, kOffS = Lay::kOffS,
                 kOffZ = Lay::kOffZ, kOffBar = Lay::kOffBar;
-  constexpr uint32_t kStageTx = Lay::kStageTx;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte aligned base by pointer arithmetic on the shared array (accesses stay shared-space)
+  uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   uint8_t* sA = smem;
   uint8_t* sB = smem + kOffB;
   uint8_t* sW = smem + kOffW;
@@ -94,11 +99,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * kBN, m0 = blockIdx.y * kBM;
+  const bool two = m0 + kHalfRows < p.M;  // second 128-row half has rows (uniform per CTA)
+  const uint32_t stage_tx = Lay::kWTx + (two ? 2 : 1) * kAHalfBytes;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&deq[s], 128);
+      mbar_init(&deq[s], kDeqThreads);
       mbar_init(&empty[s], 1);
     }
     mbar_init(done, 1);
@@ -106,7 +113,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbar_init();
   }
   if (warp == 1) {
-    tc::tmem_alloc(tmem_slot, kBN);
+    tc::tmem_alloc(tmem_slot, kTmemCols);
     tc::tmem_relinquish();
   }
   tc::fence_before_sync();
@@ -132,8 +139,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&full[s], kStageTx);
+        mbar_arrive_expect_tx(&full[s], stage_tx);
         tma_load_2d(sA + s * kABytes, &mx, kt * kBK, m0, &full[s]);
+        if (two) tma_load_2d(sA + s * kABytes + kAHalfBytes, &mx, kt * kBK, m0 + kHalfRows, &full[s]);
         if (kFp8) {
           tma_load_2d(sW + s * kWBytes, &mq, n0, kt * kBK, &full[s]);  // e4m3 [64 K rows][128 N]
         } else {
@@ -146,7 +154,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = tc::idesc_f16_f32(kBM, kBN);
+      constexpr uint32_t idesc = tc::idesc_f16_f32(kHalfRows, kBN);
       for (int kt = 0; kt < p.ktiles; ++kt) {
         const int s = kt % kStages;
         const uint32_t par = (kt / kStages) & 1;
@@ -158,20 +166,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::fence_after_sync();
         const uint32_t a0 = smem_addr(sA + s * kABytes), b0 = smem_addr(sB + s * kBBytes);
 #pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk)
-          tc::mma_f16(tmem, tc::sdesc_k_sw128(a0 + 32 * kk), tc::sdesc_k_sw128(b0 + 32 * kk), idesc,
-                      (kt | kk) != 0 ? 1u : 0u);
+        for (int kk = 0; kk < kBK / 16; ++kk) {
+          const uint64_t bdesc = tc::sdesc_k_sw128(b0 + 32 * kk);
+          const uint32_t acc = (kt | kk) != 0 ? 1u : 0u;
+          tc::mma_f16(tmem, tc::sdesc_k_sw128(a0 + 32 * kk), bdesc, idesc, acc);
+          if (two) tc::mma_f16(tmem + kBN, tc::sdesc_k_sw128(a0 + kAHalfBytes + 32 * kk), bdesc, idesc, acc);
+        }
         tc::commit(&empty[s]);  // the stage is free once these MMAs have read it
       }
-      tc::commit(done);  // the accumulator is final once every MMA issued above has completed
+      tc::commit(done);  // the accumulators are final once every MMA issued above has completed
     }
   } else if (kFp8) {
-    // ------------------------------------------------------------ e4m3 -> fp16 (warps 2-5), transposing
-    // Lane c owns columns 4c..4c+3; of the stage's 8 K-blocks (8 rows each) warp w takes the pair
-    // 2 * ((w + c / 2) % 4) + {0, 1}, so the 4 warps cover all 8 and the lanes of one store spread
-    // over the bank groups. A K-block: 8 row words (4 columns each) -> PRMT pairs rows (2i, 2i+1)
-    // per column -> cvt gives fp16 (k even, k odd) -> one 16-byte chunk per column.
+    // ------------------------------------------------------------ e4m3 -> fp16 (warps 2-9), transposing
+    // Lane c owns columns 4c..4c+3; of the stage's 8 K-blocks (8 rows each) warp w takes block
+    // (w + c / 2) % 8, so the 8 warps cover all 8 and the lanes of one store spread over the bank
+    // groups. A K-block: 8 row words (4 columns each) -> PRMT pairs rows (2i, 2i+1) per column ->
+    // cvt gives fp16 (k even, k odd) -> one 16-byte chunk per column.
     const int c = lane, w = warp - 2;
+    const int kb = (w + (c >> 1)) & 7;
     for (int kt = 0; kt < p.ktiles; ++kt) {
       const int s = kt % kStages;
       if (!mbar_wait(&full[s], (kt / kStages) & 1, p.err, DK_DEVERR_WAIT_FULL)) {
@@ -179,36 +191,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       const uint32_t* raw = reinterpret_cast<const uint32_t*>(sW + s * kWBytes);  // row k: 32 words
+      uint32_t r[8];
 #pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int kb = 2 * ((w + (c >> 1)) & 3) + i;
-        uint32_t r[8];
+      for (int j = 0; j < 8; ++j) r[j] = raw[(kb * 8 + j) * (kBN / 4) + c];
+      uint32_t h[4][4];  // [column][k pair]
 #pragma unroll
-        for (int j = 0; j < 8; ++j) r[j] = raw[(kb * 8 + j) * (kBN / 4) + c];
-        uint32_t h[4][4];  // [column][k pair]
+      for (int j = 0; j < 4; ++j) {
+        uint32_t lo, hi;
+        e4m3x4_to_f16(prmt(r[2 * j], r[2 * j + 1], 0x5140u), lo, hi);  // columns 0, 1 of rows 2j, 2j+1
+        h[0][j] = lo;
+        h[1][j] = hi;
+        e4m3x4_to_f16(prmt(r[2 * j], r[2 * j + 1], 0x7362u), lo, hi);  // columns 2, 3
+        h[2][j] = lo;
+        h[3][j] = hi;
+      }
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint32_t lo, hi;
-          e4m3x4_to_f16(prmt(r[2 * j], r[2 * j + 1], 0x5140u), lo, hi);  // columns 0, 1 of rows 2j, 2j+1
-          h[0][j] = lo;
-          h[1][j] = hi;
-          e4m3x4_to_f16(prmt(r[2 * j], r[2 * j + 1], 0x7362u), lo, hi);  // columns 2, 3
-          h[2][j] = lo;
-          h[3][j] = hi;
-        }
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          const int n = 4 * c + cc;  // row n of the B tile, chunk kb
-          *reinterpret_cast<uint4*>(sB + s * kBBytes + (n >> 3) * 1024 + (n & 7) * 128 + ((kb ^ (n & 7)) << 4)) =
-              make_uint4(h[cc][0], h[cc][1], h[cc][2], h[cc][3]);
-        }
+      for (int cc = 0; cc < 4; ++cc) {
+        const int n = 4 * c + cc;  // row n of the B tile, chunk kb
+        *reinterpret_cast<uint4*>(sB + s * kBBytes + (n >> 3) * 1024 + (n & 7) * 128 + ((kb ^ (n & 7)) << 4)) =
+            make_uint4(h[cc][0], h[cc][1], h[cc][2], h[cc][3]);
       }
       tc::fence_proxy_async_smem();
       mbar_arrive(&deq[s]);
     }
   } else {
-    // ------------------------------------------------------------------ dequantization (warps 2-5)
-    const int t = threadIdx.x - 64;  // output column n0 + t, row t of the B tile
+    // ------------------------------------------------------------------ dequantization (warps 2-9)
+    const int t = threadIdx.x - 64;
+    const int col = t & (kBN - 1);  // output column n0 + col, row col of the B tile
+    const int c0 = (t >> 7) * 4;    // this thread's half of the 8 packed rows (16-byte chunks)
     const uint32_t mul2 = 0x2C003C00u;  // (1.0, 1/16)
     for (int kt = 0; kt < p.ktiles; ++kt) {
       const int s = kt % kStages;
@@ -217,16 +227,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       const uint32_t* w = reinterpret_cast<const uint32_t*>(sW + s * kWBytes);
-      const __half sc = reinterpret_cast<const __half*>(sS + s * kSZBytes)[t];
-      const __half zc = reinterpret_cast<const __half*>(sZ + s * kSZBytes)[t];
+      const __half sc = reinterpret_cast<const __half*>(sS + s * kSZBytes)[col];
+      const __half zc = reinterpret_cast<const __half*>(sZ + s * kSZBytes)[col];
       const __half lo = __hneg(__hadd(__float2half_rn(1024.f), zc));  // -(1024 + z), exact
       const __half hi = __hneg(__hadd(__float2half_rn(64.f), zc));    // -(64 + z), exact
       const uint32_t add2 = half2_bits(lo, hi);
       const uint32_t sc2 = half2_bits(sc, sc);
-      uint8_t* brow = sB + s * kBBytes + (t >> 3) * 1024 + (t & 7) * 128;
+      uint8_t* brow = sB + s * kBBytes + (col >> 3) * 1024 + (col & 7) * 128;
 #pragma unroll
-      for (int c = 0; c < kBK / 8; ++c) {  // packed row c = K values 8c..8c+7 = 16-byte chunk c of row t
-        const uint32_t word = w[c * kBN + t];
+      for (int i = 0; i < 4; ++i) {  // packed row c = K values 8c..8c+7 = 16-byte chunk c of row col
+        const int c = c0 + i;
+        const uint32_t word = w[c * kBN + col];
         uint32_t h[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -234,7 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t u = lop3_and_or(v, 0x00F0000Fu, 0x64006400u);  // (1024 + q_2j, 1024 + 16 q_2j+1)
           h[j] = hmul2_rn(hfma2_rn(u, mul2, add2), sc2);                   // ((q - z) * s) for both
         }
-        *reinterpret_cast<uint4*>(brow + ((c ^ (t & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<uint4*>(brow + ((c ^ (col & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
       }
       tc::fence_proxy_async_smem();  // these generic-proxy writes feed tcgen05.mma (async proxy)
       mbar_arrive(&deq[s]);
@@ -252,19 +263,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
   }
 
-  // ------------------------------------------------------------------ epilogue (warps 2-5)
+  // ------------------------------------------------------------------ epilogue (warps 2-9)
   if (warp >= 2) {
     const bool have = mbar_wait(done, 0, p.err, DK_DEVERR_WAIT_FULL) && !failed;
     __syncwarp();  // tcgen05.ld is warp-collective: reconverge after the spin above
     tc::fence_after_sync();
-    const int q = warp & 3;  // this warp's TMEM lane quarter: accumulator rows 32q..32q+31
-    const int row = m0 + 32 * q + lane;
+    const int q = warp & 3;          // this warp's TMEM lane quarter (warp id mod 4)
+    const int a = (warp - 2) >> 2;   // accumulator: rows 0-127 or 128-255 of the tile
+    const int row = m0 + a * kHalfRows + 32 * q + lane;
+    const bool used = a == 0 || two;
 #pragma unroll 1
     for (int c0 = 0; c0 < kBN; c0 += 32) {
       float v[32];
-      tc::tmem_ld32(tmem + (static_cast<uint32_t>(32 * q) << 16) + c0, v);
+      tc::tmem_ld32(tmem + (static_cast<uint32_t>(32 * q) << 16) + a * kBN + c0, v);
       const int n = n0 + c0;
-      if (!have || row >= p.M || n >= p.N) continue;
+      if (!have || !used || row >= p.M || n >= p.N) continue;
       if (kFp8) {
 #pragma unroll
         for (int i = 0; i < 32; ++i)
@@ -296,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     __syncwarp();
     tc::fence_after_sync();
-    tc::tmem_dealloc(tmem, kBN);
+    tc::tmem_dealloc(tmem, kTmemCols);
   }
 }
 
@@ -321,7 +334,7 @@ bool smem_ready() {
 // inside the tensors), 16-byte aligned operands, x rows 16-byte aligned; group_size 128.
 bool gemm_tc_ok(const void* x, int64_t ldx, const void* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
                 int64_t group_size) {
-  return M >= kBM && N >= kBN && N % 8 == 0 && K % 128 == 0 && group_size == 128 && aligned16(x) && ldx % 8 == 0 &&
+  return M >= kHalfRows && N >= kBN && N % 8 == 0 && K % 128 == 0 && group_size == 128 && aligned16(x) && ldx % 8 == 0 &&
          y != nullptr && M <= INT32_MAX && N <= INT32_MAX;
 }
 
@@ -331,7 +344,8 @@ int launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight, const voi
   if (!smem_ready<false>())
     return set_error(DK_ERR_UNSUPPORTED, "w4a16 gemm: %d bytes of shared memory do not fit", kSmemBytes);
   CUtensorMap mx, mq, ms, mz;
-  if (!make_tensor_map_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, K, M, ldx * 2, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+  if (!make_tensor_map_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, K, M, ldx * 2, kBK, kHalfRows,
+                          CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_tensor_map_2d(&mq, qweight, CU_TENSOR_MAP_DATA_TYPE_INT32, N, K / 8, N * 4, kBN, kBK / 8,
                           CU_TENSOR_MAP_SWIZZLE_NONE) ||
       !make_tensor_map_2d(&ms, scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, N, K / 128, N * 2, kBN, 1,
@@ -360,7 +374,7 @@ int launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight, const voi
 // for large M. Same shape conditions as the int4 GEMM (M >= 128, N >= 128, N % 16 == 0 for the byte
 // tile's 16-byte rows, K % 64 == 0, aligned operands).
 bool gemm_tc_fp8_ok(const void* x, int64_t ldx, const void* wq, int64_t M, int64_t N, int64_t K) {
-  return M >= kBM && N >= kBN && N % 16 == 0 && K % kBK == 0 && K > 0 && aligned16(x) && ldx % 8 == 0 &&
+  return M >= kHalfRows && N >= kBN && N % 16 == 0 && K % kBK == 0 && K > 0 && aligned16(x) && ldx % 8 == 0 &&
          aligned16(wq) && M <= INT32_MAX && N <= INT32_MAX;
 }
 
@@ -370,7 +384,8 @@ int launch_gemm_tc_fp8(const void* x, int64_t ldx, const uint8_t* wq, const void
   if (!smem_ready<true>())
     return set_error(DK_ERR_UNSUPPORTED, "w8a16 gemm: %d bytes of shared memory do not fit", kSmemBytes);
   CUtensorMap mx, mw;
-  if (!make_tensor_map_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, K, M, ldx * 2, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+  if (!make_tensor_map_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, K, M, ldx * 2, kBK, kHalfRows,
+                          CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_tensor_map_2d(&mw, wq, CU_TENSOR_MAP_DATA_TYPE_UINT8, N, K, N, kBN, kBK, CU_TENSOR_MAP_SWIZZLE_NONE))
     return DK_ERR_CUDA;
   GemmParams p;

@@ -10,6 +10,8 @@
         five launches of one W4A16 GEMV of shape [M, K] x [K, N].
     python .../profile_cases.py gemm M N K
         three launches of the tcgen05 W4A16 GEMM of shape [M, K] x [K, N], then 20 timed ones.
+    python .../profile_cases.py chain [n]
+        the cost of a kernel boundary: n tiny launches in one CUDA graph, with and without PDL.
     python .../profile_cases.py attention
         28 decode-attention launches (one per layer, Qwen2.5-1.5B heads, position 767) eagerly,
         then as a CUDA graph replayed 21 times.
@@ -109,6 +111,33 @@ def gemm(M, N, K):
     print(f"gemm M={M} N={N} K={K}: {ms * 1e3:.1f} us, {2 * M * N * K / ms / 1e9:.1f} TFLOP/s")
 
 
+def chain(n="200"):
+    """Cost of a kernel boundary: a CUDA graph of `n` back-to-back launches of the smallest
+    libdecodek kernel (SwiGLU of one 16-wide row), with programmatic dependent launch on and off."""
+    from kernels import _lib
+    from kernels.bench.harness import capture
+    from kernels.swiglu import swiglu_fused
+
+    n = int(n)
+    x = torch.randn(1, 32, device="cuda").half()
+    for pdl in (1, 0):
+        _lib.set_pdl(bool(pdl))
+        swiglu_fused(x)
+        torch.cuda.synchronize()
+        graph, _ = capture(lambda: [swiglu_fused(x) for _ in range(n)])
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        e0.record()
+        for _ in range(10):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        print(f"chain of {n} tiny launches, pdl={pdl}: {e0.elapsed_time(e1) / 10 / n * 1e3:.3f} us per launch")
+        del graph
+    _lib.set_pdl(True)
+
+
 def attention():
     a = config.QWEN15
     nq, nkv, hd = a["num_attention_heads"], a["num_key_value_heads"], a["head_dim"]
@@ -140,7 +169,7 @@ def attention():
     print(f"attention: {e0.elapsed_time(e1) * 1e3 / (20 * layers):.2f} us/launch (position {pos})")
 
 
-CASES = {"decode": decode, "gemv_layer": gemv_layer, "gemv": gemv, "attention": attention, "gemm": gemm}
+CASES = {"decode": decode, "gemv_layer": gemv_layer, "gemv": gemv, "attention": attention, "gemm": gemm, "chain": chain}
 
 if __name__ == "__main__":
     if len(sys.argv) < 2 or sys.argv[1] not in CASES:

@@ -81,18 +81,30 @@ def tp_model(dtype, device):
     return transformers.Qwen2ForCausalLM(cfg).to(device=device, dtype=dtype).eval()
 
 
-def _runner_worker(rank, world, port, q):
+def tp_model_7b_heads(dtype, device):
+    """A tiny Qwen2 with Qwen2.5-7B's head layout (28 query / 4 kv heads of 128): at 8 ranks each kv
+    head is replicated on 2 ranks, which take 3 and 4 of its 7 query heads."""
+    cfg = transformers.Qwen2Config(
+        vocab_size=1024, hidden_size=256, intermediate_size=2048, num_hidden_layers=2, num_attention_heads=28,
+        num_key_value_heads=4, head_dim=128, max_position_embeddings=256, tie_word_embeddings=False,
+        rms_norm_eps=1e-6)
+    torch.manual_seed(0)
+    return transformers.Qwen2ForCausalLM(cfg).to(device=device, dtype=dtype).eval()
+
+
+def _runner_worker(rank, world, port, q, arch="tp"):
     import torch.distributed as dist
 
     from kernels.e2e.model import QwenRunner, make_backend
     from kernels.tp import TensorParallel
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.set_num_threads(1)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         torch.manual_seed(0)
-        model = tp_model(torch.float32, "cpu")
-        ids = torch.randint(0, 512, (2, 10))
+        model = tp_model(torch.float32, "cpu") if arch == "tp" else tp_model_7b_heads(torch.float32, "cpu")
+        ids = torch.randint(0, 512, (2, 10))  # within both models' vocabularies
         tp = TensorParallel(mode="nccl")
         shard = QwenRunner(model, make_backend("fp16"), max_len=32, batch=2, tp=tp)
         full = QwenRunner(model, make_backend("fp16"), max_len=32, batch=2)
@@ -135,6 +147,27 @@ def test_tp_runner_world2_gloo_matches_unsharded():
     for rank, err, nq, nkv in res:
         assert (nq, nkv) == (2, 1)
         assert err < 1e-4, err
+
+
+def test_tp_runner_world8_gloo_7b_head_layout():
+    """8 ranks on CPU with the 7B head layout (uneven 3/4 query heads per rank, replicated kv heads,
+    MLP and vocabulary shards of 2 groups / 128 rows): the same logits and greedy tokens as the
+    unsharded runner."""
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_runner_worker, args=(r, 8, port, q, "7b")) for r in range(8)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    res = sorted(q.get(timeout=5) for _ in range(8))
+    assert [(nq, nkv) for _, _, nq, nkv in res] == [(3, 1), (4, 1)] * 4
+    for rank, err, nq, nkv in res:
+        assert err < 1e-4, (rank, err)
 
 
 # -------------------------------------------------------------------------- fused kernel on GPUs
