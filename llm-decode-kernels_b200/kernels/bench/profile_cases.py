@@ -12,9 +12,9 @@
         three launches of the tcgen05 W4A16 GEMM of shape [M, K] x [K, N], then 20 timed ones.
     python .../profile_cases.py chain [n]
         the cost of a kernel boundary: n tiny launches in one CUDA graph, with and without PDL.
-    python .../profile_cases.py attention
-        28 decode-attention launches (one per layer, Qwen2.5-1.5B heads, position 767) eagerly,
-        then as a CUDA graph replayed 21 times.
+    python .../profile_cases.py attention [pos] [splits]
+        28 decode-attention launches (one per layer, Qwen2.5-1.5B heads, position 767 by default,
+        automatic split) eagerly, then as a CUDA graph replayed 21 times.
 
 Every case allocates at most a few hundred MB and ends by itself.
 """
@@ -138,10 +138,10 @@ def chain(n="200"):
     _lib.set_pdl(True)
 
 
-def attention():
+def attention(pos="767", splits="0"):
     a = config.QWEN15
     nq, nkv, hd = a["num_attention_heads"], a["num_key_value_heads"], a["head_dim"]
-    layers, max_len, pos = a["num_hidden_layers"], 2048, 767
+    layers, max_len, pos, splits = a["num_hidden_layers"], 2048, int(pos), int(splits)
     qkv = torch.randn(1, 1, (nq + 2 * nkv) * hd, device="cuda").half()
     kc = torch.randn(layers, 1, nkv, max_len, hd, device="cuda").half()
     vc = torch.randn(layers, 1, nkv, max_len, hd, device="cuda").half()
@@ -151,7 +151,7 @@ def attention():
 
     def run():
         for i in range(layers):
-            decode_attention(qkv, kc[i], vc[i], p, cos, sin, nq, nkv, static_cache=True)
+            decode_attention(qkv, kc[i], vc[i], p, cos, sin, nq, nkv, splits=splits, static_cache=True)
 
     run()
     torch.cuda.synchronize()
@@ -166,10 +166,17 @@ def attention():
         g.replay()
     e1.record()
     torch.cuda.synchronize()
-    print(f"attention: {e0.elapsed_time(e1) * 1e3 / (20 * layers):.2f} us/launch (position {pos})")
+    print(f"attention: {e0.elapsed_time(e1) * 1e3 / (20 * layers):.2f} us/launch (position {pos}, splits {splits})")
 
 
-CASES = {"decode": decode, "gemv_layer": gemv_layer, "gemv": gemv, "attention": attention, "gemm": gemm, "chain": chain}
+def attention_sweep():
+    """Decode attention us/launch over positions x cluster splits (one process)."""
+    for pos in ("511", "1023", "2047"):
+        for splits in ("2", "4", "8", "16"):
+            attention(pos, splits)
+
+
+CASES = {"decode": decode, "gemv_layer": gemv_layer, "gemv": gemv, "attention": attention, "gemm": gemm, "chain": chain, "attention_sweep": attention_sweep}
 
 if __name__ == "__main__":
     if len(sys.argv) < 2 or sys.argv[1] not in CASES:

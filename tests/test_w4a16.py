@@ -179,3 +179,11 @@ def test_no_device_errors_recorded():
 
     _check(16, 17920, 1536)
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("M,N,K,bn", [(4, 151936, 1536, 0), (16, 40000, 1024, 256), (1, 9472, 3584, 256),
+                                      (3, 2368 * 32, 512, 128)])
+def test_tail_tiles(M, N, K, bn):
+    """Column counts that leave some persistent CTAs a partial last tile (fewer chunks than the tile
+    holds), with M <= 8 and M = 16 variants."""
+    _check(M, N, K, config={"BLOCK_N": bn} if bn else None)
