@@ -427,8 +427,14 @@ extern "C" int dk_decode_attention(const void* qkv, void* k_cache, void* v_cache
   if (!aligned16(qkv) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out) ||
       (reinterpret_cast<uintptr_t>(cos) & 7) || (reinterpret_cast<uintptr_t>(sin) & 7) || (rope_stride & 3))
     return set_error(DK_ERR_ALIGN, "decode_attention: qkv, caches and out need 16-byte alignment, cos/sin 8 bytes");
-  // S: a power of two (every rank combines an even number of output dims), at most 16
-  int want = splits > 0 ? splits : static_cast<int>(std::min<int64_t>(kMaxSplit, (max_len + 127) / 128));
+  // S: a power of two (every rank combines an even number of output dims), at most 16. Automatic:
+  // enough slices for one 128-position chunk pair each at max_len, but no more clusters than one wave
+  // of CTAs (one per SM) once the (kv head, sequence) pairs alone fill the GPU - at batch 16 a 16-way
+  // split ran 3.5 waves of CTAs.
+  const int64_t per_wave = std::max<int64_t>(1, device_info().num_sms / (B * nkv));
+  int want = splits > 0 ? splits
+                        : static_cast<int>(std::min<int64_t>(std::min<int64_t>(kMaxSplit, (max_len + 127) / 128),
+                                                             per_wave));
   want = std::max(1, std::min(want, kMaxSplit));
   int S = 1;
   while (S * 2 <= want) S *= 2;

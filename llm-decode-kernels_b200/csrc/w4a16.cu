@@ -907,6 +907,8 @@ Choice choose_uncached(int M, int units, int K, bool swiglu, const dk_matmul_con
   const DeviceInfo& dev = device_info();
   const int stages_total = (K + 256 - 1) / 256;
   const int nt = M <= 8 ? 1 : 2;
+  // M > 8 variants hold one CTA per SM (registers), so their ring may use the SM's whole shared memory
+  const size_t budget = nt == 1 ? kSmemBudget : 2 * kSmemBudget;
   Choice best = {0, 0, 0, 0, 0, 1e300};
   // requested split: clamped to what K allows (every rank needs at least one 256-wide stage)
   int want_split = (cfg && cfg->split_k > 0) ? std::min(cfg->split_k, std::min(8, stages_total)) : 0;
@@ -929,7 +931,7 @@ Choice choose_uncached(int M, int units, int K, bool swiglu, const dk_matmul_con
       const int stages_per_cta = sps * (split > 1 ? 1 : (tiles + dev.num_sms - 1) / dev.num_sms);
       int nbuf = std::min(std::max(stages_per_cta, 2), 16);
       SmemLayout L = smem_layout(cw, nbuf, M, pitch, split);
-      while (nbuf > 2 && static_cast<size_t>(L.total) + 1024 > kSmemBudget) {
+      while (nbuf > 2 && static_cast<size_t>(L.total) + 1024 > budget) {
         --nbuf;
         L = smem_layout(cw, nbuf, M, pitch, split);
       }
@@ -1077,6 +1079,10 @@ bool gemm_tc_ok(const void* x, int64_t ldx, const void* y, int64_t ldy, int64_t 
                 int64_t group_size);
 int launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const void* zeros,
                    const void* bias, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, cudaStream_t st);
+void skinny_choice(int64_t rows, int64_t N, int64_t K, int* mb_out, int* split_out);
+int launch_skinny_tc(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const void* zeros,
+                     const void* bias, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, bool static_weights,
+                     cudaStream_t st);
 }  // namespace dk
 
 extern "C" int dk_w4a16_matmul(const void* x, int64_t ldx, const int32_t* qweight, const void* scales,
@@ -1101,6 +1107,7 @@ extern "C" int dk_w4a16_matmul(const void* x, int64_t ldx, const int32_t* qweigh
   }
   if (!(flags & DK_FLAG_GEMV) && gemm_tc_ok(x, ldx, y, ldy, M, N, K, group_size))
     return launch_gemm_tc(x, ldx, qweight, scales, zeros, bias, y, ldy, M, N, K, st);
+
   return run_fast(x, ldx, qweight, scales, zeros, bias, y, ldy, M, N, K, group_size, cfg, 0, NormArgs(), st);
 }
 

@@ -1,6 +1,6 @@
 """Small, self-terminating workloads for profiler captures (ncu launch lists and single-kernel reports).
 
-    python llm-decode-kernels_b200/kernels/bench/profile_cases.py decode [ours|fp16] [steps] [l2_prefetch 0|1]
+    python llm-decode-kernels_b200/kernels/bench/profile_cases.py decode [ours|fp16] [steps] [l2_prefetch 0|1] [batch]
         Qwen2.5-1.5B (random init) batch-1 decode through the CUDA graph; the profiler range
         (cudaProfilerStart/Stop) covers exactly `steps` graph replays at context 512.
     python .../profile_cases.py gemv_layer
@@ -38,13 +38,14 @@ def _q(N, K):
     return quantize_rtn((torch.randn(N, K, device="cuda") * 0.02).half(), config.GROUP_SIZE)
 
 
-def decode(backend="ours", steps="2", l2_prefetch="0"):
+def decode(backend="ours", steps="2", l2_prefetch="0", batch="1"):
     from kernels.e2e.model import QwenRunner, make_backend, random_qwen2
     from kernels.e2e.run import GraphDecoder
-    steps = int(steps)
+    steps, batch = int(steps), int(batch)
     model = random_qwen2(config.QWEN15, dtype=torch.float16, device="cuda", seed=0)
-    ids = torch.randint(0, config.QWEN15["vocab_size"], (1, 512), device="cuda")
-    dec = GraphDecoder(QwenRunner(model, make_backend(backend), max_len=2048, l2_prefetch=l2_prefetch != "0"))
+    ids = torch.randint(0, config.QWEN15["vocab_size"], (batch, 512), device="cuda")
+    dec = GraphDecoder(QwenRunner(model, make_backend(backend), max_len=2048, batch=batch,
+                                  l2_prefetch=l2_prefetch != "0"))
     dec.capture(ids)
     dec.prefill(ids)
     for _ in range(5):

@@ -15,6 +15,8 @@ pytestmark = pytest.mark.gpu
 @pytest.mark.parametrize("M,N,K,bias", [
     (128, 128, 128, False), (200, 200, 256, True), (256, 1536, 1536, True), (512, 2048, 1536, False),
     (130, 17920, 1536, False), (384, 1536, 8960, False), (129, 256, 4096, True), (640, 4608, 3584, True),
+    # 256-column tiles (taken when the 256 x 256 tile grid has at least one tile per SM)
+    (1024, 17920, 1536, True), (520, 38008, 512, False),
 ])
 def test_gemm_matches_oracle(M, N, K, bias):
     from kernels.w4a16 import w4a16_matmul
