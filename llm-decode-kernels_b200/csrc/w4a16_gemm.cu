@@ -416,7 +416,7 @@ int launch_gemm_tc_fp8(const void* x, int64_t ldx, const uint8_t* wq, const void
 }  // namespace dk
 
 // ------------------------------------------------------------------------------------------------
-// Small-M W4A16 on tcgen05 (16 <= M < 128 rows: batched decode), "swap AB": the MMA's M dimension is
+// Small-M W4A16 (and W8A16) on tcgen05 (16 <= M < 128 rows: batched decode), "swap AB": the MMA's M dimension is
 // 128 output columns (the dequantized weight tile is the A operand) and its N dimension is the batch
 // rows padded to MB = 16, 32 or 64 (x is the B operand), so the tensor core does no wasted work at small
 // batch and the weights are read once for all rows. Replaces the reference's small-M tile kernel
@@ -435,17 +435,19 @@ namespace {
 
 constexpr int kSkStages = 4;
 constexpr int kSkBN = 128;                         // output columns per CTA (the MMA's M)
-constexpr int kSkWBytes = (kBK / 8) * kSkBN * 4;   // 4 KB packed weights per 64-K step
+constexpr int kSkWBytes = (kBK / 8) * kSkBN * 4;   // 4 KB packed int4 weights per 64-K step
+constexpr int kSkWSlot = kBK * kSkBN;              // ring slot: 8 KB (the e4m3 tile [64 K][128 N])
 constexpr int kSkSZ = kSkBN * 2;                   // one scale (or zero) row
 constexpr int kSkABytes = kSkBN * kBK * 2;         // 16 KB dequantized weight tile
 constexpr int kSkXBudget = 96 * 1024;              // staged x slice per CTA
 constexpr int kSkMaxSplit = 8;
 constexpr int kSkOffW = kSkStages * kSkABytes;
-constexpr int kSkOffS = kSkOffW + kSkStages * kSkWBytes;
+constexpr int kSkOffS = kSkOffW + kSkStages * kSkWSlot;
 constexpr int kSkOffZ = kSkOffS + kSkStages * kSkSZ;
 constexpr int kSkOffX = kSkOffZ + kSkStages * kSkSZ;  // 1024-aligned (all terms are multiples of 1024)
 
 struct SkinnyParams {
+  const __half* scale;  // e4m3 format: per-column scale applied to the fp32 sum (kernels/fp8.py:81-82)
   const __half* x;
   int64_t ldx;
   __half* y;
@@ -462,7 +464,7 @@ __host__ __device__ constexpr int skinny_smem_bytes(int MB, int ks) {
   return kSkOffX + ks * MB * 128 + (2 * kSkStages + 2) * 8 + 16 + 1024;
 }
 
-template <int MB>
+template <int MB, bool kFp8>
 __global__ void __launch_bounds__(kThreads, 1)
     w4a16_skinny_tc_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap ms,
                            const __grid_constant__ CUtensorMap mz, const SkinnyParams p) {
@@ -519,8 +521,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!p.static_weights) pdl_wait();
     if (lane == 0) {
       prefetch_tensormap(&mq);
-      prefetch_tensormap(&ms);
-      prefetch_tensormap(&mz);
+      if (!kFp8) {
+        prefetch_tensormap(&ms);
+        prefetch_tensormap(&mz);
+      }
       for (int i = 0; i < nk; ++i) {
         const int s = i % kSkStages;
         if (i >= kSkStages && !mbar_wait(&empty[s], ((i / kSkStages) - 1) & 1, p.err, DK_DEVERR_WAIT_EMPTY)) {
@@ -528,10 +532,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         const int kt = kt0 + i;
-        mbar_arrive_expect_tx(&full[s], kSkWBytes + 2 * kSkSZ);
-        tma_load_2d(sW + s * kSkWBytes, &mq, n0, kt * (kBK / 8), &full[s]);
-        tma_load_2d(sS + s * kSkSZ, &ms, n0, (kt * kBK) / 128, &full[s]);
-        tma_load_2d(sZ + s * kSkSZ, &mz, n0, (kt * kBK) / 128, &full[s]);
+        if (kFp8) {
+          mbar_arrive_expect_tx(&full[s], kSkWSlot);
+          tma_load_2d(sW + s * kSkWSlot, &mq, n0, kt * kBK, &full[s]);  // e4m3 [64 K rows][128 N]
+        } else {
+          mbar_arrive_expect_tx(&full[s], kSkWBytes + 2 * kSkSZ);
+          tma_load_2d(sW + s * kSkWSlot, &mq, n0, kt * (kBK / 8), &full[s]);
+          tma_load_2d(sS + s * kSkSZ, &ms, n0, (kt * kBK) / 128, &full[s]);
+          tma_load_2d(sZ + s * kSkSZ, &mz, n0, (kt * kBK) / 128, &full[s]);
+        }
         issued = i + 1;
       }
     }
@@ -584,7 +593,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = false;
         break;
       }
-      const uint32_t* w = reinterpret_cast<const uint32_t*>(sW + s * kSkWBytes);
+      if constexpr (kFp8) {
+        // e4m3 -> fp16, transposing: lane c owns columns 4c..4c+3, warp w the K-block (w + c / 2) % 8
+        const int c = lane, kb = ((warp - 2) + (c >> 1)) & 7;
+        const uint32_t* raw = reinterpret_cast<const uint32_t*>(sW + s * kSkWSlot);  // row k: 32 words
+        uint32_t r[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) r[j] = raw[(kb * 8 + j) * (kSkBN / 4) + c];
+        uint32_t h[4][4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t lo, hi;
+          e4m3x4_to_f16(prmt(r[2 * j], r[2 * j + 1], 0x5140u), lo, hi);
+          h[0][j] = lo;
+          h[1][j] = hi;
+          e4m3x4_to_f16(prmt(r[2 * j], r[2 * j + 1], 0x7362u), lo, hi);
+          h[2][j] = lo;
+          h[3][j] = hi;
+        }
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          const int n = 4 * c + cc;
+          *reinterpret_cast<uint4*>(sA + s * kSkABytes + (n >> 3) * 1024 + (n & 7) * 128 + ((kb ^ (n & 7)) << 4)) =
+              make_uint4(h[cc][0], h[cc][1], h[cc][2], h[cc][3]);
+        }
+        tc::fence_proxy_async_smem();
+        mbar_arrive(&deq[s]);
+        continue;
+      }
+      const uint32_t* w = reinterpret_cast<const uint32_t*>(sW + s * kSkWSlot);
       const __half sc = reinterpret_cast<const __half*>(sS + s * kSkSZ)[col];
       const __half zc = reinterpret_cast<const __half*>(sZ + s * kSkSZ)[col];
       const uint32_t add2 = half2_bits(__hneg(__hadd(__float2half_rn(1024.f), zc)), __hneg(__hadd(__float2half_rn(64.f), zc)));
@@ -641,6 +678,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int j = 0; j < kHalf; ++j) {
         const int m = hrow * kHalf + j;
+        if (kFp8 && n < p.N) v[j] *= __half2float(p.scale[n]);
         if (S == 1) {
           if (m < p.M && n < p.N) {
             float a = v[j];
@@ -681,7 +719,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int MB>
+template <int MB, bool kFp8>
 bool skinny_smem_ready(int bytes) {
   static std::mutex mu;
   static int limit[64] = {};
@@ -690,7 +728,7 @@ bool skinny_smem_ready(int bytes) {
   if (dev < 0 || dev >= 64) return false;
   std::lock_guard<std::mutex> lock(mu);
   if (limit[dev] == 0) {
-    limit[dev] = opt_in_dynamic_smem(w4a16_skinny_tc_kernel<MB>);
+    limit[dev] = opt_in_dynamic_smem(w4a16_skinny_tc_kernel<MB, kFp8>);
     if (limit[dev] == 0) limit[dev] = -1;
   }
   return limit[dev] >= bytes;
@@ -703,7 +741,7 @@ bool skinny_smem_ready(int bytes) {
 void skinny_choice(int64_t rows, int64_t N, int64_t K, int* mb_out, int* split_out) {
   *mb_out = 0;
   *split_out = 0;
-  if (rows < 1 || N < kSkBN || K % 128 != 0) return;
+  if (rows < 1 || N < kSkBN || K % kBK != 0 || K <= 0) return;
   const int ktiles = static_cast<int>(K / kBK);
   const int tiles_n = static_cast<int>((N + kSkBN - 1) / kSkBN);
   const int sms = device_info().num_sms;
@@ -725,24 +763,19 @@ void skinny_choice(int64_t rows, int64_t N, int64_t K, int* mb_out, int* split_o
   }
 }
 
-int launch_skinny_tc(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const void* zeros,
-                     const void* bias, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, bool static_weights,
-                     cudaStream_t st) {
-  CUtensorMap mq, ms, mz;
-  if (!make_tensor_map_2d(&mq, qweight, CU_TENSOR_MAP_DATA_TYPE_INT32, N, K / 8, N * 4, kSkBN, kBK / 8,
-                          CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !make_tensor_map_2d(&ms, scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, N, K / 128, N * 2, kSkBN, 1,
-                          CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !make_tensor_map_2d(&mz, zeros, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, N, K / 128, N * 2, kSkBN, 1,
-                          CU_TENSOR_MAP_SWIZZLE_NONE))
-    return DK_ERR_CUDA;
+namespace {
+template <bool kFp8>
+int launch_skinny_core(const CUtensorMap& mq, const CUtensorMap& ms, const CUtensorMap& mz, const void* x, int64_t ldx,
+                       const void* scale, const void* bias, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
+                       bool static_weights, cudaStream_t st) {
   for (int64_t m0 = 0; m0 < M;) {
     int mb = 0, S = 0;
     skinny_choice(M - m0, N, K, &mb, &S);
-    if (mb == 0) return set_error(DK_ERR_UNSUPPORTED, "w4a16 small-M gemm: no tile fits (N=%lld, K=%lld)",
+    if (mb == 0) return set_error(DK_ERR_UNSUPPORTED, "small-M tcgen05 gemm: no tile fits (N=%lld, K=%lld)",
                                   (long long)N, (long long)K);
     const int rows = static_cast<int>(std::min<int64_t>(mb, M - m0));
     SkinnyParams p;
+    p.scale = static_cast<const __half*>(scale);
     p.x = static_cast<const __half*>(x) + m0 * ldx;
     p.ldx = ldx;
     p.y = static_cast<__half*>(y) + m0 * ldy;
@@ -757,29 +790,53 @@ int launch_skinny_tc(const void* x, int64_t ldx, const int32_t* qweight, const v
     p.err = device_info().err_word;
     const int smem = skinny_smem_bytes(mb, p.ks);
     const dim3 grid(static_cast<unsigned>((N + kSkBN - 1) / kSkBN), static_cast<unsigned>(S), 1);
-    cudaError_t e;
+    cudaError_t e = cudaSuccess;
     bool ready;
     if (mb == 16) {
-      ready = skinny_smem_ready<16>(smem);
-      e = ready ? launch(w4a16_skinny_tc_kernel<16>, grid, dim3(kThreads), smem, st, pdl_enabled(), dim3(1, S, 1),
-                         mq, ms, mz, p)
-                : cudaSuccess;
+      ready = skinny_smem_ready<16, kFp8>(smem);
+      if (ready)
+        e = launch(w4a16_skinny_tc_kernel<16, kFp8>, grid, dim3(kThreads), smem, st, pdl_enabled(), dim3(1, S, 1), mq,
+                   ms, mz, p);
     } else if (mb == 32) {
-      ready = skinny_smem_ready<32>(smem);
-      e = ready ? launch(w4a16_skinny_tc_kernel<32>, grid, dim3(kThreads), smem, st, pdl_enabled(), dim3(1, S, 1),
-                         mq, ms, mz, p)
-                : cudaSuccess;
+      ready = skinny_smem_ready<32, kFp8>(smem);
+      if (ready)
+        e = launch(w4a16_skinny_tc_kernel<32, kFp8>, grid, dim3(kThreads), smem, st, pdl_enabled(), dim3(1, S, 1), mq,
+                   ms, mz, p);
     } else {
-      ready = skinny_smem_ready<64>(smem);
-      e = ready ? launch(w4a16_skinny_tc_kernel<64>, grid, dim3(kThreads), smem, st, pdl_enabled(), dim3(1, S, 1),
-                         mq, ms, mz, p)
-                : cudaSuccess;
+      ready = skinny_smem_ready<64, kFp8>(smem);
+      if (ready)
+        e = launch(w4a16_skinny_tc_kernel<64, kFp8>, grid, dim3(kThreads), smem, st, pdl_enabled(), dim3(1, S, 1), mq,
+                   ms, mz, p);
     }
-    if (!ready) return set_error(DK_ERR_UNSUPPORTED, "w4a16 small-M gemm: %d bytes of shared memory do not fit", smem);
-    if (e != cudaSuccess) return set_error(DK_ERR_CUDA, "w4a16 small-M gemm launch: %s", cudaGetErrorString(e));
+    if (!ready) return set_error(DK_ERR_UNSUPPORTED, "small-M tcgen05 gemm: %d bytes of shared memory do not fit", smem);
+    if (e != cudaSuccess) return set_error(DK_ERR_CUDA, "small-M tcgen05 gemm launch: %s", cudaGetErrorString(e));
     m0 += rows;
   }
   return DK_OK;
+}
+}  // namespace
+
+int launch_skinny_tc(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const void* zeros,
+                     const void* bias, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, bool static_weights,
+                     cudaStream_t st) {
+  CUtensorMap mq, ms, mz;
+  if (!make_tensor_map_2d(&mq, qweight, CU_TENSOR_MAP_DATA_TYPE_INT32, N, K / 8, N * 4, kSkBN, kBK / 8,
+                          CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !make_tensor_map_2d(&ms, scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, N, K / 128, N * 2, kSkBN, 1,
+                          CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !make_tensor_map_2d(&mz, zeros, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, N, K / 128, N * 2, kSkBN, 1,
+                          CU_TENSOR_MAP_SWIZZLE_NONE))
+    return DK_ERR_CUDA;
+  return launch_skinny_core<false>(mq, ms, mz, x, ldx, nullptr, bias, y, ldy, M, N, K, static_weights, st);
+}
+
+// The e4m3 weight-only form (kernels/fp8.py:200-223 at 16..127 rows): wq [K, N] bytes, scale fp16 [N].
+int launch_skinny_tc_fp8(const void* x, int64_t ldx, const uint8_t* wq, const void* scale, const void* bias, void* y,
+                         int64_t ldy, int64_t M, int64_t N, int64_t K, bool static_weights, cudaStream_t st) {
+  CUtensorMap mw;
+  if (!make_tensor_map_2d(&mw, wq, CU_TENSOR_MAP_DATA_TYPE_UINT8, N, K, N, kSkBN, kBK, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return DK_ERR_CUDA;
+  return launch_skinny_core<true>(mw, mw, mw, x, ldx, scale, bias, y, ldy, M, N, K, static_weights, st);
 }
 
 }  // namespace dk

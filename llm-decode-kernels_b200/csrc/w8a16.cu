@@ -401,6 +401,9 @@ namespace dk {
 bool gemm_tc_fp8_ok(const void* x, int64_t ldx, const void* wq, int64_t M, int64_t N, int64_t K);
 int launch_gemm_tc_fp8(const void* x, int64_t ldx, const uint8_t* wq, const void* scale, const void* bias, void* y,
                        int64_t ldy, int64_t M, int64_t N, int64_t K, cudaStream_t st);
+void skinny_choice(int64_t rows, int64_t N, int64_t K, int* mb_out, int* split_out);
+int launch_skinny_tc_fp8(const void* x, int64_t ldx, const uint8_t* wq, const void* scale, const void* bias, void* y,
+                         int64_t ldy, int64_t M, int64_t N, int64_t K, bool static_weights, cudaStream_t st);
 }  // namespace dk
 
 extern "C" int dk_w8a16_matmul(const void* x, int64_t ldx, const uint8_t* wq, const void* scale, const void* bias,
@@ -426,6 +429,14 @@ extern "C" int dk_w8a16_matmul(const void* x, int64_t ldx, const uint8_t* wq, co
   }
   if (!(flags & DK_FLAG_GEMV) && gemm_tc_fp8_ok(x, ldx, wq, M, N, K))
     return launch_gemm_tc_fp8(x, ldx, wq, scale, bias, y, ldy, M, N, K, st);
+  // batched decode (16..127 rows) on the tcgen05 small-M kernel, the same rule as the int4 path
+  if (!(flags & DK_FLAG_GEMV) && M >= 16 && N >= 128 && N % 16 == 0 && K % 64 == 0 && aligned16(x) &&
+      ldx % 8 == 0 && (M > 16 || K >= 4096)) {
+    int mb = 0, split = 0;
+    skinny_choice(M, N, K, &mb, &split);
+    if (mb != 0)
+      return launch_skinny_tc_fp8(x, ldx, wq, scale, bias, y, ldy, M, N, K, (flags & DK_FLAG_STATIC_WEIGHTS) != 0, st);
+  }
   CUtensorMap mw;
   if (!make_tensor_map_2d(&mw, wq, CU_TENSOR_MAP_DATA_TYPE_UINT8, N, K, N, 32, kRows, CU_TENSOR_MAP_SWIZZLE_NONE))
     return DK_ERR_CUDA;

@@ -170,6 +170,33 @@ def attention(pos="767", splits="0"):
     print(f"attention: {e0.elapsed_time(e1) * 1e3 / (20 * layers):.2f} us/launch (position {pos}, splits {splits})")
 
 
+def small_m():
+    """us per launch of W4A16 at M = 16 and 32 on the Qwen2.5-1.5B shapes: the tcgen05 small-M kernel
+    (default) against 16-row launches of the decode GEMV (DECODE_GEMV), CUDA graph of 20 launches."""
+    from kernels.bench.harness import capture
+
+    for label, N, K in config.QWEN15_SHAPES[:4]:
+        qw, s, z = _q(N, K)
+        for M in (16, 32):
+            x = torch.randn(M, K, device="cuda").half()
+            res = []
+            for cfg in ({"STATIC_WEIGHTS": True}, {"STATIC_WEIGHTS": True, "DECODE_GEMV": True}):
+                w4a16_matmul(x, qw, s, z, config=cfg)
+                torch.cuda.synchronize()
+                graph, _ = capture(lambda: [w4a16_matmul(x, qw, s, z, config=cfg) for _ in range(20)])
+                graph.replay()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+                e0.record()
+                for _ in range(5):
+                    graph.replay()
+                e1.record()
+                torch.cuda.synchronize()
+                res.append(e0.elapsed_time(e1) / 100 * 1e3)
+                del graph
+            print(f"{label} {N}x{K} M={M}: tcgen05 small-M {res[0]:.2f} us, decode GEMV {res[1]:.2f} us")
+
+
 def attention_sweep():
     """Decode attention us/launch over positions x cluster splits (one process)."""
     for pos in ("511", "1023", "2047"):
@@ -177,7 +204,7 @@ def attention_sweep():
             attention(pos, splits)
 
 
-CASES = {"decode": decode, "gemv_layer": gemv_layer, "gemv": gemv, "attention": attention, "gemm": gemm, "chain": chain, "attention_sweep": attention_sweep}
+CASES = {"decode": decode, "gemv_layer": gemv_layer, "gemv": gemv, "attention": attention, "gemm": gemm, "chain": chain, "attention_sweep": attention_sweep, "small_m": small_m}
 
 if __name__ == "__main__":
     if len(sys.argv) < 2 or sys.argv[1] not in CASES:

@@ -16,9 +16,10 @@ kernel may prefetch them before the previous kernel finishes), `GENERIC` (force 
 any-alignment kernel, which always rounds like the reference) and `DECODE_GEMV` (run large M as
 16-row launches of the decode kernel instead of the tensor-core GEMM).
 
-Inputs of 128 rows or more (prefill) run the tcgen05 tensor-core GEMM, which dequantizes with the
-reference's fp16 rounding; the fused SwiGLU and RMSNorm variants then run as the GEMM plus the
-separate norm / activation kernels.
+Inputs of 128 rows or more (prefill) run the tcgen05 tensor-core GEMM and 16..127 rows (batched
+decode) the tcgen05 small-M kernel; both dequantize with the reference's fp16 rounding. Above 16
+rows the fused SwiGLU and RMSNorm variants run as that GEMM plus the separate norm / activation
+kernels.
 """
 
 from __future__ import annotations
@@ -31,6 +32,9 @@ from kernels import _lib
 
 _choices: dict[tuple, dict] = {}  # (m_key, N, K, bias) -> config used (export/import_choices)
 TC_MIN_ROWS = 128  # rows from which dk_w4a16_matmul runs the tensor-core GEMM
+# rows above which the fused norm / SwiGLU entry points run as separate kernels around the tcgen05
+# small-M GEMM (16 < M < 128) or the prefill GEMM instead of looping the fused decode GEMV per 16 rows
+SPLIT_FUSED_ROWS = 16
 
 
 def _config(config: dict | None) -> _lib.MatmulConfig:
@@ -103,7 +107,7 @@ def w4a16_swiglu(x, qweight, scales, zeros, group_size=128, bias=None, config=No
         x2 = x2.contiguous()
     aligned = all(t.data_ptr() % 16 == 0 for t in (x2, qweight, scales, zeros)) and x2.stride(0) % 8 == 0
     cfg = _config(config)
-    big = x2.shape[0] >= TC_MIN_ROWS and not cfg.flags & _lib.FLAG_GEMV
+    big = x2.shape[0] > SPLIT_FUSED_ROWS and not cfg.flags & _lib.FLAG_GEMV
     if I % 32 != 0 or group_size != 128 or not aligned or cfg.flags & _lib.FLAG_GENERIC or big:
         from kernels.swiglu import swiglu_fused
 
@@ -142,7 +146,7 @@ def w4a16_rmsnorm_matmul(x, norm_weight, eps, residual, qweight, scales, zeros, 
     cfg = _config(config)
     I = N // 2
     tensors = [x2, qweight, scales, zeros, norm_weight] + ([r2] if r2 is not None else [])
-    big = M >= TC_MIN_ROWS and not cfg.flags & _lib.FLAG_GEMV
+    big = M > SPLIT_FUSED_ROWS and not cfg.flags & _lib.FLAG_GEMV
     fast = (group_size == 128 and N % 8 == 0 and (not swiglu or I % 32 == 0) and not cfg.flags & _lib.FLAG_GENERIC
             and not big
             and all(t.data_ptr() % 16 == 0 for t in tensors) and x2.stride(0) % 8 == 0

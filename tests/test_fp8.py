@@ -124,3 +124,18 @@ def test_w8a16_tensor_core_gemm(M, N, K, bias):
     assert torch.equal(out, w8a16_matmul(xc, wc, sc, bias=bc))
     gemv = w8a16_matmul(xc, wc, sc, bias=bc, config={"DECODE_GEMV": True})
     torch.testing.assert_close(out.float(), gemv.float(), **MATMUL_TOL)
+
+
+@pytest.mark.parametrize("M", [16, 17, 32, 48, 100])
+@pytest.mark.parametrize("N,K", [(2048, 1536), (1536, 8960), (256, 4096)])
+def test_w8a16_small_m_tensor_core(M, N, K):
+    """16..127 rows run the tcgen05 small-M kernel (e4m3 tile converted to fp16 in shared memory, batch
+    rows as the MMA's N, cluster split-K): oracle tolerance, deterministic, close to the decode kernel."""
+    from kernels.fp8 import FP8, w8a16_matmul
+
+    x, _, wq, s, b = _case(M, N, K, seed=M + N, bias=True)
+    xc, sc, bc = to_cuda(x, s, b)
+    wc = torch.from_numpy(wq).cuda().view(FP8)
+    out = w8a16_matmul(xc, wc, sc, bias=bc)
+    np.testing.assert_allclose(out.float().cpu().numpy(), ref.w8a16_ref(x, wq, s, b), **MATMUL_TOL)
+    assert torch.equal(out, w8a16_matmul(xc, wc, sc, bias=bc))

@@ -96,3 +96,65 @@ def test_prefill_swiglu_and_norm_paths():
     h, res2 = rmsnorm(xc, nw, 1e-6, residual=r)
     assert torch.equal(res, res2)
     assert torch.equal(y, swiglu_fused(w4a16_matmul(h, qc, sc, zc)))
+
+
+# ----------------------------------------------------------- small-M (batched decode) tensor-core path
+@pytest.mark.parametrize("M", [16, 17, 24, 32, 40, 64, 65, 100, 127])
+@pytest.mark.parametrize("N,K", [(2048, 1536), (1536, 8960), (3584, 2432), (256, 4096)])
+def test_small_m_tcgen05_matches_oracle(M, N, K):
+    """16 <= M < 128 rows run the swap-AB tcgen05 kernel (batch rows as the MMA's N, cluster split-K):
+    the oracle's tolerance, deterministic."""
+    from kernels.w4a16 import w4a16_matmul
+
+    x, qw, s, z, b = w4_case(M, N, K, seed=M * 3 + N, bias=True)
+    xc, qc, sc, zc, bc = to_cuda(x, qw, s, z, b)
+    out = w4a16_matmul(xc, qc, sc, zc, 128, bias=bc, config={"STATIC_WEIGHTS": True})
+    assert_matmul_close(out, w4_ref(x, qw, s, z, b))
+    assert torch.equal(out, w4a16_matmul(xc, qc, sc, zc, 128, bias=bc))
+    from kernels import _lib
+
+    assert _lib.device_error() == 0
+
+
+def test_small_m_gate_up_and_graph():
+    """A gate_up-sized layer (one CTA per 128 columns, no split) at batch 32, inside a CUDA graph."""
+    from kernels.bench.harness import capture
+    from kernels.w4a16 import w4a16_matmul
+
+    x, qw, s, z, _ = w4_case(32, 17920, 1536, seed=12)
+    xc, qc, sc, zc = to_cuda(x, qw, s, z)
+    ref = w4a16_matmul(xc, qc, sc, zc)
+    assert_matmul_close(ref, w4_ref(x, qw, s, z, None))
+    res = {}
+
+    def step():
+        res["y"] = w4a16_matmul(xc, qc, sc, zc)
+
+    step()
+    torch.cuda.synchronize()
+    graph, _ = capture(step)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(res["y"], ref)
+    del graph
+
+
+@pytest.mark.parametrize("M", [17, 32, 64])
+def test_small_m_fused_entry_points_split(M):
+    """Above 16 rows the fused SwiGLU / RMSNorm entry points run the small-M GEMM plus the separate
+    kernels: identical to calling those ops one by one."""
+    from kernels.rmsnorm import rmsnorm
+    from kernels.swiglu import swiglu_fused
+    from kernels.w4a16 import w4a16_matmul, w4a16_rmsnorm_matmul, w4a16_swiglu
+
+    I, K = 8960, 1536
+    x, qw, s, z, _ = w4_case(M, 2 * I, K, seed=M)
+    xc, qc, sc, zc = to_cuda(x, qw, s, z)
+    assert torch.equal(w4a16_swiglu(xc, qc, sc, zc), swiglu_fused(w4a16_matmul(xc, qc, sc, zc)))
+    r = torch.randn(M, K, device="cuda").half()
+    nw = (1 + 0.05 * torch.randn(K, device="cuda")).half()
+    y, res = w4a16_rmsnorm_matmul(xc, nw, 1e-6, r, qc, sc, zc, swiglu=True)
+    h, res2 = rmsnorm(xc, nw, 1e-6, residual=r)
+    assert torch.equal(res, res2)
+    assert torch.equal(y, swiglu_fused(w4a16_matmul(h, qc, sc, zc)))
