@@ -229,8 +229,10 @@ class TensorParallel:
         if self.mode == "fused" and self.comm is None:
             self.comm = TPComm(max_n=hidden, max_m=16, group=self.group, device=device)
 
-    # rows up to which the fused kernel is used (decode batches); prefill-sized inputs use NCCL
-    FUSED_MAX_ROWS = 32
+    # rows up to which the fused GEMV + allreduce kernel is used: it runs 16 rows per launch, so above
+    # that the tcgen05 small-M kernel (one pass over the weights) plus NCCL is faster (7B TP=2 at batch
+    # 32: 4760 vs 4539 tok/s); prefill-sized inputs use the GEMM plus NCCL
+    FUSED_MAX_ROWS = 16
 
     def reduce_linear(self, be, x, p):
         """sum over ranks of the row-sharded projection p of x (+ p.bias once)."""
