@@ -3,8 +3,9 @@
  *
  * Every entry point takes plain device pointers, sizes in elements, row strides in elements and
  * a CUDA stream, and returns an int status (DK_OK = 0, negative on error, with the message in
- * dk_last_error()). Nothing allocates device memory, synchronizes or reads device memory from
- * the host, so every call can be captured in a CUDA graph. Kernels are queued on `stream` and
+ * dk_last_error()). Apart from the tensor-parallel set-up calls (dk_tp_buffer_*, which allocate and
+ * synchronize once, before any capture), nothing allocates device memory, synchronizes or reads
+ * device memory from the host, so every launch can be captured in a CUDA graph. Kernels are queued on `stream` and
  * report launch errors through the status; asynchronous device-side conditions (a bounded wait
  * that gave up) are recorded in a per-device error word read with dk_device_error().
  *
@@ -172,7 +173,8 @@ int dk_swiglu(const void* gate, int64_t ldg, const void* up, int64_t ldu, void* 
  * fused projection output; caches [B, nkv, max_len, head_dim]; cos, sin [head_dim] for this
  * position; out [B, nq * head_dim]. `pos` is a device pointer (graph-capturable); a position outside
  * [0, max_len) writes nothing and sets DK_DEVERR_BAD_POSITION. splits: positions are cut into this
- * many slices combined inside a thread-block cluster (0 = automatic, max 16). head_dim 32, 64 or 128. */
+ * many slices combined inside a thread-block cluster (0 = automatic: max_len / 128, at most 16, and no
+ * more than one wave of CTAs over B * nkv clusters; max 16). head_dim 32, 64 or 128. */
 #define DK_ATTN_STATIC_CACHE 1 /* flags: the cache rows before *pos and *pos itself were not written
                                   by the kernel immediately before this one (true inside a decode
                                   step): the cache slice is fetched before waiting for that kernel */

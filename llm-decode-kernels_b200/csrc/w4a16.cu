@@ -447,6 +447,12 @@ __device__ __forceinline__ void stage_x(const GemvParams& p, uint8_t* xs, float*
   __shared__ float inv[16];
   __shared__ float part[16][kWarps];
   const bool norm = p.norm_w != nullptr;
+  // One row (M == 1, K <= 4096) and a slice that starts on a multiple of 256 blocks: the thread that
+  // holds block kb0 + b in the sum-of-squares pass (v = tid + j * 256) is the one that stages block b,
+  // so it keeps x + residual in registers instead of reading them from L2 a second time. The pass
+  // order is unchanged, so every CTA of the launch computes the same 1/rms.
+  const bool keep = norm && p.M == 1 && p.K / 8 <= 2 * kThr && kb0 % kThr == 0;
+  uint4 keep0 = make_uint4(0, 0, 0, 0), keep1 = make_uint4(0, 0, 0, 0);
   if (norm) {
     const int nv = p.K / 8;
     for (int m = 0; m < p.M; ++m) {
@@ -460,6 +466,12 @@ __device__ __forceinline__ void stage_x(const GemvParams& p, uint8_t* xs, float*
 #pragma unroll
           for (int j = 0; j < 4; ++j) ah[j] = __hadd2_rn(ah[j], rh[j]);
           if (writer) reinterpret_cast<uint4*>(p.res_out + m * p.ldro)[v] = a;
+        }
+        if (keep) {
+          if (v < kThr)
+            keep0 = a;
+          else
+            keep1 = a;
         }
         const __half2* ah = reinterpret_cast<const __half2*>(&a);
 #pragma unroll
@@ -491,10 +503,13 @@ __device__ __forceinline__ void stage_x(const GemvParams& p, uint8_t* xs, float*
     const int k = (kb0 + b) * 8;
     uint4 v = make_uint4(0, 0, 0, 0);
     if (k < p.K) {
-      v = __ldcg(reinterpret_cast<const uint4*>(p.x + m * p.ldx + k));
+      if (keep)  // this thread read block kb0 + b (= tid + j * 256) in the pass above
+        v = (kb0 + b) < kThr ? keep0 : keep1;
+      else
+        v = __ldcg(reinterpret_cast<const uint4*>(p.x + m * p.ldx + k));
       if (norm) {
         __half2* vh = reinterpret_cast<__half2*>(&v);
-        if (p.res != nullptr) {
+        if (p.res != nullptr && !keep) {
           const uint4 r = __ldcg(reinterpret_cast<const uint4*>(p.res + m * p.ldr + k));
           const __half2* rh = reinterpret_cast<const __half2*>(&r);
 #pragma unroll
