@@ -139,3 +139,13 @@ def test_w8a16_small_m_tensor_core(M, N, K):
     out = w8a16_matmul(xc, wc, sc, bias=bc)
     np.testing.assert_allclose(out.float().cpu().numpy(), ref.w8a16_ref(x, wq, s, b), **MATMUL_TOL)
     assert torch.equal(out, w8a16_matmul(xc, wc, sc, bias=bc))
+
+
+@pytest.mark.parametrize("M,N,K", [(20, 208, 192), (64, 1008, 64)])
+def test_w8a16_small_m_edges(M, N, K):
+    from kernels.fp8 import FP8, w8a16_matmul
+
+    x, _, wq, s, b = _case(M, N, K, seed=7, bias=True)
+    xc, sc, bc = to_cuda(x, s, b)
+    out = w8a16_matmul(xc, torch.from_numpy(wq).cuda().view(FP8), sc, bias=bc)
+    np.testing.assert_allclose(out.float().cpu().numpy(), ref.w8a16_ref(x, wq, s, b), **MATMUL_TOL)

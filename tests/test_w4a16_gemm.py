@@ -158,3 +158,14 @@ def test_small_m_fused_entry_points_split(M):
     h, res2 = rmsnorm(xc, nw, 1e-6, residual=r)
     assert torch.equal(res, res2)
     assert torch.equal(y, swiglu_fused(w4a16_matmul(h, qc, sc, zc)))
+
+
+@pytest.mark.parametrize("M,N,K", [(20, 200, 256), (64, 1000, 128), (33, 136, 2048), (16, 4104, 4096)])
+def test_small_m_edges(M, N, K):
+    """Small-M tcgen05 kernel at a partial last 128-column tile, the smallest K (one 128-group), and
+    exactly 64 rows."""
+    from kernels.w4a16 import w4a16_matmul
+
+    x, qw, s, z, b = w4_case(M, N, K, seed=N + K, bias=True)
+    xc, qc, sc, zc, bc = to_cuda(x, qw, s, z, b)
+    assert_matmul_close(w4a16_matmul(xc, qc, sc, zc, 128, bias=bc), w4_ref(x, qw, s, z, b))
