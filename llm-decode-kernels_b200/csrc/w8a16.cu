@@ -42,6 +42,7 @@ struct W8Params {
   int64_t ldy;
   int M, N, K;
   int stages_total, split_stages, chunks, nbuf, xs_pitch, static_weights;
+  uint32_t nbuf_rcp;  // ceil(2^32 / nbuf): it / nbuf == __umulhi(it, nbuf_rcp) for it < 2^28
   int* err;
   L2Prefetch pf;  // ranges to pull into L2 for a later launch (a hint)
 };
@@ -99,7 +100,8 @@ __global__ void __launch_bounds__((kWarps8 + 1) * 32, 3 - NT)
     w8a16_gemv_kernel(const __grid_constant__ CUtensorMap mw, const W8Params p) {
   constexpr int WPC = kWarps8 / CW;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte aligned base by pointer arithmetic on the shared array (accesses stay shared-space)
+  uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   const int S = gridDim.y;
   const Layout8 L = layout8(CW, p.nbuf, p.M, p.xs_pitch, S);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
@@ -137,8 +139,9 @@ __global__ void __launch_bounds__((kWarps8 + 1) * 32, 3 - NT)
       for (int tile = c_begin; tile < c_end && ok; tile += CW) {
         const int nch = min(CW, c_end - tile);
         for (int s = s_begin; s < s_end; ++s, ++it) {
-          const int buf = it % p.nbuf;
-          if (it >= p.nbuf && !mbar_wait(&empty[buf], ((it / p.nbuf) - 1) & 1, p.err, DK_DEVERR_WAIT_EMPTY)) {
+          const int round = static_cast<int>(__umulhi(static_cast<uint32_t>(it), p.nbuf_rcp));
+          const int buf = it - round * p.nbuf;
+          if (it >= p.nbuf && !mbar_wait(&empty[buf], (round - 1) & 1, p.err, DK_DEVERR_WAIT_EMPTY)) {
             ok = false;
             break;
           }
@@ -186,8 +189,9 @@ __global__ void __launch_bounds__((kWarps8 + 1) * 32, 3 - NT)
           for (int c = 0; c < 4; ++c) acc[a][b][c] = 0.f;
       for (int ls = phase; ls < nst && ok; ls += WPC) {
         const int it = tile_idx * nst + ls;
-        const int buf = it % p.nbuf;
-        if (!mbar_wait(&full[buf], (it / p.nbuf) & 1, p.err, DK_DEVERR_WAIT_FULL)) {
+        const int round = static_cast<int>(__umulhi(static_cast<uint32_t>(it), p.nbuf_rcp));
+        const int buf = it - round * p.nbuf;
+        if (!mbar_wait(&full[buf], round & 1, p.err, DK_DEVERR_WAIT_FULL)) {
           ok = false;
           break;
         }
@@ -459,6 +463,7 @@ extern "C" int dk_w8a16_matmul(const void* x, int64_t ldx, const uint8_t* wq, co
     p.split_stages = (p.stages_total + c.split - 1) / c.split;
     p.chunks = static_cast<int>((N + 31) / 32);
     p.nbuf = c.nbuf;
+    p.nbuf_rcp = static_cast<uint32_t>((0x100000000ull + c.nbuf - 1) / c.nbuf);
     p.xs_pitch = xs_pitch8(p.split_stages);
     p.static_weights = (flags & DK_FLAG_STATIC_WEIGHTS) ? 1 : 0;
     p.err = dev.err_word;

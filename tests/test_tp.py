@@ -415,3 +415,44 @@ def test_tp_runner_world2_matches_unsharded():
             assert err < 5e-2, (rank, mode, err)
             assert same_argmax, (rank, mode)
             assert toks == out["plain_tokens"], (rank, mode)
+
+
+def _argmax_worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    from kernels.tp import TensorParallel
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        V = 24  # 12 vocabulary rows per rank
+        full = torch.tensor([
+            [0.0] * V,                                  # all equal: index 0
+            [1.0 if i in (5, 17) else 0.0 for i in range(V)],   # tie across ranks: 5
+            [2.0 if i in (14, 19) else 0.0 for i in range(V)],  # tie inside rank 1: 14
+            [float(i % 7) for i in range(V)],           # max 6 at 6 (rank 0), 13 and 20 (rank 1): 6
+        ], dtype=torch.float16)
+        lo = full[:, rank * 12:(rank + 1) * 12]
+        got = TensorParallel(mode="nccl").argmax(lo, rank * 12)
+        q.put((rank, got.tolist(), full.argmax(-1).tolist()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp_argmax_ties_match_full_row():
+    """The cross-rank greedy token equals torch.argmax over the whole row, ties included (lowest
+    vocabulary index wins, within a rank and across ranks)."""
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_argmax_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    for _ in range(2):
+        rank, got, want = q.get(timeout=5)
+        assert got == want == [0, 5, 14, 6], (rank, got, want)
