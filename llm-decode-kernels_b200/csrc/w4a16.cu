@@ -952,6 +952,12 @@ Choice choose_uncached(int M, int units, int K, bool swiglu, const dk_matmul_con
       }
       const size_t smem = static_cast<size_t>(L.total) + 1024;
       if (smem > static_cast<size_t>(dev.max_smem_optin)) continue;
+      // Ring depth: a consumer warp's next stage is kWarps / cw stages after its previous one (and
+      // its first stage of a tile at most that far after a stage the whole CTA has consumed), so
+      // once buffers are reused the ring must hold at least that many stages; a shallower ring
+      // would let a full-barrier parity wait pass on the buffer's previous phase. (Only very long
+      // K slices with narrow tiles reach this: x's staging then leaves little shared memory.)
+      if (nbuf < std::min(kWarps / cw, stages_per_cta)) continue;
       const int occ = occupancy(nt, cw, smem);
       const int nctas = split == 1 ? std::min(units, dev.num_sms * occ) : tiles;
       if (split > 1 && static_cast<long>(nctas) * split > static_cast<long>(dev.num_sms) * occ) continue;

@@ -345,7 +345,8 @@ Choice8 choose8_uncached(int M, int N, int K, const dk_matmul_config* cfg) {
       const int pitch = xs_pitch8(sps);
       if (static_cast<size_t>(M) * pitch > 64 * 1024) continue;
       const int tiles = (chunks + cw - 1) / cw;
-      int nbuf = std::min(std::max(sps * (split > 1 ? 1 : (tiles + dev.num_sms - 1) / dev.num_sms), 2), 16);
+      const int stages_per_cta = sps * (split > 1 ? 1 : (tiles + dev.num_sms - 1) / dev.num_sms);
+      int nbuf = std::min(std::max(stages_per_cta, 2), 16);
       Layout8 L = layout8(cw, nbuf, M, pitch, split);
       while (nbuf > 2 && static_cast<size_t>(L.total) + 1024 > 110 * 1024) {
         --nbuf;
@@ -353,6 +354,9 @@ Choice8 choose8_uncached(int M, int N, int K, const dk_matmul_config* cfg) {
       }
       const size_t smem = static_cast<size_t>(L.total) + 1024;
       if (smem > static_cast<size_t>(dev.max_smem_optin)) continue;
+      // ring depth >= warps per chunk once buffers are reused (the W4A16 GEMV's rule: a shallower
+      // ring would let a full-barrier parity wait pass on the buffer's previous phase)
+      if (nbuf < std::min(wpc, stages_per_cta)) continue;
       int occ = 0;
       if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, variant8(nt, cw), (kWarps8 + 1) * 32, smem) != cudaSuccess) {
         cudaGetLastError();

@@ -15,6 +15,9 @@
     python .../profile_cases.py attention [pos] [splits]
         28 decode-attention launches (one per layer, Qwen2.5-1.5B heads, position 767 by default,
         automatic split) eagerly, then as a CUDA graph replayed 21 times.
+    python .../profile_cases.py config_sweep [M]
+        the cost model's GEMV choice against every BLOCK_N x SPLIT_K of one decoder layer's four
+        launches, and the lm_head-shaped GEMV at three widths.
 
 Every case allocates at most a few hundred MB and ends by itself.
 """
@@ -204,7 +207,57 @@ def attention_sweep():
             attention(pos, splits)
 
 
-CASES = {"decode": decode, "gemv_layer": gemv_layer, "gemv": gemv, "attention": attention, "gemm": gemm, "chain": chain, "attention_sweep": attention_sweep, "small_m": small_m}
+def config_sweep(M="1"):
+    """The static cost model's choice against the BLOCK_N x SPLIT_K space: us per launch of the four
+    W4A16 launches of a Qwen2.5-1.5B decoder layer as the runner issues them (norm+qkv, o_proj,
+    norm+gate_up+SwiGLU, down) at M rows, for BLOCK_N in {auto, 32, 64, 128, 256} and the split-K
+    factors K allows; then the lm_head-shaped GEMV at three widths (the slope is its marginal
+    bandwidth). Timed like the reference's harness (CUDA graph, rotating weight copies >= 4x L2)."""
+    from kernels.bench.harness import time_rotating
+
+    M = int(M)
+    H, inter = config.QWEN15["hidden_size"], config.QWEN15["intermediate_size"]
+    x = torch.randn(M, H, device="cuda").half()
+    res = torch.randn(M, H, device="cuda").half()
+    nw = (1 + 0.05 * torch.randn(H, device="cuda")).half()
+    xd = torch.randn(M, inter, device="cuda").half()
+
+    def op(kind, cfg):
+        if kind == "norm":
+            return lambda xx, q, s, z: w4a16_rmsnorm_matmul(xx, nw, 1e-6, res, q, s, z, config=cfg)
+        if kind == "norm_swiglu":
+            return lambda xx, q, s, z: w4a16_rmsnorm_matmul(xx, nw, 1e-6, res, q, s, z, swiglu=True, config=cfg)
+        return lambda xx, q, s, z: w4a16_matmul(xx, q, s, z, config=cfg)
+
+    layer = [("norm+qkv", "norm", 2048, H, x), ("o_proj", "plain", H, H, x),
+             ("norm+gate_up+swiglu", "norm_swiglu", 2 * inter, H, x), ("down", "plain", H, inter, xd)]
+    for label, kind, N, K, xin in layer:
+        qw, s, z = _q(N, K)
+        stages = (K + 255) // 256
+        # the split-K factors the kernel accepts as given (every cluster rank gets a stage)
+        splits = [0] + [sp for sp in range(1, 9) if sp <= stages and (sp - 1) * -(-stages // sp) < stages]
+        rows = []
+        for bn in (0, 32, 64, 128, 256):
+            for sp in splits:
+                cfg = {"STATIC_WEIGHTS": True, "BLOCK_N": bn, "SPLIT_K": sp}
+                us = time_rotating(op(kind, cfg), (xin, qw, s, z), rotate=(1, 2, 3)) * 1e3
+                rows.append((us, bn, sp))
+                print(f"M={M} {label} BLOCK_N={bn or 'auto'} SPLIT_K={sp or 'auto'}: {us:.2f} us", flush=True)
+        auto = rows[0][0]
+        best = min(rows)
+        print(f"M={M} {label}: auto {auto:.2f} us, best {best[0]:.2f} us (BLOCK_N={best[1] or 'auto'}, "
+              f"SPLIT_K={best[2] or 'auto'})", flush=True)
+        del qw, s, z
+        torch.cuda.empty_cache()
+    for N in (37984, 75968, 151936):
+        qw, s, z = _q(N, H)
+        us = time_rotating(op("plain", {"STATIC_WEIGHTS": True}), (x[:1], qw, s, z), rotate=(1, 2, 3)) * 1e3
+        print(f"lm_head-shaped GEMV N={N} K={H} M=1: {us:.2f} us", flush=True)
+        del qw, s, z
+        torch.cuda.empty_cache()
+
+
+CASES = {"decode": decode, "gemv_layer": gemv_layer, "gemv": gemv, "attention": attention, "gemm": gemm, "chain": chain, "attention_sweep": attention_sweep, "small_m": small_m, "config_sweep": config_sweep}
 
 if __name__ == "__main__":
     if len(sys.argv) < 2 or sys.argv[1] not in CASES:

@@ -152,6 +152,14 @@ def test_strided_x_and_static_flag():
     assert_matmul_close(out, w4_ref(x, qw, s, z, b))
 
 
+@pytest.mark.parametrize("config", [None, {"BLOCK_N": 32, "SPLIT_K": 1}, {"BLOCK_N": 64, "SPLIT_K": 1}])
+def test_long_k_slice(config):
+    """K = 32512 in one slice: staging x leaves shared memory for a two-stage ring only, fewer stages
+    than the warps that share a 32- or 64-column chunk, so those forced tiles are refused and the
+    automatic choice (a ring at least as deep) runs instead."""
+    _check(1, 1536, 32512, config=config)
+
+
 def test_deterministic():
     from kernels.w4a16 import w4a16_matmul
 
