@@ -107,9 +107,10 @@ def plan_for(cfg, world: int, rank: int) -> ShardPlan:
 class TPComm:
     """The NVLink exchange buffers of one tensor-parallel group (set-up: allocates, maps, syncs).
 
-    Every rank allocates one buffer (partial sums of launches up to `max_m` rows x `max_n` columns,
-    plus per-CTA flags), exports its CUDA IPC handle, gathers the others' over `group` and maps
-    them. With group None and no process group initialized, a single-rank communicator (world 1):
+    Every rank allocates one buffer (two slots of epoch-tagged partial sums of launches up to `max_m`
+    rows x `max_n` columns per rank, behind a header holding the launch epoch and an arrival count),
+    exports its CUDA IPC handle, gathers the others' over `group` and maps them. If set-up fails on
+    this rank, what it allocated or mapped is released before the error propagates. With group None and no process group initialized, a single-rank communicator (world 1):
     the fused kernel then pushes to and waits on its own buffer only."""
 
     def __init__(self, max_n: int, max_m: int = 16, group=None, device=None):
@@ -121,7 +122,19 @@ class TPComm:
         self.world = dist.get_world_size(group) if self.dist else 1
         self.max_m, self.max_n = int(max_m), int(max_n)
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.handle = None
+        self._own = None
+        self._opened = []
         lib = _lib.lib()
+        try:
+            self._setup(lib, dist, group)
+        except BaseException:
+            self._release(lib)  # this rank's mappings and buffer; the peers fail at their next collective
+            raise
+        if self.world > 1:
+            dist.barrier(group=group)
+
+    def _setup(self, lib, dist, group) -> None:
         nbytes = ctypes.c_uint64(0)
         _lib.check(lib.dk_tp_buffer_bytes(self.world, self.max_m, self.max_n, ctypes.byref(nbytes)), "tp_buffer_bytes")
         handle = ctypes.create_string_buffer(64)
@@ -129,7 +142,6 @@ class TPComm:
         with torch.cuda.device(self.device):
             _lib.check(lib.dk_tp_buffer_alloc(nbytes.value, ctypes.byref(own), handle), "tp_buffer_alloc")
         self._own = own
-        self._opened = []
         handles = [bytes(handle.raw)]
         if self.world > 1:
             handles = [None] * self.world
@@ -149,8 +161,19 @@ class TPComm:
         _lib.check(lib.dk_tp_comm_create(ctypes.byref(comm), self.rank, self.world, ptrs, self.max_m, self.max_n),
                    "tp_comm_create")
         self.handle = comm
-        if self.world > 1:
-            dist.barrier(group=group)
+
+    def _release(self, lib) -> None:
+        if self.handle is not None:
+            lib.dk_tp_comm_destroy(self.handle)
+            self.handle = None
+        if self._opened or self._own is not None:
+            with torch.cuda.device(self.device):
+                for p in self._opened:
+                    lib.dk_tp_buffer_close(p)
+                if self._own is not None:
+                    lib.dk_tp_buffer_free(self._own)
+        self._opened = []
+        self._own = None
 
     def close(self) -> None:
         """Unmap the peers' buffers and free this rank's (after a barrier: no peer may still write)."""
@@ -159,14 +182,7 @@ class TPComm:
         torch.cuda.synchronize(self.device)
         if self.world > 1:
             self.dist_barrier()
-        lib = _lib.lib()
-        lib.dk_tp_comm_destroy(self.handle)
-        self.handle = None
-        with torch.cuda.device(self.device):
-            for p in self._opened:
-                lib.dk_tp_buffer_close(p)
-            lib.dk_tp_buffer_free(self._own)
-        self._opened = []
+        self._release(_lib.lib())
 
     def dist_barrier(self) -> None:
         import torch.distributed as dist

@@ -456,3 +456,73 @@ def test_tp_argmax_ties_match_full_row():
     for _ in range(2):
         rank, got, want = q.get(timeout=5)
         assert got == want == [0, 5, 14, 6], (rank, got, want)
+
+
+# --------------------------------------------------------------- communicator set-up failure (CPU)
+class _FakeTpLib:
+    """Stands in for libdecodek's TP set-up entry points: allocation succeeds, mapping the peer
+    `fail_peer` fails; records what was allocated, mapped, closed and freed."""
+
+    def __init__(self, fail_peer):
+        self.fail_peer, self.log = fail_peer, []
+
+    def dk_tp_buffer_bytes(self, world, max_m, max_n, out):
+        out._obj.value = 256 + 2 * world * max_m * max_n * 8
+        return 0
+
+    def dk_tp_buffer_alloc(self, nbytes, out, handle):
+        out._obj.value = 0x1000
+        handle.raw = b"\x00" * 64
+        self.log.append("alloc")
+        return 0
+
+    def dk_tp_buffer_open(self, handle, out):
+        peer = handle.raw[0]
+        if peer == self.fail_peer:
+            return -3
+        out._obj.value = 0x2000 + peer
+        self.log.append(f"open{peer}")
+        return 0
+
+    def dk_tp_buffer_close(self, p):
+        self.log.append(f"close{p.value - 0x2000}")
+        return 0
+
+    def dk_tp_buffer_free(self, p):
+        self.log.append("free")
+        return 0
+
+    def dk_tp_comm_create(self, *a):
+        self.log.append("create")
+        return 0
+
+    def dk_last_error(self):
+        return b"cannot map the peer's buffer"
+
+
+def test_tpcomm_setup_failure_releases_buffers(monkeypatch):
+    """A rank whose mapping of a peer's exchange buffer fails closes the mappings made so far, frees
+    its own buffer and raises (a fake library and a fake 4-rank group on the CPU)."""
+    import contextlib
+
+    import torch.distributed as dist
+
+    from kernels import _lib
+    from kernels.tp import TPComm
+
+    fake = _FakeTpLib(fail_peer=3)
+    monkeypatch.setattr(_lib, "lib", lambda: fake)
+    monkeypatch.setattr(torch.cuda, "device", lambda d: contextlib.nullcontext())
+    monkeypatch.setattr(dist, "is_initialized", lambda: True)
+    monkeypatch.setattr(dist, "get_rank", lambda group=None: 0)
+    monkeypatch.setattr(dist, "get_world_size", lambda group=None: 4)
+
+    def gather(out, obj, group=None):  # rank q's handle starts with the byte q
+        for q in range(len(out)):
+            out[q] = bytes([q]) + obj[1:]
+
+    monkeypatch.setattr(dist, "all_gather_object", gather)
+    monkeypatch.setattr(dist, "barrier", lambda group=None: None)
+    with pytest.raises(RuntimeError, match="tp_buffer_open: cannot map"):
+        TPComm(max_n=64, device="cuda:0")
+    assert fake.log == ["alloc", "open1", "open2", "close1", "close2", "free"]
