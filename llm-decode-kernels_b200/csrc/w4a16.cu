@@ -1030,9 +1030,16 @@ int run_fast(const void* x, int64_t ldx, const int32_t* qweight, const void* sca
   const DeviceInfo& dev = device_info();
   const int units = swiglu_i > 0 ? (swiglu_i + 31) / 32 : static_cast<int>((N + 31) / 32);
   const int64_t rows_per_launch = tp != nullptr ? std::min<int64_t>(16, tp->max_m) : 16;
-  for (int64_t m0 = 0; m0 < M; m0 += rows_per_launch) {
-    const int mc = static_cast<int>(std::min<int64_t>(rows_per_launch, M - m0));
-    const Choice c = choose(mc, units, static_cast<int>(K), swiglu_i > 0, cfg);
+  for (int64_t m0 = 0; m0 < M;) {
+    int mc = static_cast<int>(std::min<int64_t>(rows_per_launch, M - m0));
+    Choice c = choose(mc, units, static_cast<int>(K), swiglu_i > 0, cfg);
+    // The staged x grows with the rows: when a long K slice leaves no tile for mc rows, launch fewer
+    // rows at a time. (Not with the fused allreduce: every rank must make the same launches, and
+    // the ranks' K shards may differ.)
+    while (tp == nullptr && c.cw == 0 && mc > 1) {
+      mc = (mc + 1) / 2;
+      c = choose(mc, units, static_cast<int>(K), swiglu_i > 0, cfg);
+    }
     if (c.cw == 0) return set_error(DK_ERR_UNSUPPORTED, "w4a16: no tile fits (M=%d, K=%lld)", mc, (long long)K);
     if (tp != nullptr && mc > tp->max_m)
       return set_error(DK_ERR_UNSUPPORTED, "w4a16_matmul_allreduce: %d rows exceed the communicator", mc);
@@ -1067,6 +1074,7 @@ int run_fast(const void* x, int64_t ldx, const int32_t* qweight, const void* sca
       std::memset(&p.tp, 0, sizeof(p.tp));
     const int rc = launch_gemv(mq, ms, mz, p, c, (flags & DK_FLAG_EXACT_DEQUANT) != 0, st);
     if (rc != DK_OK) return rc;
+    m0 += mc;
   }
   return DK_OK;
 }

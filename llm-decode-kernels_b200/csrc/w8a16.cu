@@ -449,9 +449,13 @@ extern "C" int dk_w8a16_matmul(const void* x, int64_t ldx, const uint8_t* wq, co
   if (!make_tensor_map_2d(&mw, wq, CU_TENSOR_MAP_DATA_TYPE_UINT8, N, K, N, 32, kRows, CU_TENSOR_MAP_SWIZZLE_NONE))
     return DK_ERR_CUDA;
   const DeviceInfo& dev = device_info();
-  for (int64_t m0 = 0; m0 < M; m0 += 16) {
-    const int mc = static_cast<int>(std::min<int64_t>(16, M - m0));
-    const Choice8 c = choose8(mc, static_cast<int>(N), static_cast<int>(K), cfg);
+  for (int64_t m0 = 0; m0 < M;) {
+    int mc = static_cast<int>(std::min<int64_t>(16, M - m0));
+    Choice8 c = choose8(mc, static_cast<int>(N), static_cast<int>(K), cfg);
+    while (c.cw == 0 && mc > 1) {  // a long K slice leaves no tile for mc staged rows: fewer rows per launch
+      mc = (mc + 1) / 2;
+      c = choose8(mc, static_cast<int>(N), static_cast<int>(K), cfg);
+    }
     if (c.cw == 0) return set_error(DK_ERR_UNSUPPORTED, "w8a16_matmul: no tile fits (M=%d, K=%lld)", mc, (long long)K);
     W8Params p;
     p.x = static_cast<const __half*>(x) + m0 * ldx;
@@ -476,6 +480,7 @@ extern "C" int dk_w8a16_matmul(const void* x, int64_t ldx, const uint8_t* wq, co
     cudaError_t e = launch(variant8(mc <= 8 ? 1 : 2, c.cw), grid, dim3((kWarps8 + 1) * 32), c.smem, st, pdl_enabled(),
                            dim3(1, c.split, 1), mw, p);
     if (e != cudaSuccess) return set_error(DK_ERR_CUDA, "w8a16 gemv launch: %s", cudaGetErrorString(e));
+    m0 += mc;
   }
   return DK_OK;
 }

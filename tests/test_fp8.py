@@ -94,6 +94,11 @@ def test_fp8_every_tile_and_split(split, block_n):
     _check(9, 512, 1000, bias=True, config={"SPLIT_K": split, "BLOCK_N": block_n})
 
 
+def test_fp8_rows_split_when_staging_is_full():
+    """14 rows of a K = 18944 slice: no tile fits 14 staged rows, so the rows go in launches of 7."""
+    _check(14, 1536, 18944)
+
+
 def test_fp8_prefill_rows():
     _check(40, 1536, 1536)
 

@@ -160,6 +160,12 @@ def test_long_k_slice(config):
     _check(1, 1536, 32512, config=config)
 
 
+def test_rows_split_when_staging_is_full():
+    """13 rows of a K = 18944 slice (Qwen2.5-7B down): the staged x of 13 rows leaves no tile, so the
+    rows go in launches of 7 and 6 (before this, no tile fitted and the call failed)."""
+    _check(13, 3584, 18944)
+
+
 def test_deterministic():
     from kernels.w4a16 import w4a16_matmul
 
