@@ -268,6 +268,31 @@ def gemv_sweep(peak_gbs: float) -> dict:
     return out
 
 
+def layer_sweep(peaks: dict) -> dict:
+    """BASELINE configs[1] at M in {1, 4, 16} (our W4A16, our FP8, cuBLAS fp16) and configs[2]
+    (RMSNorm with and without residual, SwiGLU, M in {1, 16, 2048}), three sweeps with the median,
+    min/max spread and the >10% flag (kernels/bench/sweep.py). A failure is recorded in the line
+    rather than ending the benchmark."""
+    from kernels import _lib
+    from kernels.bench import sweep
+
+    t0 = time.perf_counter()
+    try:
+        rows = sweep.run(sweep.KERNELS, sweeps=3)
+        agg = sweep.aggregate(rows, peaks["hbm_gbs"], peaks["bf16_tflops"])
+        out = {"method": "harness.time_rotating per case (CUDA graph, all inputs rotated >= 4x L2, median of 7); "
+                         "median of 3 sweeps; pct_peak of MEASURED_PEAKS hbm_gbs",
+               "flagged_spreads": sum(1 for r in agg if r.get("flag_spread")), "cases": sweep.compact(agg)}
+    except Exception as e:  # recorded, not hidden
+        out = {"error": f"{type(e).__name__}: {e}"[:300]}
+    out["seconds"] = round(time.perf_counter() - t0, 1)
+    try:
+        out["device_error"] = _lib.device_error()
+    except Exception as e:
+        out["device_error"] = f"{type(e).__name__}: {e}"[:200]
+    return out
+
+
 # ------------------------------------------------------------------------------ 7B tensor parallel
 TP_PROMPT = 1024
 
@@ -458,6 +483,9 @@ def run_ours(args, world, rank, local):
         del dec, runner
         torch.cuda.empty_cache()
         extras["tp7b"] = run_tp7b(args, world, rank)
+    if not args.no_extras and world == 1 and rank == 0:
+        torch.cuda.empty_cache()
+        extras["layer_sweep"] = layer_sweep(peaks)
     # our kernels per token: per layer norm+qkv, attention, o_proj, norm+gate_up+SwiGLU, down (FP8:
     # separate norm and SwiGLU kernels, 8 per layer), then the final norm and a quantized lm_head
     per_layer = 8 if args.backend.startswith("ours_fp8") else 5

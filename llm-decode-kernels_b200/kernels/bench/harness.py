@@ -84,9 +84,11 @@ def time_graph(fn: Callable, sets: list) -> float:
     return statistics.median(samples)
 
 
-def time_rotating(fn: Callable, args: tuple, rotate: tuple, max_copies: int = 64) -> float:
+def time_rotating(fn: Callable, args: tuple, rotate: tuple, max_copies: int = 512) -> float:
     """Graph time of fn(*args) with the tensors at positions `rotate` copied until the working set
-    exceeds 4x L2 (read from the device)."""
+    exceeds 4x L2 (read from the device), within `n_copies`' limits (at most 512 copies and 3 GiB,
+    at least 2: the reference's measure(), kernels/bench/harness.py:144-160). Sets of under ~1 MB
+    (RMSNorm or SwiGLU of a few rows) stay below 4x L2 at 512 copies, as in the reference."""
     l2_mb = torch.cuda.get_device_properties(torch.cuda.current_device()).L2_cache_size / 2**20
     nbytes = sum(tensor_bytes(args[i]) for i in rotate)
     copies = min(n_copies(nbytes, l2_mb), max_copies)

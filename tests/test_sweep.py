@@ -1,0 +1,57 @@
+"""Host logic of the layer sweep (kernels/bench/sweep.py): the case inventory, the algorithmic bytes
+(the reference's formulas, kernels/bench/sweep.py:167-169 and kernels/quant.py:52-54), and the
+median / spread aggregation over sweeps (reference kernels/bench/sweep.py:206-233). CPU only."""
+
+import pytest
+
+from kernels.bench import sweep
+
+
+def test_case_inventory():
+    specs = sweep.case_specs()
+    kinds = [s["kernel"] for s in specs]
+    assert kinds.count("copy") == 1
+    assert kinds.count("rmsnorm") == 6  # M in {1, 16, 2048} x residual or not
+    assert kinds.count("swiglu") == 3
+    assert kinds.count("w4a16") == 5 * 3 * 3  # 5 Qwen2.5-1.5B shapes x M in {1, 4, 16} x 3 impls
+    w4 = {(s["shape"]["layer"], s["shape"]["M"], s["impl"]) for s in specs if s["kernel"] == "w4a16"}
+    assert ("lm_head", 16, "fp8") in w4 and ("down", 4, "fp16") in w4
+    assert len(sweep.case_specs(("w4a16",), quick=True)) == 2 * 3 * 3
+    with pytest.raises(ValueError):
+        sweep.case_specs(("gemm",))
+
+
+def test_algorithmic_bytes():
+    def spec(kernel, impl, **shape):
+        return {"kernel": kernel, "impl": impl, "shape": shape}
+
+    # W4A16 at M = 1: x + y + packed weights, scales and zeros (qkv, lm_head of Qwen2.5-1.5B)
+    assert sweep.bytes_and_flops(spec("w4a16", "ours", layer="qkv", M=1, N=2048, K=1536)) == (1678336, 2 * 2048 * 1536)
+    assert sweep.bytes_and_flops(spec("w4a16", "ours", layer="lm_head", M=1, N=151936, K=1536))[0] == 124286720
+    # fp16 reads 2 bytes per weight, FP8 one plus a scale per column
+    assert sweep.bytes_and_flops(spec("w4a16", "fp16", layer="o", M=1, N=1536, K=1536))[0] == 3072 + 3072 + 1536 * 1536 * 2
+    assert sweep.bytes_and_flops(spec("w4a16", "fp8", layer="o", M=1, N=1536, K=1536))[0] == 3072 + 3072 + 1536 * 1536 + 3072
+    assert sweep.bytes_and_flops(spec("rmsnorm", "ours", M=16, N=1536, residual=True)) == (4 * 16 * 1536 * 2 + 2 * 1536, 0)
+    assert sweep.bytes_and_flops(spec("swiglu", "ours", M=2048, I=8960)) == (3 * 2048 * 8960 * 2, 0)
+    assert sweep.bytes_and_flops(spec("copy", "torch", elems=1024)) == (4096, 0)
+
+
+def test_aggregate_median_spread_and_errors():
+    shape = {"layer": "qkv", "M": 1, "N": 2048, "K": 1536}
+    rows = [{"kernel": "w4a16", "impl": "ours", "shape": shape, "sweep": i, "ms": ms}
+            for i, ms in enumerate([0.0030, 0.0036, 0.0033])]
+    rows += [{"kernel": "swiglu", "impl": "ours", "shape": {"M": 1, "I": 8960}, "sweep": i, "ms": 0.002} for i in range(3)]
+    rows += [{"kernel": "swiglu", "impl": "ours", "shape": {"M": 16, "I": 8960}, "sweep": 0, "error": "RuntimeError: x"}]
+    agg = sweep.aggregate(rows, peak_gbs=1000.0, peak_tflops=100.0)
+    assert [r["kernel"] for r in agg] == ["w4a16", "swiglu", "swiglu"]
+    a = agg[0]
+    assert a["sweeps"] == 3 and a["us"] == 3.3 and a["us_min"] == 3.0 and a["us_max"] == 3.6
+    assert a["spread_pct"] == pytest.approx(18.2, abs=0.05) and a["flag_spread"]
+    assert a["gbs"] == pytest.approx(1678336 / 3.3e-6 / 1e9, rel=1e-3)
+    assert a["pct_peak"] == pytest.approx(100 * a["gbs"] / 1000.0, abs=0.1)
+    assert a["tflops"] == pytest.approx(2 * 2048 * 1536 / 3.3e-6 / 1e12, abs=0.01)
+    assert not agg[1]["flag_spread"] and agg[1]["spread_pct"] == 0.0
+    assert agg[2]["sweeps"] == 0 and agg[2]["error"].startswith("RuntimeError")
+    c = sweep.compact(agg)
+    assert set(c) == {"w4a16/ours/qkv/M1", "swiglu/M1", "swiglu/M16"}
+    assert c["w4a16/ours/qkv/M1"]["us"] == 3.3 and "error" in c["swiglu/M16"]
