@@ -55,3 +55,43 @@ def test_aggregate_median_spread_and_errors():
     c = sweep.compact(agg)
     assert set(c) == {"w4a16/ours/qkv/M1", "swiglu/M1", "swiglu/M16"}
     assert c["w4a16/ours/qkv/M1"]["us"] == 3.3 and "error" in c["swiglu/M16"]
+
+
+def test_run_records_failures_and_goes_on(monkeypatch):
+    """A case that raises is recorded with its error and the sweep continues (fake timer, CPU)."""
+    calls = []
+
+    def fake_time(spec, weights):
+        calls.append(spec["kernel"])
+        if spec["kernel"] == "swiglu" and spec["shape"]["M"] == 16:
+            raise RuntimeError("no tile")
+        return 0.001
+
+    monkeypatch.setattr(sweep, "time_case", fake_time)
+    rows = sweep.run(("rmsnorm", "swiglu"), sweeps=2)
+    assert len(rows) == 2 * (6 + 3) and len(calls) == len(rows)
+    bad = [r for r in rows if "error" in r]
+    assert len(bad) == 2 and all(r["shape"]["M"] == 16 for r in bad)
+    agg = sweep.aggregate(rows, 1000.0, 100.0)
+    assert len(agg) == 9 and sum("error" in r for r in agg) == 1
+
+
+def test_bench_line_layer_sweep(monkeypatch):
+    """bench.py's layer_sweep entry: compact cases, the spread count, and a failure recorded in the
+    line instead of ending the benchmark."""
+    import bench
+    from kernels import _lib
+
+    monkeypatch.setattr(_lib, "device_error", lambda: 0)
+    monkeypatch.setattr(sweep, "time_case", lambda spec, weights: 0.002)
+    out = bench.layer_sweep({"hbm_gbs": 6000.0, "bf16_tflops": 1600.0})
+    assert out["device_error"] == 0 and out["flagged_spreads"] == 0
+    assert len(out["cases"]) == len(sweep.case_specs())
+    assert "w4a16/fp16/lm_head/M16" in out["cases"] and "rmsnorm/M2048/residual" in out["cases"]
+
+    def boom(*a, **k):
+        raise RuntimeError("CUDA error: out of memory")
+
+    monkeypatch.setattr(sweep, "run", boom)
+    out = bench.layer_sweep({"hbm_gbs": 6000.0, "bf16_tflops": 1600.0})
+    assert out["error"].startswith("RuntimeError") and "seconds" in out
