@@ -7,6 +7,8 @@ download, perplexity and chat prompts, which need the network).
 - `prefill_speed`, `layers_only_ms`: reference run.py:142-201.
 - `step_host`: the public per-token API of a server loop - the token comes from pinned host memory,
   the graph runs, the next token is read back to the host.
+- `greedy_parity`: the reference's parity figures (run.py:289-303) between two runners - max |logit
+  diff| and the first greedy divergence - for batch-1 synthetic prompts.
 """
 
 from __future__ import annotations
@@ -165,3 +167,40 @@ def layers_only_ms(runner, M: int = 1) -> float:
         times.append(start.elapsed_time(end) / 10)
     del graph
     return statistics.median(times)
+
+
+@torch.no_grad()
+def greedy_parity(runner: QwenRunner, ref: QwenRunner, ids: torch.Tensor, steps: int = 32) -> dict:
+    """Greedy decode of `steps` tokens after the prompt `ids` [1, T] by `runner` and by `ref`, each on
+    its own KV cache (eager forward steps), fed the same tokens until they disagree. Reports what
+    the reference's parity check reports (kernels/e2e/run.py:289-303): the max |logit diff| over the
+    compared positions and the index of the first greedy divergence (`steps` if none; greedy streams
+    part for good after one near-tie, so where they part is the figure, not a match fraction), plus
+    the reference's top-2 logit margin at that position (a divergence needs a logit error of at
+    least half of it) and the largest |reference logit| (for relative tolerances)."""
+    T = ids.shape[1]
+    dev = ids.device
+    pos = torch.arange(T, device=dev)
+    la = runner.forward(ids, pos)[:, -1].float()
+    lb = ref.forward(ids, pos)[:, -1].float()
+    diff = (la - lb).abs().max().item()
+    ref_abs = lb.abs().max().item()
+    toks: list[int] = []
+    first, margin = steps, None
+    for i in range(steps):
+        a, b = int(la[0].argmax()), int(lb[0].argmax())
+        if a != b:
+            top2 = lb[0].topk(2).values
+            first, margin = i, (top2[0] - top2[1]).item()
+            break
+        toks.append(b)
+        if i + 1 == steps:
+            break
+        tok = torch.tensor([[b]], device=dev)
+        p = torch.tensor([T + i], device=dev)
+        la = runner.forward(tok, p)[:, -1].float()
+        lb = ref.forward(tok, p)[:, -1].float()
+        diff = max(diff, (la - lb).abs().max().item())
+        ref_abs = max(ref_abs, lb.abs().max().item())
+    return {"max_abs_logit_diff": diff, "max_abs_ref_logit": ref_abs, "first_divergence": first,
+            "compared_tokens": steps, "ref_margin_at_divergence": margin, "tokens": toks}

@@ -158,3 +158,45 @@ def test_graph_decoder_batch16():
     dec.capture(ids)
     toks, _ = dec.generate(ids, 5)
     assert len(toks) == 16 and all(len(t) == 6 for t in toks)
+
+
+def test_greedy_parity_report():
+    """greedy_parity gives the reference's parity figures: a runner against itself agrees on every
+    token with no logit difference; against a runner whose logit for the first greedy token is
+    lowered, the streams part at index 0 and the reference's margin there is reported (CPU-capable)."""
+    from kernels.e2e.run import greedy_parity
+
+    model = tiny_model(torch.float32, DEV)
+    ids = torch.randint(0, 512, (1, 8), generator=torch.Generator().manual_seed(3)).to(DEV)
+    a = QwenRunner(model, make_backend("fp16"), max_len=32)
+    b = QwenRunner(model, make_backend("fp16"), max_len=32)
+    same = greedy_parity(a, b, ids, steps=6)
+    assert same["first_divergence"] == 6 and same["max_abs_logit_diff"] == 0.0
+    assert len(same["tokens"]) == 6 and same["ref_margin_at_divergence"] is None
+    c = QwenRunner(model, make_backend("fp16"), max_len=32)
+    c.lm_head = c.lm_head.clone()
+    c.lm_head[same["tokens"][0]] -= 10.0  # the reference side now prefers another token first
+    parted = greedy_parity(QwenRunner(model, make_backend("fp16"), max_len=32), c, ids, steps=6)
+    assert parted["first_divergence"] == 0 and parted["tokens"] == []
+    assert parted["ref_margin_at_divergence"] >= 0.0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name,ref_name", [("ours", "w4_ref"), ("ours_lm", "w4_ref_lm")])
+def test_greedy_stream_matches_reference_numerics(name, ref_name):
+    """32 greedy tokens of the fused decode path against the reference numerics (w4_ref: dequantize,
+    fp16 matmul, SDPA) on three synthetic prompts: the logits stay within the decode tolerance at
+    every compared position, so the streams can only part where the reference's top two logits are
+    within twice that tolerance (a near-tie)."""
+    from kernels.e2e.run import greedy_parity
+
+    model = tiny_model(torch.float16, "cuda")
+    g = torch.Generator().manual_seed(7)
+    for _ in range(3):
+        ids = torch.randint(0, 512, (1, 12), generator=g).cuda()
+        r = greedy_parity(QwenRunner(model, make_backend(name), max_len=64),
+                          QwenRunner(model, make_backend(ref_name), max_len=64), ids, steps=32)
+        tol = 5e-2 + 5e-2 * r["max_abs_ref_logit"]
+        assert r["max_abs_logit_diff"] <= tol, r
+        if r["first_divergence"] < 32:
+            assert r["ref_margin_at_divergence"] <= 2 * tol, r
