@@ -9,8 +9,6 @@ RuntimeError and N must be a multiple of 4.
 
 from __future__ import annotations
 
-import torch
-
 from kernels.w4a16 import w4a16_matmul
 
 _split_choice: dict[tuple, int] = {}

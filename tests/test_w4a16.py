@@ -7,7 +7,7 @@ import numpy as np
 import pytest
 import torch
 
-from _util import MATMUL_TOL, assert_matmul_close, to_cuda, w4_case, w4_ref
+from _util import assert_matmul_close, to_cuda, w4_case, w4_ref
 
 pytestmark = pytest.mark.gpu
 
