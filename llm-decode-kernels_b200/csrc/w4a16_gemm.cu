@@ -334,8 +334,9 @@ bool smem_ready() {
 }  // namespace
 
 // True when the tensor-core GEMM takes this shape: M >= 128 and N >= 128 (whole TMA boxes start
-// inside the tensors), 16-byte aligned operands, x rows 16-byte aligned; group_size 128.
-bool gemm_tc_ok(const void* x, int64_t ldx, const void* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
+// inside the tensors), 16-byte aligned operands, x rows 16-byte aligned; group_size 128. Any y row
+// stride works: the epilogue uses 16-byte stores only where the destination is aligned.
+bool gemm_tc_ok(const void* x, int64_t ldx, const void* y, int64_t /*ldy*/, int64_t M, int64_t N, int64_t K,
                 int64_t group_size) {
   return M >= kHalfRows && N >= 128 && N % 8 == 0 && K % 128 == 0 && group_size == 128 && aligned16(x) && ldx % 8 == 0 &&
          y != nullptr && M <= INT32_MAX && N <= INT32_MAX;
