@@ -376,6 +376,37 @@ def cpu_decode_rate(model, steps: int, threads: int | None = None) -> dict:
                       f"(oracle/runner.py, fp32 dequantize-then-matmul linears), after 1 untimed token"}
 
 
+def cpu_gemv_baseline(N: int = 17920, K: int = 1536, calls: int = 5) -> dict:
+    """BASELINE configs[0]: the reference's CPU W4A16 path (unpack, dequantize in fp16, fp32 matmul;
+    kernels/quant.py:31-35, kernels/reference.py:27-45) at the Qwen2.5-1.5B gate_up shape, M = 1,
+    x ~ N(0,1) and W ~ N(0,0.02) RTN int4 g128 from seed 0, with torch on all host cores
+    (oracle/torch_ref.py, pinned bit for bit to the reference's dequantized weights). Quantization is
+    excluded; median of `calls` after one warm-up call."""
+    import oracle
+    from kernels.quant import weight_bytes
+    from oracle import torch_ref
+
+    threads = os.cpu_count()
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(1, K, generator=g).half()
+    w = (torch.randn(N, K, generator=g) * 0.02).half()
+    qw, s, z = (torch.from_numpy(a) for a in oracle.quantize_rtn(w.numpy(), 128))
+    torch_ref.w4a16_ref(x, qw, s, z, 128)
+    times = []
+    for _ in range(calls):
+        t0 = time.perf_counter()
+        y = torch_ref.w4a16_ref(x, qw, s, z, 128)
+        times.append(time.perf_counter() - t0)
+    sec = statistics.median(times)
+    byts = weight_bytes(N, K) + 2 * K + 2 * N
+    assert y.shape == (1, N) and bool(torch.isfinite(y).all())
+    return {"value": round(sec * 1e3, 3), "unit": "ms", "gbs": round(byts / sec / 1e9, 3), "cores": threads,
+            "kind": "port", "shape": {"M": 1, "N": N, "K": K},
+            "sample": f"{calls} calls after 1 warm-up of the reference's w4a16_ref steps on torch CPU "
+                      f"({threads} threads)"}
+
+
 def oracle_weights(model) -> dict:
     """Packed int4 weights for the CPU oracle, quantized by libdecodek on the GPU (bit-exact with the
     oracle's quantizer, tests/test_quant.py) to keep the setup short, then moved to the host."""
@@ -478,6 +509,7 @@ def run_ours(args, world, rank, local):
         torch.cuda.empty_cache()
         if world == 1 and rank == 0:
             extras["cpu_baseline"] = cpu_decode_rate(model, steps=4)
+            extras["cpu_gemv_baseline"] = cpu_gemv_baseline()
     assert _lib.device_error() == 0, "a kernel recorded a device-side error"
     if args.tp7b == "on" or (args.tp7b == "auto" and world > 1):
         del dec, runner

@@ -127,3 +127,25 @@ def test_e4m3_roundtrip_all_codes():
             continue
         v = lib.oracle_e4m3_to_f32(b)
         assert lib.oracle_f32_to_e4m3(v) == (b if v != 0 or b == 0 else b), b
+
+
+def test_torch_cpu_restatement_golden(golden):
+    """oracle.torch_ref (the reference's CPU W4A16 path on torch, used to time the CPU baseline)
+    gives the reference's dequantized weights bit for bit, its unpacking matches the golden
+    pack/unpack vectors, and its matmul matches the reference outputs."""
+    import torch
+
+    from oracle import torch_ref
+
+    q = golden("quant")
+    unpacked = torch_ref.unpack_int4(torch.from_numpy(q["pack_packed"]))
+    assert np.array_equal(unpacked.numpy(), q["pack_unpacked"])
+    g = golden("matmul")
+    for i, (M, N, K, has_bias) in enumerate(g["w4_cases"]):
+        x, qw, s, z = (torch.from_numpy(g[f"w4_{i}_{k}"]) for k in ("x", "qweight", "scales", "zeros"))
+        if f"w4_{i}_deq" in g:
+            deq = torch_ref.dequantize(qw, s, z, 128).contiguous().numpy()
+            assert np.array_equal(_bits16(deq), _bits16(g[f"w4_{i}_deq"]))
+        bias = torch.from_numpy(g[f"w4_{i}_bias"]) if has_bias else None
+        out = torch_ref.w4a16_ref(x, qw, s, z, 128, bias).numpy()
+        np.testing.assert_allclose(out, g[f"w4_{i}_ref"], rtol=1e-5, atol=1e-5)

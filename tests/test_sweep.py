@@ -95,3 +95,13 @@ def test_bench_line_layer_sweep(monkeypatch):
     monkeypatch.setattr(sweep, "run", boom)
     out = bench.layer_sweep({"hbm_gbs": 6000.0, "bf16_tflops": 1600.0})
     assert out["error"].startswith("RuntimeError") and "seconds" in out
+
+
+def test_bench_cpu_gemv_baseline_small():
+    """bench.py's configs[0] CPU baseline (the reference's w4a16_ref steps on torch CPU) on a small
+    shape: a median time in ms, the bandwidth it implies and the thread count."""
+    import bench
+
+    out = bench.cpu_gemv_baseline(N=256, K=256, calls=2)
+    assert out["unit"] == "ms" and out["value"] > 0 and out["cores"] >= 1 and out["kind"] == "port"
+    assert out["shape"] == {"M": 1, "N": 256, "K": 256}
