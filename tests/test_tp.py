@@ -526,3 +526,60 @@ def test_tpcomm_setup_failure_releases_buffers(monkeypatch):
     with pytest.raises(RuntimeError, match="tp_buffer_open: cannot map"):
         TPComm(max_n=64, device="cuda:0")
     assert fake.log == ["alloc", "open1", "open2", "close1", "close2", "free"]
+
+
+# ------------------------------------------------ failure detection on the host (CPU, gloo ranks)
+def _departing_rank_worker(rank, world, port, q):
+    """Both ranks run one sharded decode step; rank 1 then leaves (between steps, nothing in flight)
+    and rank 0 tries the next step. Its first collective must fail within the process group's
+    timeout instead of waiting for good."""
+    import datetime
+    import time
+
+    import torch.distributed as dist
+
+    from kernels.e2e.model import QwenRunner, make_backend
+    from kernels.tp import TensorParallel
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.set_num_threads(1)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    model = tp_model(torch.float32, "cpu")
+    ids = torch.randint(0, 512, (1, 6), generator=torch.Generator().manual_seed(1))
+    shard = QwenRunner(model, make_backend("fp16"), max_len=16, batch=1, tp=TensorParallel(mode="nccl"))
+    tok = shard.greedy(shard.forward(ids, torch.arange(6)))
+    dist.barrier()
+    if rank == 1:
+        q.put((rank, "left", 0.0))
+        q.close()
+        q.join_thread()  # the message is on the pipe before the process goes
+        os._exit(0)  # leaves without a word: no destroy_process_group, no more collectives
+    time.sleep(1.0)
+    t0 = time.perf_counter()
+    try:
+        shard.forward(tok.view(1, 1), torch.tensor([6]))
+        q.put((rank, "no error", time.perf_counter() - t0))
+    except Exception as e:  # the collective reports the departed peer
+        q.put((rank, type(e).__name__, time.perf_counter() - t0))
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+def test_departed_rank_is_detected_by_the_next_collective():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_departing_rank_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    got = dict((r, (what, sec)) for r, what, sec in (q.get(timeout=5) for _ in range(2)))
+    assert got[1][0] == "left"
+    what, sec = got[0]
+    assert what != "no error", "the surviving rank's collective did not notice the departed rank"
+    assert sec < 60, f"detection took {sec:.1f} s"
