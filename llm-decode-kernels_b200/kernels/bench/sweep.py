@@ -2,6 +2,7 @@
 
     python llm-decode-kernels_b200/kernels/bench/sweep.py [--kernels copy,rmsnorm,swiglu,w4a16]
                                                           [--sweeps 3] [--quick] [--out FILE]
+                                                          [--checkpoint FILE.jsonl]
 
 Cases (the benchmark configurations of the hot path):
 * w4a16: every Qwen2.5-1.5B linear shape at M in {1, 4, 16}, for our W4A16 matmul ("ours"), our
@@ -16,8 +17,8 @@ each case reports the median over sweeps with min and max, flagging spreads over
 kernels/bench/sweep.py:206-233, docs/DECISIONS.md:27-52). Algorithmic bytes follow the reference:
 matmuls M*K*2 + M*N*2 + weight bytes, RMSNorm `rmsnorm_bytes`, SwiGLU `swiglu_bytes`.
 
-The reference's Modal checkpointing, torch.compile and torchao baselines are not part of the
-decode hot path and are left out.
+Checkpoints (`--checkpoint`) are a local JSONL file of finished rows. The reference's Modal volume,
+torch.compile and torchao baselines are not part of the decode hot path and are left out.
 """
 
 from __future__ import annotations
@@ -27,7 +28,6 @@ import json
 import os
 import statistics
 import sys
-from dataclasses import dataclass
 
 if __name__ == "__main__":
     sys.path.insert(0, os.path.abspath(os.path.join(os.path.dirname(__file__), "..", "..")))
@@ -150,22 +150,47 @@ def time_case(spec: dict, weights: _Weights) -> float:
     return time_rotating(F.linear, (x, wt["fp16"]), rotate=(0, 1))
 
 
-def run(kernels=KERNELS, sweeps: int = 3, quick: bool = False, log=None) -> list[dict]:
+def _row_key(row: dict) -> str:
+    return json.dumps([row["sweep"], row["kernel"], row["impl"], row["shape"]], sort_keys=True)
+
+
+def run(kernels=KERNELS, sweeps: int = 3, quick: bool = False, log=None, checkpoint: str | None = None) -> list[dict]:
     """Raw rows: one per (sweep, case), {"ms": ...} or {"error": ...} (a failing case is recorded
-    and the sweep goes on)."""
+    and the sweep goes on). With `checkpoint`, every finished row is appended to that JSONL file as
+    it completes, and rows already in it are reused instead of measured again, so an interrupted
+    sweep resumes where it stopped (the reference's resumable sweeps, kernels/bench/sweep.py:3-4)."""
     specs = case_specs(kernels, quick)
+    done = {}
+    if checkpoint and os.path.exists(checkpoint):
+        with open(checkpoint) as f:
+            for line in f:
+                line = line.strip()
+                if line:
+                    r = json.loads(line)
+                    done[_row_key(r)] = r
+    sink = open(checkpoint, "a") if checkpoint else None
     weights = _Weights()
     rows = []
-    for sweep in range(sweeps):
-        for spec in specs:
-            row = {**spec, "sweep": sweep}
-            try:
-                row["ms"] = time_case(spec, weights)
-            except Exception as e:  # recorded, not hidden
-                row["error"] = f"{type(e).__name__}: {e}"[:300]
-            rows.append(row)
-            if log is not None:
-                log(row)
+    try:
+        for sweep in range(sweeps):
+            for spec in specs:
+                row = {**spec, "sweep": sweep}
+                if _row_key(row) in done:
+                    rows.append(done[_row_key(row)])
+                    continue
+                try:
+                    row["ms"] = time_case(spec, weights)
+                except Exception as e:  # recorded, not hidden
+                    row["error"] = f"{type(e).__name__}: {e}"[:300]
+                rows.append(row)
+                if sink is not None:
+                    sink.write(json.dumps(row) + "\n")
+                    sink.flush()
+                if log is not None:
+                    log(row)
+    finally:
+        if sink is not None:
+            sink.close()
     return rows
 
 
@@ -228,11 +253,12 @@ def main():
     ap.add_argument("--sweeps", type=int, default=3)
     ap.add_argument("--quick", action="store_true")
     ap.add_argument("--out", default=None, help="write raw rows and the aggregate as JSON")
+    ap.add_argument("--checkpoint", default=None, help="JSONL of finished rows: appended to, and reused on a rerun")
     args = ap.parse_args()
     pk = config.peaks()
     kernels = [k for k in args.kernels.split(",") if k]
-    rows = run(kernels, args.sweeps, args.quick,
-               log=lambda r: print(json.dumps(r), flush=True))
+    rows = run(kernels, args.sweeps, args.quick, log=lambda r: print(json.dumps(r), flush=True),
+               checkpoint=args.checkpoint)
     agg = aggregate(rows, pk["hbm_gbs"], pk["bf16_tflops"])
     for r in agg:
         print(json.dumps(r), flush=True)

@@ -105,3 +105,27 @@ def test_bench_cpu_gemv_baseline_small():
     out = bench.cpu_gemv_baseline(N=256, K=256, calls=2)
     assert out["unit"] == "ms" and out["value"] > 0 and out["cores"] >= 1 and out["kind"] == "port"
     assert out["shape"] == {"M": 1, "N": 256, "K": 256}
+
+
+def test_checkpoint_resumes_without_measuring_again(monkeypatch, tmp_path):
+    """Rows go to the checkpoint as they finish; a rerun reuses them and measures only what is
+    missing (the reference's resumable sweeps)."""
+    ck = str(tmp_path / "sweep.jsonl")
+    calls = []
+
+    def timer(spec, weights):
+        calls.append(spec["kernel"])
+        if len(calls) == 5:
+            raise KeyboardInterrupt  # the first run is interrupted after 4 cases
+        return 0.001 * len(calls)
+
+    monkeypatch.setattr(sweep, "time_case", timer)
+    with pytest.raises(KeyboardInterrupt):
+        sweep.run(("rmsnorm",), sweeps=1, checkpoint=ck)
+    assert len(open(ck).read().splitlines()) == 4
+    calls.clear()
+    monkeypatch.setattr(sweep, "time_case", lambda spec, weights: calls.append(1) or 0.5)
+    rows = sweep.run(("rmsnorm",), sweeps=1, checkpoint=ck)
+    assert len(rows) == 6 and len(calls) == 2  # only the two unfinished cases were measured
+    assert [r["ms"] for r in rows[:4]] == [0.001, 0.002, 0.003, 0.004]
+    assert len(open(ck).read().splitlines()) == 6
