@@ -149,6 +149,27 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def env_info() -> dict:
+    """GPU, driver, toolkit and library versions of this run (the reference's env_info,
+    kernels/remote.py:15-52)."""
+    import platform
+
+    out = {"torch": torch.__version__, "cuda_runtime": torch.version.cuda, "python": platform.python_version(),
+           "host_cpus": os.cpu_count()}
+    try:
+        if torch.cuda.is_available():
+            p = torch.cuda.get_device_properties(torch.cuda.current_device())
+            out.update(gpu=p.name, capability=f"{p.major}.{p.minor}", sms=p.multi_processor_count,
+                       memory_gib=round(p.total_memory / 2**30, 1))
+        r = subprocess.run(["nvidia-smi", "--query-gpu=driver_version", "--format=csv,noheader"],
+                           capture_output=True, text=True, timeout=10)
+        if r.returncode == 0 and r.stdout.strip():
+            out["driver"] = r.stdout.strip().splitlines()[0]
+    except Exception as e:  # informational only
+        out["env_error"] = f"{type(e).__name__}: {e}"[:200]
+    return out
+
+
 # ------------------------------------------------------------------------------ model
 def build_model(batch: int, seed: int = 0):
     from kernels import config
@@ -535,7 +556,7 @@ def run_ours(args, world, rank, local):
                     "what": "GraphDecoder.step_host: pinned-host token -> device, graph replay, next token -> host, "
                             "host wait, every step"},
             "gpu_launches": per_step_launches * args.steps,
-            "clocks": clocks.summary()}
+            "clocks": clocks.summary(), "env": env_info()}
 
 
 def main():

@@ -129,3 +129,12 @@ def test_checkpoint_resumes_without_measuring_again(monkeypatch, tmp_path):
     assert len(rows) == 6 and len(calls) == 2  # only the two unfinished cases were measured
     assert [r["ms"] for r in rows[:4]] == [0.001, 0.002, 0.003, 0.004]
     assert len(open(ck).read().splitlines()) == 6
+
+
+def test_bench_env_info():
+    """The bench line's env entry (versions, host cores; GPU fields where a GPU is present) never
+    raises, even without nvidia-smi."""
+    import bench
+
+    env = bench.env_info()
+    assert env["torch"] and env["host_cpus"] >= 1 and "python" in env
