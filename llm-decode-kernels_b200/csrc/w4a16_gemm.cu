@@ -4,18 +4,20 @@
 // the per-column scale to the fp32 accumulator in the epilogue.
 //
 // Replaces the reference's Triton tensor-core tile kernel for large M (kernels/w4a16.py:31-97,
-// the `direct` path of w4a16_matmul) with tcgen05.mma. One CTA computes a 128 x 128 tile of y:
-// * warp 0 (one lane) streams, per 64-wide K step, the x tile [128 rows x 64] with TMA into the
-//   128-byte-swizzled K-major layout, and the packed weights of the tile (8 rows of qweight x 128
-//   columns, int32) plus the step's scale and zero rows, into a 4-stage ring;
-// * warps 2-5 dequantize: thread t owns output column n0 + t and turns its 8 packed words (64 K
-//   values) into one 128-byte row of the fp16 B tile, (q - z) * s with the reference's rounding
-//   (kernels/reference.py:35: q - z is exact in fp16, one fp16 multiply by s), written straight
-//   into the swizzled K-major layout that tcgen05 reads (16-byte chunk c of row t at c ^ (t % 8));
-// * warp 1 allocates 128 TMEM columns (the 128 x 128 fp32 accumulator) and one lane issues four
-//   K = 16 tcgen05.mma per step, releasing each stage with tcgen05.commit;
-// * warps 2-5 then read the accumulator back (tcgen05.ld, one 32-lane quarter of TMEM per warp),
-//   add the bias, round to fp16 and store.
+// the `direct` path of w4a16_matmul) with tcgen05.mma. One CTA computes a 256 x BN tile of y (BN =
+// 128, or 256 when the grid still has a tile per SM) as two 128-row accumulators that share each
+// dequantized weight tile, so a weight is dequantized once per 256 rows of x:
+// * warp 0 (one lane) streams, per 64-wide K step, the x tile [256 rows x 64] (two 128-row boxes)
+//   with TMA into the 128-byte-swizzled K-major layout, and the packed weights of the tile (8 rows of
+//   qweight x BN columns, int32) plus the step's scale and zero rows, into a 3- or 4-stage ring;
+// * warps 2-9 dequantize: the 256 threads turn the BN columns' packed words (64 K values each) into
+//   128-byte rows of the fp16 B tile, (q - z) * s with the reference's rounding (kernels/reference.py:35:
+//   q - z is exact in fp16, one fp16 multiply by s), written straight into the swizzled K-major layout
+//   that tcgen05 reads (16-byte chunk c of row t at c ^ (t % 8));
+// * warp 1 allocates 2 x BN TMEM columns (the two 128 x BN fp32 accumulators) and one lane issues the
+//   K = 16 tcgen05.mma of both halves per step, releasing each stage with tcgen05.commit;
+// * warps 2-9 then read the accumulators back (tcgen05.ld, 32-lane quarters of TMEM), apply the e4m3
+//   column scale, add the bias, round to fp16 and store.
 // Nibble pairs become fp16 with the LOP3 "magic number" conversion (0x6400 exponent; Kim et al.,
 // "Who Says Elephants Can't Run?"), after a PRMT that puts K values 2j and 2j+1 of a word into the
 // low nibble of byte 0 and the high nibble of byte 2; one fp16x2 FMA with (1, 1/16) and
