@@ -1,15 +1,38 @@
 """The reference's CPU W4A16 path, restated with torch CPU ops (multi-threaded), for timing it.
 TEST INFRASTRUCTURE AND CPU BASELINE ONLY (never the product path).
 
-Same steps as kernels/quant.py:31-35 (unpack: arithmetic shift by 4i, mask 0xF) and
+Same steps as kernels/quant.py:20-49 (pack, RTN quantization, unpack: arithmetic shift by 4i, mask 0xF) and
 kernels/reference.py:27-45 (dequantize: `(q.to(fp16) - z) * s` in fp16 with scales and zeros
 repeated over each group, transposed to [N, K]; matmul: `x.float() @ W.float().t()`). The results
-are pinned bit for bit against the C restatement (`oracle.dequantize_int4`) by tests/test_oracle.py.
+are pinned bit for bit against the golden vectors and the C restatement by tests/test_oracle.py.
 """
 
 from __future__ import annotations
 
 import torch
+
+
+def pack_int4(q: torch.Tensor) -> torch.Tensor:
+    """[K, N] integers 0..15 -> int32 [K/8, N]: value i of 8 consecutive K rows in bits 4i..4i+3 of a
+    32-bit word, read as a signed int32 (kernels/quant.py:20-28)."""
+    K, N = q.shape
+    rows = q.to(torch.int64).reshape(K // 8, 8, N)
+    word = (rows << torch.arange(0, 32, 4, dtype=torch.int64).view(1, 8, 1)).sum(dim=1)
+    return (word - ((word >> 31) << 32)).to(torch.int32)
+
+
+def quantize_rtn(weight: torch.Tensor, group_size: int = 128):
+    """fp16 [N, K] -> (qweight int32 [K/8, N], scales fp16 [K/g, N], zeros fp16 [K/g, N]): per group of
+    `group_size` K values and column, fp32 min and max, scale = (max - min) / 15 clamped to >= 1e-6,
+    zero = round(-min / scale) clamped to 0..15, q = round(w / scale + zero) clamped to 0..15, rounding
+    half to even (kernels/quant.py:38-49)."""
+    N, K = weight.shape
+    w = weight.t().float().reshape(K // group_size, group_size, N)
+    lo, hi = w.amin(dim=1), w.amax(dim=1)
+    scale = ((hi - lo) / 15).clamp(min=1e-6)
+    zero = (-lo / scale).round().clamp(0, 15)
+    q = (w / scale[:, None, :] + zero[:, None, :]).round().clamp(0, 15)
+    return pack_int4(q.reshape(K, N).to(torch.int32)), scale.to(weight.dtype), zero.to(weight.dtype)
 
 
 def unpack_int4(packed: torch.Tensor) -> torch.Tensor:

@@ -149,3 +149,56 @@ def test_torch_cpu_restatement_golden(golden):
         bias = torch.from_numpy(g[f"w4_{i}_bias"]) if has_bias else None
         out = torch_ref.w4a16_ref(x, qw, s, z, 128, bias).numpy()
         np.testing.assert_allclose(out, g[f"w4_{i}_ref"], rtol=1e-5, atol=1e-5)
+
+
+def test_torch_quantize_rtn_golden(golden):
+    """oracle.torch_ref.quantize_rtn reproduces the reference's golden quantizations bit for bit."""
+    import torch
+
+    from oracle import torch_ref
+
+    g = golden("quant")
+    for case in ("rtn0", "rtn1", "rtn2", "rtn3", "rtn4", "rtnedge"):
+        qw, s, z = torch_ref.quantize_rtn(torch.from_numpy(g[f"{case}_w"]), 128)
+        assert np.array_equal(qw.numpy(), g[f"{case}_qweight"]), case
+        assert np.array_equal(_bits16(s.numpy()), _bits16(g[f"{case}_scales"])), case
+        assert np.array_equal(_bits16(z.numpy()), _bits16(g[f"{case}_zeros"])), case
+
+
+def _weights_strategy():
+    from hypothesis import strategies as st
+    from hypothesis.extra import numpy as hnp
+
+    finite16 = st.floats(min_value=-60000, max_value=60000, allow_nan=False, allow_infinity=False, width=16)
+    specials = st.sampled_from([0.0, -0.0, 1.0, -1.0, 6e-8, -6e-8, 1e-4, 65504.0, -65504.0, 0.5, 0.25])
+    return st.tuples(st.integers(1, 4), st.sampled_from([128, 256])).flatmap(
+        lambda nk: hnp.arrays(np.float16, (nk[0], nk[1]), elements=st.one_of(finite16, specials)))
+
+
+def test_two_restatements_of_rtn_agree():
+    """Property check of the quantizer's edge handling: the C restatement (oracle.quantize_rtn) and the
+    torch one (oracle.torch_ref) agree on arbitrary fp16 groups - constants, signed zeros, subnormals,
+    the fp16 extremes, mixed magnitudes: packed weights and scales bit for bit, zero points by value.
+    A group whose minimum is a zero present with both signs is the one place the zero point's sign
+    bit can differ: torch's min/max reductions return whichever signed zero their lane order keeps
+    (a [+0, -0, ...] group gives -0, a [-0, +0, ...] one +0), the C loop the first one. The sign of a
+    zero point changes no packed value and no dequantized weight ((q - (+0)) and (q - (-0)) are equal),
+    and the defined cases (all +0, all -0) are pinned bit for bit by the golden vectors."""
+    import torch
+    from hypothesis import given, settings
+
+    from oracle import torch_ref
+
+    @settings(max_examples=300, deadline=None)
+    @given(_weights_strategy())
+    def check(w):
+        qc, sc, zc = oracle.quantize_rtn(w, 128)
+        qt, st_, zt = torch_ref.quantize_rtn(torch.from_numpy(w), 128)
+        assert np.array_equal(qc, qt.numpy())
+        assert np.array_equal(_bits16(sc), _bits16(st_.numpy()))
+        assert np.array_equal(zc.astype(np.float32), zt.numpy().astype(np.float32))
+        deq_c = oracle.dequantize_int4(qc, sc, zc, 128)
+        deq_t = torch_ref.dequantize(qt, st_, zt, 128).contiguous().numpy()
+        assert np.array_equal(deq_c.astype(np.float32), deq_t.astype(np.float32))
+
+    check()
