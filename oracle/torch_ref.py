@@ -1,7 +1,8 @@
 """The reference's CPU W4A16 path, restated with torch CPU ops (multi-threaded), for timing it.
 TEST INFRASTRUCTURE AND CPU BASELINE ONLY (never the product path).
 
-Same steps as kernels/quant.py:20-49 (pack, RTN quantization, unpack: arithmetic shift by 4i, mask 0xF) and
+Same steps as kernels/quant.py:20-49 (pack, RTN quantization, unpack: arithmetic shift by 4i, mask 0xF),
+kernels/fp8.py:25-30 (e4m3 quantization) and
 kernels/reference.py:27-45 (dequantize: `(q.to(fp16) - z) * s` in fp16 with scales and zeros
 repeated over each group, transposed to [N, K]; matmul: `x.float() @ W.float().t()`). The results
 are pinned bit for bit against the golden vectors and the C restatement by tests/test_oracle.py.
@@ -55,3 +56,13 @@ def w4a16_ref(x: torch.Tensor, qweight, scales, zeros, group_size: int = 128, bi
     if bias is not None:
         out = out + bias.float()
     return out
+
+
+def quantize_fp8(weight: torch.Tensor):
+    """fp16 [N, K] -> (e4m3 bytes uint8 [K, N], scale fp16 [N]): per output row, scale = max |w| / 448
+    clamped to >= 1e-12, then w / scale clamped to +-448 and rounded to e4m3 by torch's cast
+    (kernels/fp8.py:25-30)."""
+    w = weight.float()
+    scale = (w.abs().amax(dim=1) / 448.0).clamp(min=1e-12)
+    wq = (w / scale[:, None]).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+    return wq.t().contiguous().view(torch.uint8), scale.to(weight.dtype)

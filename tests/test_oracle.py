@@ -202,3 +202,23 @@ def test_two_restatements_of_rtn_agree():
         assert np.array_equal(deq_c.astype(np.float32), deq_t.astype(np.float32))
 
     check()
+
+
+def test_two_restatements_of_fp8_agree():
+    """The C e4m3 quantizer (oracle.quantize_fp8, its own round-to-nearest-even encoder) and torch's
+    float8_e4m3fn cast as the reference uses it (oracle.torch_ref.quantize_fp8) agree bit for bit on
+    arbitrary fp16 rows: zeros, subnormals, fp16 extremes, values that land on e4m3 rounding ties."""
+    import torch
+    from hypothesis import given, settings
+
+    from oracle import torch_ref
+
+    @settings(max_examples=300, deadline=None)
+    @given(_weights_strategy())
+    def check(w):
+        qc, sc = oracle.quantize_fp8(w)
+        qt, st_ = torch_ref.quantize_fp8(torch.from_numpy(w))
+        assert np.array_equal(_bits16(sc), _bits16(st_.numpy()))
+        assert np.array_equal(qc, qt.numpy())
+
+    check()
