@@ -66,3 +66,18 @@ def quantize_fp8(weight: torch.Tensor):
     scale = (w.abs().amax(dim=1) / 448.0).clamp(min=1e-12)
     wq = (w / scale[:, None]).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
     return wq.t().contiguous().view(torch.uint8), scale.to(weight.dtype)
+
+
+def rmsnorm_ref(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, residual=None):
+    """The reference's RMSNorm on torch (kernels/reference.py:9-19): x + residual in fp16, mean of
+    squares in fp32, weight * fp16(h * rsqrt(var + eps)). Returns `out` or `(out, x + residual)`."""
+    if residual is not None:
+        x = x + residual
+    h = x.float()
+    out = weight * (h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + eps)).to(x.dtype)
+    return out if residual is None else (out, x)
+
+
+def swiglu_ref(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """silu(gate) * up in fp16 (kernels/reference.py:22-24)."""
+    return torch.nn.functional.silu(gate) * up

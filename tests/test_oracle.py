@@ -222,3 +222,41 @@ def test_two_restatements_of_fp8_agree():
         assert np.array_equal(qc, qt.numpy())
 
     check()
+
+
+def _ulps_f16(a, b):
+    a = _bits16(np.asarray(a, dtype=np.float16)).astype(np.int32)
+    b = _bits16(np.asarray(b, dtype=np.float16)).astype(np.int32)
+    a = np.where(a & 0x8000, 0x8000 - a, a)
+    b = np.where(b & 0x8000, 0x8000 - b, b)
+    return np.abs(a - b)
+
+
+def test_rmsnorm_and_swiglu_restatements_agree():
+    """The numpy oracle's RMSNorm and SwiGLU against the reference's torch formulation on random rows
+    (hypothesis): residual outputs bit for bit, normalized outputs and activations within one fp16 ulp
+    (numpy and torch may round rsqrt / exp in fp32 differently by an ulp before the fp16 rounding)."""
+    import torch
+    from hypothesis import given, settings
+    from hypothesis import strategies as st
+    from hypothesis.extra import numpy as hnp
+
+    from oracle import torch_ref
+
+    vals = st.floats(min_value=-8, max_value=8, allow_nan=False, width=16)
+
+    @settings(max_examples=150, deadline=None)
+    @given(st.integers(1, 3).flatmap(lambda m: st.tuples(
+        hnp.arrays(np.float16, (m, 64), elements=vals), hnp.arrays(np.float16, (m, 64), elements=vals),
+        hnp.arrays(np.float16, (64,), elements=st.floats(0.5, 1.5, width=16)))))
+    def check(args):
+        x, r, w = args
+        out_n, res_n = ref.rmsnorm_ref(x, w, 1e-6, residual=r)
+        out_t, res_t = torch_ref.rmsnorm_ref(torch.from_numpy(x), torch.from_numpy(w), 1e-6, torch.from_numpy(r))
+        assert np.array_equal(_bits16(res_n), _bits16(res_t.numpy()))
+        assert (_ulps_f16(out_n, out_t.numpy()) <= 1).all()
+        act_n = ref.swiglu_ref(x, r)
+        act_t = torch_ref.swiglu_ref(torch.from_numpy(x), torch.from_numpy(r))
+        assert (_ulps_f16(act_n, act_t.numpy()) <= 1).all()
+
+    check()
