@@ -1,11 +1,12 @@
-"""The reference's CPU W4A16 path, restated with torch CPU ops (multi-threaded), for timing it.
+"""The reference's CPU path for the hot-path ops, restated with torch CPU ops (multi-threaded): to
+time the CPU baseline and to cross-check the C / numpy oracle on many inputs.
 TEST INFRASTRUCTURE AND CPU BASELINE ONLY (never the product path).
 
-Same steps as kernels/quant.py:20-49 (pack, RTN quantization, unpack: arithmetic shift by 4i, mask 0xF),
-kernels/fp8.py:25-30 (e4m3 quantization) and
-kernels/reference.py:27-45 (dequantize: `(q.to(fp16) - z) * s` in fp16 with scales and zeros
-repeated over each group, transposed to [N, K]; matmul: `x.float() @ W.float().t()`). The results
-are pinned bit for bit against the golden vectors and the C restatement by tests/test_oracle.py.
+Same steps as kernels/quant.py:20-49 (pack, RTN quantization, unpack: arithmetic shift by 4i, mask
+0xF), kernels/fp8.py:25-30 (e4m3 quantization) and kernels/reference.py:9-45 (RMSNorm, SwiGLU;
+dequantize: `(q.to(fp16) - z) * s` in fp16 with scales and zeros repeated over each group,
+transposed to [N, K]; matmul: `x.float() @ W.float().t()`). tests/test_oracle.py pins these against
+the golden vectors and checks them against the C / numpy oracle.
 """
 
 from __future__ import annotations
