@@ -463,7 +463,12 @@ def run_reference(args, world, rank):
         return {"impl": "reference", "unavailable": "needs a GPU to generate the benchmark model's weights"}
     base = cpu_decode_rate(model, steps)
     v = base["value"]
+    try:
+        gemv = cpu_gemv_baseline()
+    except Exception as e:  # informational beside the arm's own number
+        gemv = {"error": f"{type(e).__name__}: {e}"[:200]}
     return {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus,
+            "cpu_gemv_baseline": gemv,
             "steps": steps, "warmup": 1, "ms_per_step": round(1e3 / v, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": workload_config(args, world),
