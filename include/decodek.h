@@ -102,9 +102,12 @@ int dk_dequantize_int4(const int32_t* qweight, const void* scales, const void* z
 /* w4a16_matmul (kernels/w4a16.py:301-330) and w4a16_decode (kernels/cuda/w4a16_decode.cu:136-181):
  * y[M, N] fp16 = x[M, K] fp16 @ dequant(W).T (+ bias[N]), fp32 accumulation.
  * x rows have stride ldx, y rows stride ldy (elements). bias may be NULL. cfg may be NULL.
- * M <= 16 rows per launch run the decode GEMV; M >= 128 and N >= 128 (aligned, group_size 128) run the
- * tcgen05 tensor-core GEMM (kernels/w4a16.py:31-97), which always rounds every dequantized weight to
- * fp16 like the reference's dequantize-then-matmul; other shapes loop the GEMV over 16-row blocks. */
+ * Dispatch by rows (fast-path shapes: N % 8 == 0, group_size 128, 16-byte aligned operands):
+ * up to 15 rows, or 16 with K < 4096: the decode GEMV, up to 16 rows per launch (fewer when a long K
+ * slice leaves no tile for the staged rows); 16-127 rows with N >= 128: the tcgen05 small-M kernel;
+ * M >= 128 and N >= 128: the tcgen05 tensor-core GEMM (kernels/w4a16.py:31-97). The tcgen05 kernels
+ * round every dequantized weight to fp16 like the reference's dequantize-then-matmul. DK_FLAG_GEMV
+ * keeps any M on the decode GEMV. Other shapes run a one-thread-per-output kernel. */
 int dk_w4a16_matmul(const void* x, int64_t ldx, const int32_t* qweight, const void* scales,
                     const void* zeros, const void* bias, void* y, int64_t ldy, int64_t M,
                     int64_t N, int64_t K, int64_t group_size, const dk_matmul_config* cfg,
@@ -146,8 +149,10 @@ int dk_dequantize_fp8(const uint8_t* wq, const void* scale, void* w, int64_t N, 
 /* w8a16_matmul (kernels/fp8.py:200-223): y[M, N] fp16 = (x[M, K] @ fp16(wq)) * scale (+ bias),
  * wq e4m3 [K, N] (N contiguous), scale fp16 [N], fp32 accumulation, the scale applied to the
  * fp32 sum (kernels/fp8.py:81-82). cfg as for dk_w4a16_matmul (split_k, block_n, flags).
- * M >= 128 and N >= 128 (N % 16 == 0, K % 64 == 0, aligned) run the tcgen05 tensor-core GEMM
- * (kernels/fp8.py:42-127 for large M); DK_FLAG_GEMV keeps the 16-row decode kernel. */
+ * Dispatch by rows as for dk_w4a16_matmul: the decode GEMV (up to 16 rows per launch, fewer for long
+ * K slices), the tcgen05 small-M kernel for 16-127 rows (N >= 128, K % 64 == 0; 16 rows only with
+ * K >= 4096), the tcgen05 tensor-core GEMM for M >= 128 and N >= 128 (N % 16 == 0, K % 64 == 0,
+ * aligned; kernels/fp8.py:42-127 for large M). DK_FLAG_GEMV keeps any M on the decode kernel. */
 int dk_w8a16_matmul(const void* x, int64_t ldx, const uint8_t* wq, const void* scale, const void* bias,
                     void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, const dk_matmul_config* cfg,
                     dk_stream_t stream);
