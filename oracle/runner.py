@@ -4,7 +4,7 @@ TEST INFRASTRUCTURE AND CPU BASELINE ONLY (never the product path).
 Follows kernels/e2e/model.py:216-253 (layer structure, fused residual+RMSNorm, fused qkv and
 gate_up, RoPE, GQA attention over positions 0..pos, tied lm_head) with the linears of
 kernels/reference.py:39-45 (`x.float() @ dequant(W).float().t()`): every weight is dequantized once
-with the oracle's bit-exact int4 dequantization and kept in fp32; activations stay fp32 (the
+(oracle.torch_ref, bit-exact with the reference's dequantization) and kept in fp32; activations stay fp32 (the
 reference's CPU path computes its matmuls in fp32). Used to time the reference's CPU path on the
 benchmark model and, on the tiny model, pinned against the reference runner's golden logits.
 """
@@ -17,6 +17,7 @@ import numpy as np
 import torch
 
 import oracle
+from oracle import torch_ref
 
 
 class OracleRunner:
@@ -31,8 +32,9 @@ class OracleRunner:
         self.nq, self.nkv, self.hd, self.eps, self.max_len = n_heads, n_kv, head_dim, eps, max_len
 
         def dense(w):
-            if isinstance(w, tuple):
-                return torch.from_numpy(oracle.dequantize_int4(*w, 128).astype(np.float32))
+            if isinstance(w, tuple):  # torch restatement of the dequantization: same bits, all cores
+                qw, s, z = (torch.as_tensor(np.asarray(a)) for a in w)
+                return torch_ref.dequantize(qw, s, z, 128).float().contiguous()
             return torch.as_tensor(np.asarray(w, dtype=np.float32))
 
         f32 = lambda a: torch.as_tensor(np.asarray(a, dtype=np.float32))  # noqa: E731
