@@ -19,6 +19,9 @@ def decode_attention(qkv, k_cache, v_cache, pos, cos, sin, n_heads, n_kv, splits
     hd = k_cache.shape[-1]
     max_len = k_cache.shape[-2]
     assert T == 1 and width == (n_heads + 2 * n_kv) * hd
+    assert tuple(k_cache.shape) == (B, n_kv, max_len, hd) and v_cache.shape == k_cache.shape, (
+        "decode_attention: k_cache and v_cache must be [B, n_kv, max_len, head_dim]")
+    assert pos.numel() >= 1, "decode_attention: pos holds the position"
     _lib.require_cuda("decode_attention", qkv, k_cache, v_cache, pos, cos, sin)
     _lib.require_dtype("decode_attention", torch.float16, qkv, k_cache, v_cache, cos, sin)
     _lib.require_dtype("decode_attention", torch.int64, pos)

@@ -23,6 +23,7 @@ def _launch(gate2: torch.Tensor, up2: torch.Tensor) -> torch.Tensor:
 
 def swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     """silu(gate) * up for two same-shape tensors (reference kernels/swiglu.py:49-53)."""
+    assert gate.shape == up.shape, "swiglu: gate and up must have the same shape"
     I = gate.shape[-1]
     out = _launch(gate.reshape(-1, I), up.reshape(-1, I))
     return out.view(gate.shape)

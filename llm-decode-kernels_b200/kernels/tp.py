@@ -194,11 +194,12 @@ def w4a16_matmul_allreduce(x, qweight, scales, zeros, comm: TPComm, group_size=1
     """Row-sharded w4a16_matmul with the allreduce fused in: every rank passes its K-shard of x
     [..., K_r] and of the weight and gets y = fp16(sum over ranks of x_r @ dequant(W_r).T + bias),
     identical on every rank. All ranks must make the same calls in the same order."""
-    from kernels.w4a16 import _config
+    from kernels.w4a16 import _check_weight_shapes, _config
 
     K = x.shape[-1]
     N = qweight.shape[1]
     assert qweight.shape[0] * 8 == K and K % group_size == 0
+    _check_weight_shapes("w4a16_matmul_allreduce", K, N, scales, zeros, group_size, bias)
     _lib.require_cuda("w4a16_matmul_allreduce", x, qweight, scales, zeros, bias)
     _lib.require_dtype("w4a16_matmul_allreduce", torch.float16, x, scales, zeros, bias)
     _lib.require_dtype("w4a16_matmul_allreduce", torch.int32, qweight)

@@ -37,6 +37,15 @@ TC_MIN_ROWS = 128  # rows from which dk_w4a16_matmul runs the tensor-core GEMM
 SPLIT_FUSED_ROWS = 16
 
 
+def _check_weight_shapes(what, K, N, scales, zeros, group_size, bias):
+    """The packed weight's scales / zeros are [K/group_size, N] and the bias [N]: the kernels read
+    exactly those extents, so a smaller tensor would be read past its end."""
+    g = K // group_size
+    assert tuple(scales.shape) == (g, N) and tuple(zeros.shape) == (g, N), (
+        f"{what}: scales and zeros must be [{g}, {N}], got {tuple(scales.shape)} and {tuple(zeros.shape)}")
+    assert bias is None or tuple(bias.shape) == (N,), f"{what}: bias must be [{N}]"
+
+
 def _config(config: dict | None) -> _lib.MatmulConfig:
     c = _lib.MatmulConfig()
     if not config:
@@ -70,6 +79,7 @@ def w4a16_matmul(x, qweight, scales, zeros, group_size=128, bias=None, config=No
     K = x.shape[-1]
     N = qweight.shape[1]
     assert qweight.shape[0] * 8 == K and K % group_size == 0
+    _check_weight_shapes("w4a16_matmul", K, N, scales, zeros, group_size, bias)
     _lib.require_cuda("w4a16_matmul", x, qweight, scales, zeros, bias)
     _lib.require_dtype("w4a16_matmul", torch.float16, x, scales, zeros, bias)
     _lib.require_dtype("w4a16_matmul", torch.int32, qweight)
@@ -99,6 +109,7 @@ def w4a16_swiglu(x, qweight, scales, zeros, group_size=128, bias=None, config=No
     K = x.shape[-1]
     N = qweight.shape[1]
     assert qweight.shape[0] * 8 == K and K % group_size == 0 and N % 2 == 0
+    _check_weight_shapes("w4a16_swiglu", K, N, scales, zeros, group_size, bias)
     I = N // 2
     _lib.require_cuda("w4a16_swiglu", x, qweight, scales, zeros, bias)
     _lib.require_dtype("w4a16_swiglu", torch.float16, x, scales, zeros, bias)
@@ -134,6 +145,9 @@ def w4a16_rmsnorm_matmul(x, norm_weight, eps, residual, qweight, scales, zeros, 
     K = x.shape[-1]
     N = qweight.shape[1]
     assert qweight.shape[0] * 8 == K and K % group_size == 0
+    _check_weight_shapes("w4a16_rmsnorm_matmul", K, N, scales, zeros, group_size, bias)
+    assert norm_weight.numel() == K, f"w4a16_rmsnorm_matmul: norm_weight must have {K} elements"
+    assert residual is None or residual.shape == x.shape, "w4a16_rmsnorm_matmul: residual must match x"
     _lib.require_cuda("w4a16_rmsnorm_matmul", x, residual, norm_weight, qweight, scales, zeros, bias)
     _lib.require_dtype("w4a16_rmsnorm_matmul", torch.float16, x, residual, norm_weight, scales, zeros, bias)
     x2 = x.reshape(-1, K)
