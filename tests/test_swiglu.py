@@ -69,7 +69,7 @@ def test_gate_up_with_fused_swiglu(M, N, K):
     """w4a16_swiglu (gate_up GEMV with SwiGLU in its epilogue) == swiglu_fused(w4a16_matmul(...))
     within 1 fp16 ulp: the fused epilogue rounds g and u to fp16 before the activation exactly like
     the two-kernel path, only the fp32 summation order of the GEMV differs."""
-    from kernels.w4a16 import w4a16_matmul, w4a16_swiglu
+    from kernels.w4a16 import w4a16_swiglu
     from _util import w4_case, w4_ref
 
     x, qw, s, z, _ = w4_case(M, N, K)

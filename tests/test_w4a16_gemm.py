@@ -3,7 +3,6 @@ dequantize-then-fp32-matmul (reference kernels/reference.py:39-45), rtol 2e-2 / 
 decode GEMV run over 16-row blocks. The GEMM rounds every dequantized weight to fp16 like the
 reference, so the only differences are fp32 summation order and the final fp16 rounding."""
 
-import numpy as np
 import pytest
 import torch
 
