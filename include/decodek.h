@@ -26,7 +26,7 @@ extern "C" {
 
 typedef struct CUstream_st* dk_stream_t; /* same type as cudaStream_t */
 
-#define DK_ABI_VERSION 3
+#define DK_ABI_VERSION 4
 
 /* status codes */
 #define DK_OK 0
@@ -41,6 +41,8 @@ typedef struct CUstream_st* dk_stream_t; /* same type as cudaStream_t */
 #define DK_DEVERR_WAIT_EMPTY 2 /* the producer gave up waiting for a stage to be released */
 #define DK_DEVERR_BAD_POSITION 3 /* decode attention: position outside [0, max_len) (no write done) */
 #define DK_DEVERR_TP_WAIT 4      /* a fused-allreduce CTA gave up waiting for a peer's partial sums */
+#define DK_DEVERR_STEP_WAIT 5    /* decode step: a CTA gave up waiting for another CTA or for its weight ring */
+#define DK_DEVERR_BAD_TOKEN 6    /* decode step: a token id outside [0, vocab) (row 0 used instead) */
 
 /* dk_matmul_config.flags */
 #define DK_FLAG_STATIC_WEIGHTS 1 /* weights are not written by any kernel still in flight on the
@@ -191,6 +193,72 @@ int dk_decode_attention(const void* qkv, void* k_cache, void* v_cache, const int
                         int64_t nkv, int64_t head_dim, int64_t max_len, int64_t rope_stride,
                         int32_t splits, int32_t flags, dk_stream_t stream);
 
+/* ---- fused decode step: one persistent kernel per token ------------------------------------
+ * One greedy decode step of a Qwen2 model with W4A16 linears and a tied or untied fp16 lm_head, for
+ * 1..4 sequences: the reference runner's T == 1 forward (kernels/e2e/model.py:216-253: embedding,
+ * per layer residual + RMSNorm, qkv with bias, RoPE, KV-cache append, GQA attention over positions
+ * 0..pos, o_proj, residual + RMSNorm, gate_up, SwiGLU, down; final norm, lm_head) followed by the
+ * greedy step of its graph decoder (kernels/e2e/run.py:69-74: argmax, token feedback, position
+ * bump), as ONE cooperative kernel with one CTA per SM. Each CTA's producer warp streams its share
+ * of every op's weights into shared memory ahead of the op's input (the weights are constant), and
+ * the ops meet through arrival counters in the workspace. Numerics are those of the separate
+ * kernels: dk_w4a16_rmsnorm_matmul / dk_w4a16_matmul (factored int4), dk_decode_attention,
+ * dk_rmsnorm, and an fp16 lm_head with fp32 accumulation rounded to fp16 before the argmax (ties to
+ * the lowest index, like torch.argmax). No reference counterpart as one kernel.
+ * Limits: batch <= 4, head_dim 128, <= 8 query heads per kv head, hidden, intermediate and
+ * n_heads * 128 multiples of 256, vocab % 32 == 0, max_len % 128 == 0, group size 128, 16-byte
+ * aligned tensors (DK_ERR_UNSUPPORTED / DK_ERR_ALIGN otherwise: use the per-op entry points). */
+typedef struct dk_step_layer {
+  const void* input_norm; /* fp16 [hidden] */
+  const void* post_norm;  /* fp16 [hidden] */
+  const int32_t* qkv_qweight; /* [hidden/8, (n_heads + 2 n_kv) * head_dim]: q, k, v stacked */
+  const void* qkv_scales;
+  const void* qkv_zeros;
+  const void* qkv_bias; /* fp16 [(n_heads + 2 n_kv) * head_dim] or NULL */
+  const int32_t* o_qweight; /* [n_heads * head_dim / 8, hidden] */
+  const void* o_scales;
+  const void* o_zeros;
+  const void* o_bias;
+  const int32_t* gate_up_qweight; /* [hidden/8, 2 * intermediate]: gate then up */
+  const void* gate_up_scales;
+  const void* gate_up_zeros;
+  const void* gate_up_bias;
+  const int32_t* down_qweight; /* [intermediate/8, hidden] */
+  const void* down_scales;
+  const void* down_zeros;
+  const void* down_bias;
+} dk_step_layer;
+
+typedef struct dk_step_model {
+  int32_t n_layers, hidden, n_heads, n_kv, head_dim, intermediate, vocab, max_len, batch;
+  float eps;
+  const void* embed;      /* fp16 [vocab, hidden] */
+  const void* final_norm; /* fp16 [hidden] */
+  const void* lm_head;    /* fp16 [vocab, hidden]; may be `embed` (tied) */
+  const void* rope_cos;   /* fp16 [max_len, head_dim]: cos(pos * inv_freq) of cat(freqs, freqs) */
+  const void* rope_sin;
+  void* k_cache;          /* fp16 [n_layers, batch, n_kv, max_len, head_dim] */
+  void* v_cache;
+  const dk_step_layer* layers; /* [n_layers] */
+} dk_step_model;
+
+typedef struct dk_step_plan dk_step_plan;
+
+/* Bytes of the device workspace a plan needs (op table, tensor maps, arrival counters, the
+ * activations between ops, attention and argmax partials). */
+int dk_step_workspace_bytes(const dk_step_model* model, uint64_t* bytes);
+/* Set-up only (synchronizes): build the step program for `model` in `workspace` (device memory of
+ * at least dk_step_workspace_bytes, 256-byte aligned, owned by the caller and kept alive with the
+ * plan). The model's tensors are referenced, not copied. */
+int dk_step_create(const dk_step_model* model, void* workspace, uint64_t bytes, dk_step_plan** plan);
+/* One decode step on `stream`: tokens int64 [batch] (this step's input tokens; overwritten with the
+ * greedy picks), pos int64 [1] (their position; incremented), history int64 [batch, history_ld] or
+ * NULL (history[b][pos] = pick), logits fp16 [batch, vocab] or NULL. All device pointers, read on the
+ * device, so one captured launch replays for every step. Calls on one plan must not overlap. */
+int dk_step_run(const dk_step_plan* plan, int64_t* tokens, int64_t* pos, int64_t* history, int64_t history_ld,
+                void* logits, dk_stream_t stream);
+int dk_step_destroy(dk_step_plan* plan);
+
 /* ---- tensor parallelism: row-sharded W4A16 projection fused with its allreduce ------------
  * No reference counterpart: the reference runs on one GPU (README.md:249). These entry points serve
  * the tensor-parallel runner (column-sharded qkv/gate_up/lm_head, row-sharded o_proj/down), one
@@ -247,9 +315,11 @@ int dk_w4a16_matmul_allreduce(const void* x, int64_t ldx, const int32_t* qweight
  * (larger N returns DK_ERR_INVALID), M in launches of up to 16 rows, and the fast path's conditions
  * (group_size 128, N % 8 == 0, 16-byte aligned operands). It calls no cudaMalloc, cudaFree or
  * allocating library routine. Its first call on a device looks up the array's device address
- * (set-up): make that first call before any stream capture. Every call shares the one array and
- * clears its 16-byte header on `stream` first; calls that overlap on the GPU (other streams, other
- * host threads) race on it. */
+ * (set-up): make that first call before any stream capture. Every call shares the one array, which
+ * keeps what the last call left: the launch epoch in its header advances from call to call (the
+ * array is zero when the library loads), so partial sums left in the cells by an earlier call carry
+ * an older epoch tag and are never read as this call's. Calls that overlap on the GPU (other streams,
+ * other host threads) race on the array. */
 int dk_w4a16_matmul_reduce_static(const void* x, int64_t ldx, const int32_t* qweight, const void* scales,
                                   const void* zeros, const void* bias, void* y, int64_t ldy, int64_t M, int64_t N,
                                   int64_t K, int64_t group_size, const dk_matmul_config* cfg, dk_stream_t stream);

@@ -1,0 +1,1492 @@
+// One greedy decode step of a Qwen2 model as ONE persistent kernel (batch 1..4 rows).
+//
+// Replaces, for T == 1, the per-op launches of the runner's decode step (the reference's
+// kernels/e2e/model.py:216-253 forward plus the greedy pick and bookkeeping of
+// kernels/e2e/run.py:69-74): embedding lookup, per layer the fused residual + RMSNorm + qkv
+// projection, RoPE + KV-cache append + attention over positions 0..pos, o_proj, the fused residual +
+// RMSNorm + gate_up projection + SwiGLU, down_proj; then the final norm, the fp16 lm_head, the
+// greedy argmax, the token feedback and the position bump.
+//
+// Why one kernel. At batch 1 every op is a few MB or less: launches are latency chains (kernel
+// boundary, activation staging, the weight fetch, reduction, store), not bandwidth. The weights are
+// static, so they do not have to wait for the activations that multiply them:
+// * one CTA per SM (cooperative launch: all CTAs resident), 8 consumer warps and 1 producer warp;
+// * the producer warp walks the whole step's program and streams this CTA's share of every op's
+//   weights (and of the KV cache rows before `pos`) into a shared-memory ring with TMA, gated only by
+//   free ring slots - it runs ahead across op and layer boundaries, so an op's weights are usually
+//   on chip before its input exists;
+// * the consumer warps run the ops in order. An op waits for its input through a per-op arrival
+//   counter in global memory (every participating CTA of the previous op arrives once, after its
+//   stores), stages the input in shared memory (with the fused residual add + RMSNorm where the model
+//   has one), multiplies it with the weights already in the ring (mma.m16n8k16, fp32 accumulation,
+//   the int4 "magic number" unpack of the standalone GEMV kernel), reduces across warps in a fixed
+//   order and stores its output;
+// * attention is split over (sequence, kv head, 128-position slice) items; each CTA combines its 8
+//   warps' partials, and the last item of a (sequence, kv head) to arrive combines the slices.
+//   The greedy argmax is combined the same way: the last CTA to arrive picks the token.
+// Every wait is bounded (2 s); a CTA that gives up records DK_DEVERR_STEP_WAIT, skips the rest of its
+// work but still arrives everywhere it would have, so no other CTA waits forever and the counters
+// stay consistent for the next launch. No TMA multicast.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+
+struct dk_step_plan;
+
+namespace dk {
+namespace step {
+
+constexpr int kCWarps = 8;                    // consumer warps
+constexpr int kConsumers = kCWarps * 32;
+constexpr int kThreads = kConsumers + 32;     // + one producer warp
+constexpr int kMaxRows = 4;                   // batch rows of one step
+constexpr int kSlotW = 4096;                  // weight bytes of one ring slot (one TMA box)
+constexpr int kSlotSZ = 256;                  // scale + zero bytes of one int4 ring slot
+constexpr int kMaxChunks = 4;                 // int4 ops: 32-column chunks (or gate/up pairs) per CTA
+constexpr int kHd = 128;                      // head_dim
+constexpr int kAttnPos = 128;                 // cache positions per attention item (8 warps x 16)
+constexpr int kMaxGroup = 8;                  // query heads per kv head
+constexpr int kPartFloats = 2 + kHd;          // attention partial per head: max, sum, output[hd]
+constexpr int kXsPad = 16;
+
+enum OpKind : int { OP_QKV = 1, OP_ATTN = 2, OP_O = 3, OP_GATEUP = 4, OP_DOWN = 5, OP_HEAD = 6 };
+
+// One op of the step program (device memory, written once at set-up, read-only while kernels run).
+struct Op {
+  int kind, layer;
+  int cta0, ncta;   // participating CTAs: cta0 .. cta0 + ncta - 1 (mod grid); ATTN: first CTA of item 0
+  int units;        // int4: 32-column chunks (gate_up: gate/up chunk pairs); HEAD: 32-row vocab chunks
+  int stages;       // ring slots' worth of K per chunk: 256 K (int4) or 64 K (fp16 lm_head)
+  int K, N;         // inner dim; output columns (gate_up: I, the SwiGLU width)
+  int map;          // tensor-map index of the weights (int4: +1 scales, +2 zeros)
+  int from_embed;   // QKV of layer 0: the input rows are embedding rows of the step's tokens
+  const __half* x;      // input [M, K] (not read when from_embed)
+  const __half* res_in; // residual added to x before the norm, or nullptr
+  __half* res_out;      // receives the new residual h = x (+ res_in) (one CTA writes it), or nullptr
+  const __half* norm_w; // RMSNorm weight [K], or nullptr (no norm)
+  const __half* bias;   // [N] (gate_up: [2I]) or nullptr
+  __half* y;            // output [M, N] (HEAD: unused, the logits pointer is per call)
+  int cache_row0;       // ATTN: first row of this layer's cache in the 2-D cache maps
+};
+
+struct Params {
+  const Op* ops;
+  int n_ops;
+  const CUtensorMap* maps;
+  int kmap, vmap;  // K / V cache maps: [layers * B * nkv * max_len rows, head_dim]
+  int M, H, nq, nkv, max_len, vocab;
+  int nslots;      // ring slots
+  int kmax;        // largest K of the int4 ops (staged rows, {C, X} table)
+  int xs_pitch;    // bytes per staged input row
+  int red_bytes;   // reduction scratch
+  float eps, attn_scale;
+  const __half* embed;
+  const __half* rope_cos;  // [max_len, head_dim]
+  const __half* rope_sin;
+  __half* k_cache;         // [layers, B, nkv, max_len, head_dim]
+  __half* v_cache;
+  int64_t* tok;            // [M]: this step's tokens in, the greedy picks out
+  int64_t* pos;            // [1]: this step's position in, + 1 out
+  int64_t* hist;           // [M, hist_ld] or nullptr: hist[m][pos] = pick
+  int64_t hist_ld;
+  __half* logits;          // [M, vocab] or nullptr
+  unsigned* done;          // [n_ops] arrival counters
+  unsigned* exit_count;
+  unsigned* attn_count;    // [M * nkv]
+  unsigned* head_count;
+  float* attn_part;        // [M * nkv * max_splits][group][kPartFloats]
+  __half* attn_out;        // [M, nq * head_dim]
+  float* head_val;         // [grid][kMaxRows]
+  int* head_idx;           // [grid][kMaxRows]
+  int* err;
+};
+
+// ------------------------------------------------------------------------------ small helpers
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"r"(kConsumers) : "memory"); }
+
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
+
+// Participant index of this CTA in an op with participants cta0 .. cta0 + n - 1 (mod G), or -1.
+__device__ __forceinline__ int participant(int cta, int cta0, int n, int G) {
+  const int j = (cta - cta0 + G) % G;
+  return j < n ? j : -1;
+}
+
+// Attention items of the step: M sequences x nkv heads x slices of kAttnPos positions.
+__device__ __forceinline__ int attn_splits(int pos) { return pos / kAttnPos + 1; }
+
+// Ring slots one CTA uses for an op (the producer and every consumer warp walk the same sequence).
+__device__ __forceinline__ int op_slots(const Op& op, int cta, int G, int M, int nkv, int pos) {
+  if (op.kind == OP_ATTN) {
+    const int items = M * nkv * attn_splits(pos);
+    const int j = (cta - op.cta0 + G) % G;
+    const int mine = j < items ? (items - 1 - j) / G + 1 : 0;
+    return mine * 16;
+  }
+  const int j = participant(cta, op.cta0, op.ncta, G);
+  if (j < 0) return 0;
+  const int c0 = static_cast<int>(static_cast<int64_t>(j) * op.units / op.ncta);
+  const int c1 = static_cast<int>(static_cast<int64_t>(j + 1) * op.units / op.ncta);
+  return (c1 - c0) * op.stages * (op.kind == OP_GATEUP ? 2 : 1);
+}
+
+__device__ __forceinline__ int op_participants(const Op& op, int G, int M, int nkv, int pos) {
+  if (op.kind == OP_ATTN) return min(M * nkv * attn_splits(pos), G);
+  return op.ncta;
+}
+
+// ------------------------------------------------------------------------------ shared memory
+struct Smem {
+  uint8_t* w;      // [nslots][kSlotW], 1024-byte aligned
+  uint8_t* sz;     // [nslots][kSlotSZ]
+  uint8_t* xs;     // staged input rows
+  float* cx;       // int4 factored path: per (128-group, row) {C, X}, 8 rows per group
+  float* red;      // reduction scratch
+  uint64_t* full;
+  uint64_t* empty;
+};
+
+// bytes: offsets from the 1024-aligned base
+struct SmemLayout {
+  int w, sz, xs, cx, red, bars, total;
+};
+
+__host__ __device__ inline SmemLayout smem_layout(int nslots, int M, int xs_pitch, int kmax, int red_bytes) {
+  SmemLayout L;
+  L.w = 0;
+  L.sz = nslots * kSlotW;
+  L.xs = L.sz + nslots * kSlotSZ;
+  L.cx = L.xs + ((M * xs_pitch + 127) / 128) * 128;
+  L.red = L.cx + (kmax / 128) * 8 * 8;
+  L.bars = L.red + ((red_bytes + 127) / 128) * 128;
+  L.total = L.bars + 2 * nslots * 8;
+  return L;
+}
+
+// ------------------------------------------------------------------------------ ring access
+struct Ring {
+  Smem s;
+  int nslots;
+  volatile int* issued;  // slots the producer has armed (count); written by the producer only
+  volatile int* abort;
+  int* err;
+  int seen;              // this thread's last read of *issued
+
+  // Wait until slot sequence number `it` holds its data. First until the producer has armed it (so
+  // the parity wait below cannot match a phase two rounds old), then the full barrier's phase.
+  __device__ bool wait(int it) {
+    if (*abort) return false;
+    if (it >= seen) {
+      const uint64_t t0 = globaltimer_ns();
+      while ((seen = *issued) <= it) {
+        if (*abort) return false;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          record_device_error(err, DK_DEVERR_STEP_WAIT);
+          *abort = 1;
+          return false;
+        }
+      }
+      __threadfence_block();
+    }
+    const int slot = it % nslots;
+    if (!mbar_wait(&s.full[slot], (it / nslots) & 1, err, DK_DEVERR_STEP_WAIT)) {
+      *abort = 1;
+      return false;
+    }
+    return true;
+  }
+  __device__ void release(int it) { mbar_arrive(&s.empty[it % nslots]); }
+  // the same, agreed by the whole warp (the MMAs that follow need every lane)
+  __device__ bool warp_wait(int it) { return __all_sync(0xffffffffu, wait(it)); }
+};
+
+// ------------------------------------------------------------------------------ int4 GEMV pieces
+// One chunk-stage (32 columns x 256 K of packed int4) against the staged input, the factored
+// numerics of the standalone decode GEMV (s * (sum(x' (1024 + q')) - C - z X) per 128-group, the
+// reference's FACTORED path, kernels/w4a16.py:116-119): LOP3 with the 0x6400 exponent turns nibble
+// pairs into fp16 1024 + q (low nibble) or 1024 + 16 q (high nibble, whose x was staged / 16), the
+// MMA sums them against x (up to 8 batch rows as the B operand), and the per-(group, row) constants
+// C = 1024 sum(x') and X = sum(x) remove the magic-number offset and the zero point once per group.
+__device__ __forceinline__ void gemv_stage(uint32_t wbox, uint32_t szb, uint32_t xrow, uint32_t cxg, int xs_pitch,
+                                           int M, int g, int t, float (&acc)[2][4]) {
+  const uint32_t k1024 = 0x64006400u;
+  const uint32_t w_even = wbox + (2 * t) * 128 + ((g ^ (2 * t)) << 4);
+  const uint32_t w_odd = wbox + (2 * t + 1) * 128 + ((g ^ (2 * t + 1)) << 4);
+  const uint32_t x_even = xrow + (2 * t) * 16 + g * xs_pitch, x_odd = xrow + (2 * t + 1) * 16 + g * xs_pitch;
+  const bool have_row = g < M;
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const uint2 s4 = lds64(szb + half * 64 + g * 8);
+    const uint2 z4 = lds64(szb + 128 + half * 64 + g * 8);
+    float accg[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int st4 = 0; st4 < 4; ++st4) {
+      const int st = half * 4 + st4;
+      const uint4 wv = lds128(((st & 1) ? w_odd : w_even) + 1024 * (st >> 1));
+      uint4 xv = make_uint4(0, 0, 0, 0);
+      if (have_row) xv = lds128(((st & 1) ? x_odd : x_even) + 128 * (st >> 1));
+      const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
+      uint32_t W[4][4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint32_t w = words[c];
+        const uint32_t w8 = w >> 8;
+        W[c][0] = lop3_and_or(w, 0x000F000Fu, k1024);
+        W[c][1] = lop3_and_or(w, 0x00F000F0u, k1024);
+        W[c][2] = lop3_and_or(w8, 0x000F000Fu, k1024);
+        W[c][3] = lop3_and_or(w8, 0x00F000F0u, k1024);
+      }
+      mma_16816(accg[0], W[0][0], W[1][0], W[0][1], W[1][1], xv.x, xv.y);
+      mma_16816(accg[0], W[0][2], W[1][2], W[0][3], W[1][3], xv.z, xv.w);
+      mma_16816(accg[1], W[2][0], W[3][0], W[2][1], W[3][1], xv.x, xv.y);
+      mma_16816(accg[1], W[2][2], W[3][2], W[2][3], W[3][3], xv.z, xv.w);
+    }
+    const __half2 s01 = *reinterpret_cast<const __half2*>(&s4.x), s23 = *reinterpret_cast<const __half2*>(&s4.y);
+    const __half2 z01 = *reinterpret_cast<const __half2*>(&z4.x), z23 = *reinterpret_cast<const __half2*>(&z4.y);
+    const float sc[4] = {__low2float(s01), __high2float(s01), __low2float(s23), __high2float(s23)};
+    const float zc[4] = {__low2float(z01), __high2float(z01), __low2float(z23), __high2float(z23)};
+    // {C, X} of batch rows 2t and 2t + 1 (the D fragment's columns)
+    const uint4 cxr = lds128(cxg + half * 64 + (2 * t) * 8);
+    const float cx[2][2] = {{__uint_as_float(cxr.x), __uint_as_float(cxr.y)},
+                            {__uint_as_float(cxr.z), __uint_as_float(cxr.w)}};
+#pragma unroll
+    for (int tile = 0; tile < 2; ++tile)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int col = 2 * tile + (e >> 1), r = e & 1;
+        acc[tile][e] = fmaf(sc[col], accg[tile][e] - fmaf(zc[col], cx[r][1], cx[r][0]), acc[tile][e]);
+      }
+  }
+}
+
+// Stage the op's input rows in shared memory for the int4 path: optional residual add + RMSNorm
+// with the rounding of kernels/rmsnorm.py:28-37 (h = x + residual in fp16, var = sum(h^2)/K in fp32,
+// out = w * fp16(h / sqrt(var + eps))), then each 8-value block permuted to (0,4,1,5,2,6,3,7) for the
+// MMA fragments, odd K divided by 16 (exact) for the magic-number operands, and {C, X} per
+// (128-group, row). `writer`: this CTA stores h as the new residual.
+__device__ void stage_int4_input(const Params& p, const Op& op, const Smem& s, bool writer, float* inv_s,
+                                 float (*part)[kCWarps]) {
+  const int tid = threadIdx.x;
+  const int K = op.K;
+  const int nblk = K / 8;  // K % 256 == 0: a multiple of 32 blocks, so a warp's 32 items share a row
+  const bool norm = op.norm_w != nullptr;
+  auto row_ptr = [&](int m) -> const __half* {
+    if (op.from_embed) {
+      int64_t t = __ldcg(reinterpret_cast<const long long*>(p.tok) + m);
+      if (t < 0 || t >= p.vocab) {
+        record_device_error(p.err, DK_DEVERR_BAD_TOKEN);
+        t = 0;
+      }
+      return p.embed + t * static_cast<int64_t>(p.H);
+    }
+    return op.x + static_cast<int64_t>(m) * K;
+  };
+  auto load_h = [&](int m, int v) -> uint4 {  // 8 values of h = x (+ residual) at block v of row m
+    uint4 a = __ldcg(reinterpret_cast<const uint4*>(row_ptr(m)) + v);
+    if (op.res_in != nullptr) {
+      const uint4 r = __ldcg(reinterpret_cast<const uint4*>(op.res_in + static_cast<int64_t>(m) * K) + v);
+      __half2* ah = reinterpret_cast<__half2*>(&a);
+      const __half2* rh = reinterpret_cast<const __half2*>(&r);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) ah[j] = __hadd2_rn(ah[j], rh[j]);
+    }
+    return a;
+  };
+  if (norm) {
+    for (int m = 0; m < p.M; ++m) {
+      float acc = 0.f;
+      for (int v = tid; v < nblk; v += kConsumers) {
+        const uint4 a = load_h(m, v);
+        if (writer && op.res_out != nullptr) reinterpret_cast<uint4*>(op.res_out + static_cast<int64_t>(m) * K)[v] = a;
+        const __half2* ah = reinterpret_cast<const __half2*>(&a);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __half22float2(ah[j]);
+          acc = fmaf(f.x, f.x, acc);
+          acc = fmaf(f.y, f.y, acc);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if ((tid & 31) == 0) part[m][tid >> 5] = acc;
+    }
+    consumers_sync();
+    if (tid < p.M) {
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < kCWarps; ++w) tot += part[tid][w];
+      inv_s[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(K)), p.eps)));
+    }
+    consumers_sync();
+  }
+  for (int base = (tid & ~31); base < p.M * nblk; base += kConsumers) {
+    const int i = base + (tid & 31);
+    const int m = i / nblk, b = i % nblk;
+    uint4 v = load_h(m, b);
+    if (!norm && writer && op.res_out != nullptr)
+      reinterpret_cast<uint4*>(op.res_out + static_cast<int64_t>(m) * K)[b] = v;
+    if (norm) {
+      __half2* vh = reinterpret_cast<__half2*>(&v);
+      const uint4 wv = __ldg(reinterpret_cast<const uint4*>(op.norm_w) + b);
+      const __half2* wh = reinterpret_cast<const __half2*>(&wv);
+      const float sc = inv_s[m];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __half22float2(vh[j]);
+        vh[j] = __hmul2_rn(wh[j], __floats2half2_rn(__fmul_rn(f.x, sc), __fmul_rn(f.y, sc)));
+      }
+    }
+    uint4 o;
+    o.x = prmt(v.x, v.z, 0x5410);
+    o.y = prmt(v.x, v.z, 0x7632);
+    o.z = prmt(v.y, v.w, 0x5410);
+    o.w = prmt(v.y, v.w, 0x7632);
+    o.y = hmul2_rn(o.y, 0x2C002C00u);
+    o.w = hmul2_rn(o.w, 0x2C002C00u);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&o.x));
+    const float2 bb = __half22float2(*reinterpret_cast<const __half2*>(&o.y));
+    const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&o.z));
+    const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&o.w));
+    const float even = (a.x + a.y) + (c.x + c.y), odd = (bb.x + bb.y) + (d.x + d.y);
+    float C = even + odd, X = fmaf(16.f, odd, even);
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) {
+      C += __shfl_xor_sync(0xffffffffu, C, off);
+      X += __shfl_xor_sync(0xffffffffu, X, off);
+    }
+    if ((tid & 15) == 0) {
+      float* dst = s.cx + 2 * ((b >> 4) * 8 + m);
+      dst[0] = 1024.f * C;
+      dst[1] = X;
+    }
+    *reinterpret_cast<uint4*>(s.xs + m * p.xs_pitch + b * 16) = o;
+  }
+  consumers_sync();
+}
+
+__device__ __forceinline__ __half swiglu_pick(float g, float u, const __half* bias, int n, int I) {
+  if (bias != nullptr) {
+    g += __half2float(__ldg(bias + n));
+    u += __half2float(__ldg(bias + I + n));
+  }
+  const float gf = __half2float(__float2half_rn(g));
+  const __half act = __float2half_rn(__fdiv_rn(gf, __fadd_rn(1.0f, expf(-gf))));
+  return __hmul_rn(act, __float2half_rn(u));
+}
+
+// An int4 projection (QKV, O, GATEUP, DOWN) of this CTA's chunk range [c0, c1). Unit u of the range
+// (chunk c0 + u / stages, stage u % stages) sits at ring slot base + u (gate_up: 2u and 2u + 1, the
+// gate and the up box) and belongs to consumer warp u % kCWarps, which keeps its sum in registers
+// while consecutive units stay in one chunk and parks it in red[chunk][warp] when the chunk changes.
+__device__ void run_int4(const Params& p, const Op& op, Ring& ring, int base, int c0, int c1) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const bool pair = op.kind == OP_GATEUP;
+  const int halves = pair ? 2 : 1;
+  const int nunits = (c1 - c0) * op.stages;
+  const int M = p.M;
+  // red[chunk][warp][half][row][32]
+  float* red = ring.s.red;
+  auto cell = [&](int cl, int w, int h, int m) { return red + (((cl * kCWarps + w) * 2 + h) * kMaxRows + m) * 32; };
+  for (int cl = 0; cl < c1 - c0; ++cl)
+    for (int h = 0; h < halves; ++h)
+      for (int m = 0; m < M; ++m) cell(cl, warp, h, m)[lane] = 0.f;
+  float acc[2][2][4];
+  int cur = -1;
+  auto flush = [&]() {
+    if (cur < 0) return;
+    for (int h = 0; h < halves; ++h)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int m = 2 * t + e;
+        if (m < M) {
+          float* dst = cell(cur, warp, h, m) + 4 * g;
+          dst[0] = acc[h][0][e];
+          dst[1] = acc[h][0][2 + e];
+          dst[2] = acc[h][1][e];
+          dst[3] = acc[h][1][2 + e];
+        }
+      }
+  };
+  const uint32_t w_base = smem_addr(ring.s.w), sz_base = smem_addr(ring.s.sz);
+  const uint32_t xs_base = smem_addr(ring.s.xs), cx_base = smem_addr(ring.s.cx);
+  for (int u = warp; u < nunits; u += kCWarps) {
+    const int cl = u / op.stages, st = u % op.stages;
+    if (cl != cur) {
+      flush();
+      cur = cl;
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int a = 0; a < 2; ++a)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[h][a][e] = 0.f;
+    }
+    const uint32_t xrow = xs_base + st * 512, cxg = cx_base + st * 2 * 64;
+    for (int h = 0; h < halves; ++h) {
+      const int it = base + u * halves + h;
+      if (!ring.warp_wait(it)) break;
+      const int slot = it % ring.nslots;
+      gemv_stage(w_base + slot * kSlotW, sz_base + slot * kSlotSZ, xrow, cxg, p.xs_pitch, M, g, t, acc[h]);
+      __syncwarp();
+      if (lane == 0) ring.release(it);
+    }
+    if (__any_sync(0xffffffffu, *ring.abort)) break;
+  }
+  flush();
+  consumers_sync();
+  if (*ring.abort) return;
+  // fixed-order reduction over the warps, epilogue, store
+  const int ncols = (c1 - c0) * 32;
+  for (int e = threadIdx.x; e < M * ncols; e += kConsumers) {
+    const int m = e / ncols, col = e % ncols;
+    const int cl = col / 32, cc = col % 32;
+    float v[2] = {0.f, 0.f};
+    for (int h = 0; h < halves; ++h)
+#pragma unroll
+      for (int w = 0; w < kCWarps; ++w) v[h] += cell(cl, w, h, m)[cc];
+    const int n = c0 * 32 + col;
+    if (pair) {
+      op.y[static_cast<int64_t>(m) * op.N + n] = swiglu_pick(v[0], v[1], op.bias, n, op.N);
+    } else {
+      float a = v[0];
+      if (op.bias != nullptr) a += __half2float(__ldg(op.bias + n));
+      op.y[static_cast<int64_t>(m) * op.N + n] = __float2half_rn(a);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------ attention
+// RoPE of 4 consecutive dims and their partners half a head away with the reference's fp16 rounding
+// per op (kernels/e2e/model.py:212-214: x * cos + cat(-x2, x1) * sin).
+__device__ __forceinline__ void rope_quad(const __half* src, const __half* cosr, const __half* sinr, int d,
+                                          __half* dst) {
+  const uint2 lo = __ldcg(reinterpret_cast<const uint2*>(src + d));
+  const uint2 hi = __ldcg(reinterpret_cast<const uint2*>(src + d + kHd / 2));
+  const uint2 cl = __ldg(reinterpret_cast<const uint2*>(cosr + d)), ch = __ldg(reinterpret_cast<const uint2*>(cosr + d + kHd / 2));
+  const uint2 sl = __ldg(reinterpret_cast<const uint2*>(sinr + d)), sh = __ldg(reinterpret_cast<const uint2*>(sinr + d + kHd / 2));
+  const __half* xl = reinterpret_cast<const __half*>(&lo);
+  const __half* xh = reinterpret_cast<const __half*>(&hi);
+  const __half* c_l = reinterpret_cast<const __half*>(&cl);
+  const __half* c_h = reinterpret_cast<const __half*>(&ch);
+  const __half* s_l = reinterpret_cast<const __half*>(&sl);
+  const __half* s_h = reinterpret_cast<const __half*>(&sh);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    dst[d + i] = __hadd_rn(__hmul_rn(xl[i], c_l[i]), __hmul_rn(__hneg(xh[i]), s_l[i]));
+    dst[d + kHd / 2 + i] = __hadd_rn(__hmul_rn(xh[i], c_h[i]), __hmul_rn(xl[i], s_h[i]));
+  }
+}
+
+// Row r (0..15), dims d..d+7 of a 16-row x 128-dim cache block in a ring slot: two TMA boxes of 16 rows
+// x 64 dims with the 128-byte swizzle (16-byte chunk index XOR row % 8).
+__device__ __forceinline__ uint32_t kv_at(uint32_t slot, int r, int d) {
+  const int seg = d >> 6, c16 = (d & 63) >> 3;
+  return slot + seg * 2048 + r * 128 + (((c16 ^ r) & 7) << 4);
+}
+
+struct AttnSmem {
+  __half q[kMaxGroup][kHd + 8];
+  __half knew[kHd];
+  __half vnew[kHd];
+  __half vzero[8];
+  int last;
+};
+
+// One attention item: sequence b, kv head h, positions [s * 128, s * 128 + 128) cut at pos. Warp w
+// runs flash decoding on block w (16 positions: K slot base + 2w, V slot base + 2w + 1): q.K^T on
+// tensor cores (heads as MMA rows), softmax, P.V with P rounded to fp16 (as flash-style SDPA does on
+// fp16 inputs). The 8 warps' (max, sum, output) are combined in shared memory into one partial per
+// head; the last item of (b, h) to arrive combines every slice into the attention output.
+__device__ void run_attention_item(const Params& p, const Op& op, Ring& ring, AttnSmem& as, int base, int item,
+                                   int pos, int S) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  const int g = lane >> 2, t = lane & 3;
+  const int G = p.nq / p.nkv;
+  const int s = item % S, bh = item / S;
+  const int h = bh % p.nkv, b = bh / p.nkv;
+  const int width = (p.nq + 2 * p.nkv) * kHd;
+  const __half* qrow = op.x + static_cast<int64_t>(b) * width;
+  const __half* cosr = p.rope_cos + static_cast<int64_t>(pos) * kHd;
+  const __half* sinr = p.rope_sin + static_cast<int64_t>(pos) * kHd;
+  const bool owner = pos / kAttnPos == s;  // this slice holds position pos: append k, v
+  const int64_t row_pos = static_cast<int64_t>(op.cache_row0) + (static_cast<int64_t>(b) * p.nkv + h) * p.max_len + pos;
+
+  // ---- prologue: RoPE of this kv head's q heads and k; v as is
+  constexpr int kQuads = kHd / 8;
+  for (int e = tid; e < (G + 1) * kQuads + kHd / 8; e += kConsumers) {
+    if (e < (G + 1) * kQuads) {
+      const int hh = e / kQuads, d = 4 * (e % kQuads);
+      const __half* src = hh < G ? qrow + (h * G + hh) * kHd : qrow + (p.nq + h) * kHd;
+      __half* dst = hh < G ? &as.q[hh][0] : as.knew;
+      rope_quad(src, cosr, sinr, d, dst);
+      if (hh == G && owner) {
+        *reinterpret_cast<uint2*>(p.k_cache + row_pos * kHd + d) = *reinterpret_cast<const uint2*>(as.knew + d);
+        *reinterpret_cast<uint2*>(p.k_cache + row_pos * kHd + d + kHd / 2) =
+            *reinterpret_cast<const uint2*>(as.knew + d + kHd / 2);
+      }
+    } else {
+      const int v8 = 8 * (e - (G + 1) * kQuads);
+      const uint4 v = __ldcg(reinterpret_cast<const uint4*>(qrow + (p.nq + p.nkv + h) * kHd + v8));
+      *reinterpret_cast<uint4*>(as.vnew + v8) = v;
+      if (owner) *reinterpret_cast<uint4*>(p.v_cache + row_pos * kHd + v8) = v;
+    }
+  }
+  if (tid < 8) as.vzero[tid] = __float2half(0.f);
+  consumers_sync();
+
+  // ---- this warp's 16-position block
+  const int p0 = s * kAttnPos + 16 * warp;
+  float o[kHd / 8][4];
+#pragma unroll
+  for (int j = 0; j < kHd / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;
+  const int itk = base + 2 * warp, itv = itk + 1;
+  bool ok = ring.warp_wait(itk);
+  ok = ok && ring.warp_wait(itv);
+  if (ok && p0 <= pos) {
+    const uint32_t kt = smem_addr(ring.s.w) + (itk % ring.nslots) * kSlotW;
+    const uint32_t vt = smem_addr(ring.s.w) + (itv % ring.nslots) * kSlotW;
+    uint32_t qa[kHd / 16][2];
+#pragma unroll
+    for (int ks = 0; ks < kHd / 16; ++ks) {
+      qa[ks][0] = g < G ? *reinterpret_cast<const uint32_t*>(&as.q[g][16 * ks + 2 * t]) : 0u;
+      qa[ks][1] = g < G ? *reinterpret_cast<const uint32_t*>(&as.q[g][16 * ks + 8 + 2 * t]) : 0u;
+    }
+    const int mi = lane >> 3, rr = lane & 7;
+    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    const int krow = 8 * (mi >> 1) + rr;
+    const bool k_new = p0 + krow == pos;
+#pragma unroll
+    for (int ks = 0; ks < kHd / 16; ++ks) {
+      const int d0 = 16 * ks + 8 * (mi & 1);
+      uint32_t kb[4];
+      const uint32_t a = k_new ? smem_addr(as.knew + d0) : kv_at(kt, krow, d0);
+      asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(kb[0]), "=r"(kb[1]), "=r"(kb[2]), "=r"(kb[3])
+                   : "r"(a));
+      mma_16816(sc[0], qa[ks][0], 0u, qa[ks][1], 0u, kb[0], kb[1]);
+      mma_16816(sc[1], qa[ks][0], 0u, qa[ks][1], 0u, kb[2], kb[3]);
+    }
+    float bm = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float v = p0 + 8 * nt + 2 * t + e <= pos ? sc[nt][e] * p.attn_scale : -INFINITY;
+        sc[nt][e] = v;
+        bm = fmaxf(bm, v);
+      }
+    bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 1));
+    bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 2));
+    m_run = bm;  // finite: position p0 <= pos is inside the block
+    float pr[2][2];
+    float ls = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        pr[nt][e] = __expf(sc[nt][e] - m_run);
+        ls += pr[nt][e];
+      }
+    ls += __shfl_xor_sync(0xffffffffu, ls, 1);
+    ls += __shfl_xor_sync(0xffffffffu, ls, 2);
+    l_run = ls;
+    const uint32_t a0 = half2_bits(__float2half_rn(pr[0][0]), __float2half_rn(pr[0][1]));
+    const uint32_t a2 = half2_bits(__float2half_rn(pr[1][0]), __float2half_rn(pr[1][1]));
+    const int vrow = (mi & 1) * 8 + rr;
+    const int vpos = p0 + vrow;
+#pragma unroll
+    for (int dp = 0; dp < kHd / 16; ++dp) {
+      const int d0 = 16 * dp + (mi >> 1) * 8;
+      const uint32_t a = vpos > pos ? smem_addr(as.vzero) : vpos == pos ? smem_addr(as.vnew + d0) : kv_at(vt, vrow, d0);
+      uint32_t vb[4];
+      asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(vb[0]), "=r"(vb[1]), "=r"(vb[2]), "=r"(vb[3])
+                   : "r"(a));
+      mma_16816(o[2 * dp], a0, 0u, a2, 0u, vb[0], vb[1]);
+      mma_16816(o[2 * dp + 1], a0, 0u, a2, 0u, vb[2], vb[3]);
+    }
+  }
+  __syncwarp();
+  if (lane == 0 && ok) {
+    ring.release(itk);
+    ring.release(itv);
+  }
+  // ---- combine the 8 warps' partials of every head in shared memory: red[w][head][2 + hd]
+  float* red = ring.s.red;
+  if (g < G) {
+    float* mine = red + (warp * kMaxGroup + g) * kPartFloats;
+    if (t == 0) {
+      mine[0] = m_run;
+      mine[1] = l_run;
+    }
+#pragma unroll
+    for (int j = 0; j < kHd / 8; ++j) {
+      mine[2 + 8 * j + 2 * t] = o[j][0];
+      mine[2 + 8 * j + 2 * t + 1] = o[j][1];
+    }
+  }
+  consumers_sync();
+  float* part = p.attn_part + (static_cast<int64_t>(bh) * (p.max_len / kAttnPos) + s) * kMaxGroup * kPartFloats;
+  for (int e = tid; e < G * (kHd + 2); e += kConsumers) {
+    const int hh = e / (kHd + 2), k = e % (kHd + 2);
+    float mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kCWarps; ++w) {
+      const float* src = red + (w * kMaxGroup + hh) * kPartFloats;
+      if (src[1] > 0.f) mx = fmaxf(mx, src[0]);
+    }
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < kCWarps; ++w) {
+      const float* src = red + (w * kMaxGroup + hh) * kPartFloats;
+      if (src[1] > 0.f) {
+        const float wt = __expf(src[0] - mx);
+        acc = fmaf(wt, k == 1 ? src[1] : src[k], acc);
+      }
+    }
+    part[hh * kPartFloats + k] = k == 0 ? mx : acc;
+  }
+  consumers_sync();
+  // ---- the last slice of (b, h) to arrive combines all slices
+  if (tid == 0) {
+    __threadfence();
+    const unsigned prev = atomicAdd(p.attn_count + bh, 1u);
+    as.last = prev == static_cast<unsigned>(S - 1);
+    if (as.last) {
+      p.attn_count[bh] = 0;
+      __threadfence();
+    }
+  }
+  consumers_sync();
+  if (!as.last) return;
+  const float* parts = p.attn_part + static_cast<int64_t>(bh) * (p.max_len / kAttnPos) * kMaxGroup * kPartFloats;
+  for (int e = tid; e < G * kHd; e += kConsumers) {
+    const int hh = e / kHd, d = e % kHd;
+    float mx = -INFINITY;
+    for (int q = 0; q < S; ++q) {
+      const float* src = parts + (q * kMaxGroup + hh) * kPartFloats;
+      if (__ldcg(src + 1) > 0.f) mx = fmaxf(mx, __ldcg(src));
+    }
+    float num = 0.f, den = 0.f;
+    for (int q = 0; q < S; ++q) {
+      const float* src = parts + (q * kMaxGroup + hh) * kPartFloats;
+      const float l = __ldcg(src + 1);
+      if (l > 0.f) {
+        const float wt = __expf(__ldcg(src) - mx);
+        den = fmaf(wt, l, den);
+        num = fmaf(wt, __ldcg(src + 2 + d), num);
+      }
+    }
+    p.attn_out[static_cast<int64_t>(b) * p.nq * kHd + (h * G + hh) * kHd + d] = __float2half_rn(num / den);
+  }
+}
+
+// ------------------------------------------------------------------------------ lm_head + argmax
+// Stage the final hidden rows (residual add + final RMSNorm) in natural order for the fp16 head.
+__device__ void stage_head_input(const Params& p, const Op& op, const Smem& s, float* inv_s,
+                                 float (*part)[kCWarps]) {
+  const int tid = threadIdx.x;
+  const int K = op.K, nblk = K / 8;
+  for (int m = 0; m < p.M; ++m) {
+    float acc = 0.f;
+    for (int v = tid; v < nblk; v += kConsumers) {
+      uint4 a = __ldcg(reinterpret_cast<const uint4*>(op.x + static_cast<int64_t>(m) * K) + v);
+      const uint4 r = __ldcg(reinterpret_cast<const uint4*>(op.res_in + static_cast<int64_t>(m) * K) + v);
+      __half2* ah = reinterpret_cast<__half2*>(&a);
+      const __half2* rh = reinterpret_cast<const __half2*>(&r);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        ah[j] = __hadd2_rn(ah[j], rh[j]);
+        const float2 f = __half22float2(ah[j]);
+        acc = fmaf(f.x, f.x, acc);
+        acc = fmaf(f.y, f.y, acc);
+      }
+      *reinterpret_cast<uint4*>(s.xs + m * p.xs_pitch + v * 16) = a;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if ((tid & 31) == 0) part[m][tid >> 5] = acc;
+  }
+  consumers_sync();
+  if (tid < p.M) {
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < kCWarps; ++w) tot += part[tid][w];
+    inv_s[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(K)), p.eps)));
+  }
+  consumers_sync();
+  for (int e = tid; e < p.M * nblk; e += kConsumers) {
+    const int m = e / nblk, v = e % nblk;
+    uint4 a = *reinterpret_cast<const uint4*>(s.xs + m * p.xs_pitch + v * 16);
+    const uint4 wv = __ldg(reinterpret_cast<const uint4*>(op.norm_w) + v);
+    __half2* ah = reinterpret_cast<__half2*>(&a);
+    const __half2* wh = reinterpret_cast<const __half2*>(&wv);
+    const float sc = inv_s[m];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __half22float2(ah[j]);
+      ah[j] = __hmul2_rn(wh[j], __floats2half2_rn(__fmul_rn(f.x, sc), __fmul_rn(f.y, sc)));
+    }
+    *reinterpret_cast<uint4*>(s.xs + m * p.xs_pitch + v * 16) = a;
+  }
+  consumers_sync();
+}
+
+__device__ __forceinline__ void better(float& bv, int& bi, float v, int i) {
+  if (v > bv || (v == bv && i < bi)) {
+    bv = v;
+    bi = i;
+  }
+}
+
+// The fp16 lm_head over this CTA's vocab chunks [c0, c1) (32 rows each) with the greedy argmax.
+// Warp w takes chunks c0 + 8r + w (round r) whole: K in 64-wide ring slots (TMA box of 32 rows x 64
+// halves, 128-byte swizzle), A operand by ldmatrix, the staged rows as B; slot of (round r, stage k,
+// warp w) = base_r + k * (chunks in round r) + w. Logits are rounded to fp16 like F.linear's output
+// and compared in that precision; ties go to the lower index (torch.argmax's first maximum).
+__device__ void run_head(const Params& p, const Op& op, Ring& ring, int base, int c0, int c1, float* best_v,
+                         int* best_i) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int M = p.M;
+  const int nch = c1 - c0;
+  const uint32_t w_base = smem_addr(ring.s.w);
+  float bv[2] = {-INFINITY, -INFINITY};
+  int bi[2] = {0x7fffffff, 0x7fffffff};
+  const int mi = lane >> 3, rr = lane & 7;
+  int rbase = base;
+  for (int r = 0; 8 * r < nch; ++r) {
+    const int nr = min(8, nch - 8 * r);
+    if (warp < nr) {
+      float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      for (int k = 0; k < op.stages; ++k) {
+        const int it = rbase + k * nr + warp;
+        if (!ring.warp_wait(it)) break;
+        const uint32_t slot = w_base + (it % ring.nslots) * kSlotW;
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          const int kk = k * 64 + ks * 16;
+          uint32_t b0 = 0, b1 = 0;
+          if (g < M) {
+            b0 = *reinterpret_cast<const uint32_t*>(ring.s.xs + g * p.xs_pitch + (kk + 2 * t) * 2);
+            b1 = *reinterpret_cast<const uint32_t*>(ring.s.xs + g * p.xs_pitch + (kk + 8 + 2 * t) * 2);
+          }
+#pragma unroll
+          for (int tile = 0; tile < 2; ++tile) {
+            const int row = tile * 16 + (mi & 1) * 8 + rr;
+            const int c16 = 2 * ks + (mi >> 1);
+            const uint32_t a = slot + row * 128 + (((c16 ^ row) & 7) << 4);
+            uint32_t af[4];
+            asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                         : "=r"(af[0]), "=r"(af[1]), "=r"(af[2]), "=r"(af[3])
+                         : "r"(a));
+            mma_16816(acc[tile], af[0], af[1], af[2], af[3], b0, b1);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) ring.release(it);
+      }
+      // epilogue: rows tile*16 + g (+8) of chunk c, batch rows 2t, 2t + 1
+      const int c = c0 + 8 * r + warp;
+#pragma unroll
+      for (int tile = 0; tile < 2; ++tile)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int m = 2 * t + (e & 1);
+          const int vrow = c * 32 + tile * 16 + g + (e >> 1) * 8;
+          if (m < M && vrow < p.vocab) {
+            const __half lg = __float2half_rn(acc[tile][e]);
+            if (p.logits != nullptr) p.logits[static_cast<int64_t>(m) * p.vocab + vrow] = lg;
+            better(bv[e & 1], bi[e & 1], __half2float(lg), vrow);
+          }
+        }
+    }
+    rbase += nr * op.stages;
+    if (__any_sync(0xffffffffu, *ring.abort)) break;
+  }
+  // best over the warp's lanes with the same t (same batch rows), then over warps in shared memory
+#pragma unroll
+  for (int e = 0; e < 2; ++e)
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv[e], off);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi[e], off);
+      better(bv[e], bi[e], ov, oi);
+    }
+  if (g == 0) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int m = 2 * t + e;
+      if (m < kMaxRows) {
+        best_v[warp * kMaxRows + m] = bv[e];
+        best_i[warp * kMaxRows + m] = bi[e];
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------ the kernel
+__global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_constant__ Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+  const SmemLayout L = smem_layout(p.nslots, p.M, p.xs_pitch, p.kmax, p.red_bytes);
+  Smem s;
+  s.w = base + L.w;
+  s.sz = base + L.sz;
+  s.xs = base + L.xs;
+  s.cx = reinterpret_cast<float*>(base + L.cx);
+  s.red = reinterpret_cast<float*>(base + L.red);
+  s.full = reinterpret_cast<uint64_t*>(base + L.bars);
+  s.empty = s.full + p.nslots;
+
+  __shared__ int s_issued, s_abort, s_pos;
+  __shared__ float s_inv[kMaxRows];
+  __shared__ float s_part[kMaxRows][kCWarps];
+  __shared__ float s_best_v[kCWarps * kMaxRows];
+  __shared__ int s_best_i[kCWarps * kMaxRows];
+  __shared__ int s_head_last, s_stop;
+  __shared__ __align__(16) AttnSmem as;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int cta = blockIdx.x, G = gridDim.x;
+  if (tid == 0) {
+    for (int i = 0; i < p.nslots; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    fence_mbar_init();
+    s_issued = 0;
+    s_abort = 0;
+    int64_t pos = *reinterpret_cast<volatile const int64_t*>(p.pos);
+    if (pos < 0 || pos >= p.max_len) {
+      record_device_error(p.err, DK_DEVERR_BAD_POSITION);
+      pos = -1;
+    }
+    s_pos = static_cast<int>(pos);
+  }
+  __syncthreads();
+  const int pos = s_pos;
+  volatile int* abort = &s_abort;
+  if (pos < 0) *abort = 1;  // every CTA decides the same: nothing is written, counters still move
+
+  if (warp == kCWarps) {
+    // ================================================================ producer warp
+    if (lane == 0) {
+      int it = 0;
+      bool live = pos >= 0;
+      for (int j = 0; j < p.n_ops && live; ++j) {
+        const Op& op = p.ops[j];
+        const int n = op_slots(op, cta, G, p.M, p.nkv, pos);
+        if (n == 0) continue;
+        auto acquire = [&](int bytes) -> int {  // arm slot `it` for `bytes`; -1 on give-up
+          const int slot = it % p.nslots;
+          if (it >= p.nslots) {
+            const uint32_t par = ((it / p.nslots) - 1) & 1;
+            const uint64_t t0 = globaltimer_ns();
+            while (!mbar_try_wait(&s.empty[slot], par)) {
+              if (*abort) return -1;
+              if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                record_device_error(p.err, DK_DEVERR_STEP_WAIT);
+                *abort = 1;
+                return -1;
+              }
+            }
+          }
+          mbar_arrive_expect_tx(&s.full[slot], static_cast<uint32_t>(bytes));
+          return slot;
+        };
+        auto publish = [&]() {
+          ++it;
+          __threadfence_block();
+          *reinterpret_cast<volatile int*>(&s_issued) = it;
+        };
+        if (op.kind == OP_ATTN) {
+          const int S = attn_splits(pos);
+          const int items = p.M * p.nkv * S;
+          const int jj = (cta - op.cta0 + G) % G;
+          for (int item = jj; item < items && live; item += G) {
+            const int sidx = item % S, bh = item / S;
+            const int hh = bh % p.nkv, b = bh / p.nkv;
+            const int row0 = op.cache_row0 + (b * p.nkv + hh) * p.max_len + sidx * kAttnPos;
+            for (int blk = 0; blk < 8 && live; ++blk) {
+              const bool any = sidx * kAttnPos + 16 * blk <= pos;
+              for (int kv = 0; kv < 2; ++kv) {
+                const int slot = acquire(any ? kSlotW : 0);
+                if (slot < 0) {
+                  live = false;
+                  break;
+                }
+                if (any) {
+                  const CUtensorMap* m = &p.maps[kv == 0 ? p.kmap : p.vmap];
+                  uint8_t* dst = s.w + slot * kSlotW;
+                  tma_load_2d(dst, m, 0, row0 + 16 * blk, &s.full[slot]);
+                  tma_load_2d(dst + 2048, m, 64, row0 + 16 * blk, &s.full[slot]);
+                }
+                publish();
+              }
+            }
+          }
+          continue;
+        }
+        const int jj = participant(cta, op.cta0, op.ncta, G);
+        const int c0 = static_cast<int>(static_cast<int64_t>(jj) * op.units / op.ncta);
+        const int c1 = static_cast<int>(static_cast<int64_t>(jj + 1) * op.units / op.ncta);
+        if (op.kind == OP_HEAD) {
+          const CUtensorMap* m = &p.maps[op.map];
+          const int nch = c1 - c0;
+          for (int r = 0; 8 * r < nch && live; ++r) {
+            const int nr = min(8, nch - 8 * r);
+            for (int k = 0; k < op.stages && live; ++k)
+              for (int w = 0; w < nr; ++w) {
+                const int slot = acquire(kSlotW);
+                if (slot < 0) {
+                  live = false;
+                  break;
+                }
+                tma_load_2d(s.w + slot * kSlotW, m, k * 64, (c0 + 8 * r + w) * 32, &s.full[slot]);
+                publish();
+              }
+          }
+          continue;
+        }
+        const CUtensorMap* mq = &p.maps[op.map];
+        const CUtensorMap* ms = mq + 1;
+        const CUtensorMap* mz = mq + 2;
+        const int halves = op.kind == OP_GATEUP ? 2 : 1;
+        const int nunits = (c1 - c0) * op.stages;
+        for (int u = 0; u < nunits && live; ++u) {
+          const int c = c0 + u / op.stages, st = u % op.stages;
+          for (int h = 0; h < halves; ++h) {
+            const int slot = acquire(kSlotW + kSlotSZ);
+            if (slot < 0) {
+              live = false;
+              break;
+            }
+            const int col = c * 32 + h * op.N;
+            tma_load_2d(s.w + slot * kSlotW, mq, col, st * 32, &s.full[slot]);
+            tma_load_2d(s.sz + slot * kSlotSZ, ms, col, st * 2, &s.full[slot]);
+            tma_load_2d(s.sz + slot * kSlotSZ + 128, mz, col, st * 2, &s.full[slot]);
+            publish();
+          }
+        }
+      }
+      // copies still in flight must land before the shared memory goes away (only after a give-up:
+      // otherwise every armed slot was consumed)
+      if (*abort) {
+        const uint64_t t0 = globaltimer_ns();
+        for (int i = max(0, it - p.nslots); i < it; ++i)
+          while (!mbar_try_wait(&s.full[i % p.nslots], (i / p.nslots) & 1) && globaltimer_ns() - t0 < 500000000ull) {
+          }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ================================================================ consumer warps
+    Ring ring;
+    ring.s = s;
+    ring.nslots = p.nslots;
+    ring.issued = &s_issued;
+    ring.abort = abort;
+    ring.err = p.err;
+    ring.seen = 0;
+    int base_it = 0;
+    for (int j = 0; j < p.n_ops; ++j) {
+      const Op& op = p.ops[j];
+      const int nslots_op = pos >= 0 ? op_slots(op, cta, G, p.M, p.nkv, pos) : 0;
+      const bool part = op.kind == OP_ATTN ? nslots_op > 0 : participant(cta, op.cta0, op.ncta, G) >= 0;
+      if (!part) continue;
+      // the input of op j is complete once every participant of op j - 1 arrived
+      if (j > 0 && tid == 0 && !*abort) {
+        const unsigned target = static_cast<unsigned>(op_participants(p.ops[j - 1], G, p.M, p.nkv, pos));
+        const uint64_t t0 = globaltimer_ns();
+        while (ld_acquire(p.done + (j - 1)) < target) {
+          if (*abort) break;
+          if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            record_device_error(p.err, DK_DEVERR_STEP_WAIT);
+            *abort = 1;
+            break;
+          }
+        }
+      }
+      if (tid == 0) s_stop = *abort;
+      consumers_sync();
+      if (!s_stop) {  // one decision for the whole CTA: the branches below hold barriers
+        if (op.kind == OP_ATTN) {
+          const int S = attn_splits(pos);
+          const int items = p.M * p.nkv * S;
+          int b = base_it;
+          for (int item = (cta - op.cta0 + G) % G; item < items; item += G) {
+            run_attention_item(p, op, ring, as, b, item, pos, S);
+            b += 16;
+            if (tid == 0) s_stop = *abort;
+            consumers_sync();
+            if (s_stop) break;
+          }
+        } else {
+          const int jj = participant(cta, op.cta0, op.ncta, G);
+          const int c0 = static_cast<int>(static_cast<int64_t>(jj) * op.units / op.ncta);
+          const int c1 = static_cast<int>(static_cast<int64_t>(jj + 1) * op.units / op.ncta);
+          if (op.kind == OP_HEAD) {
+            stage_head_input(p, op, s, s_inv, s_part);
+            run_head(p, op, ring, base_it, c0, c1, s_best_v, s_best_i);
+            consumers_sync();
+            if (tid < p.M) {  // this CTA's best per row, then the grid's by the last to arrive
+              float bv = -INFINITY;
+              int bi = 0x7fffffff;
+              for (int w = 0; w < kCWarps; ++w) better(bv, bi, s_best_v[w * kMaxRows + tid], s_best_i[w * kMaxRows + tid]);
+              p.head_val[cta * kMaxRows + tid] = bv;
+              p.head_idx[cta * kMaxRows + tid] = bi;
+            }
+            consumers_sync();
+            if (tid == 0) {
+              __threadfence();
+              const unsigned prev = atomicAdd(p.head_count, 1u);
+              s_head_last = prev == static_cast<unsigned>(op.ncta - 1);
+              if (s_head_last) {
+                *p.head_count = 0;
+                __threadfence();
+              }
+            }
+            consumers_sync();
+            if (s_head_last && tid < p.M) {
+              float bv = -INFINITY;
+              int bi = 0x7fffffff;
+              for (int q = 0; q < G; ++q) {
+                if (participant(q, op.cta0, op.ncta, G) < 0) continue;
+                better(bv, bi, __ldcg(p.head_val + q * kMaxRows + tid), __ldcg(p.head_idx + q * kMaxRows + tid));
+              }
+              p.tok[tid] = bi;
+              if (p.hist != nullptr) p.hist[tid * p.hist_ld + pos] = bi;
+            }
+            consumers_sync();
+            if (s_head_last && tid == 0) *p.pos = pos + 1;
+          } else {
+            stage_int4_input(p, op, s, jj == 0, s_inv, s_part);
+            run_int4(p, op, ring, base_it, c0, c1);
+          }
+        }
+      }
+      consumers_sync();
+      if (tid == 0) {
+        __threadfence();
+        atomicAdd(p.done + j, 1u);
+      }
+      base_it += nslots_op;
+    }
+  }
+
+  // ---------------------------------------------------------------- exit: the last CTA resets the counters
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    const unsigned prev = atomicAdd(p.exit_count, 1u);
+    if (prev == static_cast<unsigned>(G - 1)) {
+      for (int j = 0; j < p.n_ops; ++j) p.done[j] = 0;
+      for (int i = 0; i < p.M * p.nkv; ++i) p.attn_count[i] = 0;
+      *p.head_count = 0;
+      *p.exit_count = 0;
+      __threadfence();
+    }
+  }
+}
+
+}  // namespace step
+}  // namespace dk
+
+// ================================================================================== host side
+using namespace dk;
+using namespace dk::step;
+
+struct dk_step_plan {
+  Params params;
+  int grid;
+  size_t smem;
+  int device;
+};
+
+namespace {
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Offsets of the pieces of a step workspace (all from its 256-byte aligned start).
+struct Workspace {
+  size_t counters, ops, maps, attn_out, qkv, o, act, down, res0, res1, attn_part, head_val, head_idx, total;
+  int n_ops, n_maps, max_splits;
+};
+
+Workspace workspace_layout(const dk_step_model* m, int grid) {
+  Workspace w;
+  const int L = m->n_layers;
+  w.n_ops = 5 * L + 1;
+  w.n_maps = 12 * L + 1 + 2;
+  w.max_splits = m->max_len / kAttnPos;
+  const int64_t M = m->batch, H = m->hidden, nqkv = (m->n_heads + 2 * m->n_kv) * m->head_dim;
+  size_t off = 0;
+  w.counters = off;
+  off = align_up(off + 4 * (w.n_ops + 4 + M * m->n_kv), 256);
+  w.ops = off;
+  off = align_up(off + sizeof(Op) * w.n_ops, 256);
+  w.maps = off;
+  off = align_up(off + sizeof(CUtensorMap) * w.n_maps, 256);
+  w.attn_out = off;
+  off = align_up(off + 2 * M * m->n_heads * m->head_dim, 256);
+  w.qkv = off;
+  off = align_up(off + 2 * M * nqkv, 256);
+  w.o = off;
+  off = align_up(off + 2 * M * H, 256);
+  w.act = off;
+  off = align_up(off + 2 * M * m->intermediate, 256);
+  w.down = off;
+  off = align_up(off + 2 * M * H, 256);
+  w.res0 = off;
+  off = align_up(off + 2 * M * H, 256);
+  w.res1 = off;
+  off = align_up(off + 2 * M * H, 256);
+  w.attn_part = off;
+  off = align_up(off + 4 * static_cast<size_t>(M) * m->n_kv * w.max_splits * kMaxGroup * kPartFloats, 256);
+  w.head_val = off;
+  off = align_up(off + 4 * static_cast<size_t>(grid) * kMaxRows, 256);
+  w.head_idx = off;
+  off = align_up(off + 4 * static_cast<size_t>(grid) * kMaxRows, 256);
+  w.total = off;
+  return w;
+}
+
+int check_model(const dk_step_model* m) {
+  if (m == nullptr || m->layers == nullptr) return set_error(DK_ERR_INVALID, "step: model description is NULL");
+  if (m->n_layers <= 0 || m->batch <= 0 || m->hidden <= 0 || m->vocab <= 0 || m->max_len <= 0)
+    return set_error(DK_ERR_INVALID, "step: sizes must be positive");
+  if (m->batch > kMaxRows) return set_error(DK_ERR_UNSUPPORTED, "step: batch %d (at most %d rows)", m->batch, kMaxRows);
+  if (m->head_dim != kHd) return set_error(DK_ERR_UNSUPPORTED, "step: head_dim %d (128 only)", m->head_dim);
+  if (m->n_kv <= 0 || m->n_heads % m->n_kv != 0 || m->n_heads / m->n_kv > kMaxGroup)
+    return set_error(DK_ERR_UNSUPPORTED, "step: %d query heads over %d kv heads", m->n_heads, m->n_kv);
+  if (m->hidden % 256 || m->intermediate % 256 || (m->n_heads * kHd) % 256)
+    return set_error(DK_ERR_UNSUPPORTED, "step: hidden, intermediate and n_heads * head_dim must be multiples of 256");
+  if (m->vocab % 32 || m->max_len % kAttnPos)
+    return set_error(DK_ERR_UNSUPPORTED, "step: vocab %% 32 == 0 and max_len %% 128 == 0 needed");
+  if (static_cast<int64_t>(m->n_layers) * m->batch * m->n_kv * m->max_len >= (int64_t(1) << 31))
+    return set_error(DK_ERR_INVALID, "step: the KV cache has too many rows");
+  const void* ptrs[] = {m->embed, m->final_norm, m->lm_head, m->rope_cos, m->rope_sin, m->k_cache, m->v_cache};
+  for (const void* q : ptrs)
+    if (q == nullptr || !aligned16(q)) return set_error(DK_ERR_ALIGN, "step: model tensors must be non-NULL and 16-byte aligned");
+  for (int l = 0; l < m->n_layers; ++l) {
+    const dk_step_layer& y = m->layers[l];
+    const void* lp[] = {y.input_norm, y.post_norm, y.qkv_qweight, y.qkv_scales, y.qkv_zeros, y.o_qweight, y.o_scales,
+                        y.o_zeros, y.gate_up_qweight, y.gate_up_scales, y.gate_up_zeros, y.down_qweight,
+                        y.down_scales, y.down_zeros};
+    for (const void* q : lp)
+      if (q == nullptr || !aligned16(q))
+        return set_error(DK_ERR_ALIGN, "step: layer %d: weights must be non-NULL and 16-byte aligned", l);
+  }
+  return DK_OK;
+}
+
+// Shared memory: ring slots as many as fit next to the staged input, the {C, X} table and the
+// reduction scratch.
+bool plan_smem(const dk_step_model* m, int* nslots, int* xs_pitch, int* red_bytes, size_t* smem) {
+  const int kmax = std::max(std::max(m->hidden, m->intermediate), m->n_heads * kHd);
+  *xs_pitch = kmax * 2 + kXsPad;
+  const int red_int4 = kMaxChunks * kCWarps * 2 * kMaxRows * 32 * 4;
+  const int red_attn = kCWarps * kMaxGroup * kPartFloats * 4;
+  *red_bytes = std::max(red_int4, red_attn);
+  cudaFuncAttributes fa;
+  if (cudaFuncGetAttributes(&fa, decode_step_kernel) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  const int limit = device_info().max_smem_optin - static_cast<int>(fa.sharedSizeBytes);
+  int n = 64;
+  while (n >= 16 && static_cast<int>(smem_layout(n, m->batch, *xs_pitch, kmax, *red_bytes).total) + 1024 > limit) --n;
+  if (n < 16) return false;
+  *nslots = n;
+  *smem = smem_layout(n, m->batch, *xs_pitch, kmax, *red_bytes).total + 1024;
+  return true;
+}
+
+}  // namespace
+
+extern "C" int dk_step_workspace_bytes(const dk_step_model* m, uint64_t* bytes) {
+  int rc = check_model(m);
+  if (rc != DK_OK) return rc;
+  if (bytes == nullptr) return set_error(DK_ERR_INVALID, "step: bytes is NULL");
+  *bytes = workspace_layout(m, device_info().num_sms).total;
+  return DK_OK;
+}
+
+extern "C" int dk_step_create(const dk_step_model* m, void* workspace, uint64_t bytes, dk_step_plan** out) {
+  int rc = check_model(m);
+  if (rc != DK_OK) return rc;
+  if (out == nullptr || workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return set_error(DK_ERR_INVALID, "step: workspace must be non-NULL and 256-byte aligned");
+  const DeviceInfo& dev = device_info();
+  const int G = dev.num_sms;
+  const Workspace w = workspace_layout(m, G);
+  if (bytes < w.total) return set_error(DK_ERR_INVALID, "step: workspace of %llu bytes, %zu needed",
+                                        (unsigned long long)bytes, w.total);
+  int nslots = 0, xs_pitch = 0, red_bytes = 0;
+  size_t smem = 0;
+  if (!plan_smem(m, &nslots, &xs_pitch, &red_bytes, &smem))
+    return set_error(DK_ERR_UNSUPPORTED, "step: the staged rows leave no room for the weight ring");
+  const int kmax = std::max(std::max(m->hidden, m->intermediate), m->n_heads * kHd);
+
+  char* ws = static_cast<char*>(workspace);
+  const int L = m->n_layers, M = m->batch, H = m->hidden, I = m->intermediate;
+  const int nqkv = (m->n_heads + 2 * m->n_kv) * kHd, nqd = m->n_heads * kHd;
+  std::vector<CUtensorMap> maps(w.n_maps);
+  std::vector<Op> ops;
+  ops.reserve(w.n_ops);
+  auto int4_maps = [&](int idx, const int32_t* q, const void* sc, const void* z, int64_t N, int64_t K) {
+    return make_tensor_map_2d(&maps[idx], q, CU_TENSOR_MAP_DATA_TYPE_INT32, N, K / 8, N * 4, 32, 32,
+                              CU_TENSOR_MAP_SWIZZLE_128B) &&
+           make_tensor_map_2d(&maps[idx + 1], sc, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, N, K / 128, N * 2, 32, 2,
+                              CU_TENSOR_MAP_SWIZZLE_NONE) &&
+           make_tensor_map_2d(&maps[idx + 2], z, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, N, K / 128, N * 2, 32, 2,
+                              CU_TENSOR_MAP_SWIZZLE_NONE);
+  };
+  __half* attn_out = reinterpret_cast<__half*>(ws + w.attn_out);
+  __half* qkv = reinterpret_cast<__half*>(ws + w.qkv);
+  __half* o = reinterpret_cast<__half*>(ws + w.o);
+  __half* act = reinterpret_cast<__half*>(ws + w.act);
+  __half* down = reinterpret_cast<__half*>(ws + w.down);
+  __half* res[2] = {reinterpret_cast<__half*>(ws + w.res0), reinterpret_cast<__half*>(ws + w.res1)};
+  // Participants. An op spreads over as many CTAs as it has chunks (each CTA multiplies whole
+  // chunks: no cross-CTA split-K), starting where the previous op's participants ended, so the
+  // weights of consecutive ops are fetched by different SMs.
+  int next_cta = 0;
+  auto place = [&](Op& op) {
+    op.ncta = std::min(op.units, G);
+    op.cta0 = op.ncta == G ? 0 : next_cta % G;
+    next_cta = (op.cta0 + op.ncta) % G;
+  };
+  int map = 0;
+  int r_in = -1;  // residual buffer holding the current residual stream (-1: none yet)
+  for (int l = 0; l < L; ++l) {
+    const dk_step_layer& y = m->layers[l];
+    Op q = {};
+    q.kind = OP_QKV;
+    q.layer = l;
+    q.units = nqkv / 32;
+    q.stages = H / 256;
+    q.K = H;
+    q.N = nqkv;
+    q.map = map;
+    if (!int4_maps(map, y.qkv_qweight, y.qkv_scales, y.qkv_zeros, nqkv, H)) return DK_ERR_CUDA;
+    map += 3;
+    q.from_embed = l == 0;
+    q.x = l == 0 ? nullptr : down;
+    q.res_in = l == 0 ? nullptr : res[r_in];
+    q.res_out = res[l == 0 ? 0 : 1 - r_in];
+    q.norm_w = static_cast<const __half*>(y.input_norm);
+    q.bias = static_cast<const __half*>(y.qkv_bias);
+    q.y = qkv;
+    place(q);
+    ops.push_back(q);
+    r_in = l == 0 ? 0 : 1 - r_in;
+
+    Op a = {};
+    a.kind = OP_ATTN;
+    a.layer = l;
+    a.x = qkv;
+    a.y = attn_out;
+    a.cta0 = next_cta;
+    a.ncta = 0;
+    a.cache_row0 = l * M * m->n_kv * m->max_len;
+    ops.push_back(a);
+    next_cta = (next_cta + M * m->n_kv * 8) % G;
+
+    Op op = {};
+    op.kind = OP_O;
+    op.layer = l;
+    op.units = H / 32;
+    op.stages = nqd / 256;
+    op.K = nqd;
+    op.N = H;
+    op.map = map;
+    if (!int4_maps(map, y.o_qweight, y.o_scales, y.o_zeros, H, nqd)) return DK_ERR_CUDA;
+    map += 3;
+    op.x = attn_out;
+    op.bias = static_cast<const __half*>(y.o_bias);
+    op.y = o;
+    place(op);
+    ops.push_back(op);
+
+    Op gu = {};
+    gu.kind = OP_GATEUP;
+    gu.layer = l;
+    gu.units = I / 32;
+    gu.stages = H / 256;
+    gu.K = H;
+    gu.N = I;
+    gu.map = map;
+    if (!int4_maps(map, y.gate_up_qweight, y.gate_up_scales, y.gate_up_zeros, 2 * I, H)) return DK_ERR_CUDA;
+    map += 3;
+    gu.x = o;
+    gu.res_in = res[r_in];
+    gu.res_out = res[1 - r_in];
+    gu.norm_w = static_cast<const __half*>(y.post_norm);
+    gu.bias = static_cast<const __half*>(y.gate_up_bias);
+    gu.y = act;
+    place(gu);
+    ops.push_back(gu);
+    r_in = 1 - r_in;
+
+    Op dn = {};
+    dn.kind = OP_DOWN;
+    dn.layer = l;
+    dn.units = H / 32;
+    dn.stages = I / 256;
+    dn.K = I;
+    dn.N = H;
+    dn.map = map;
+    if (!int4_maps(map, y.down_qweight, y.down_scales, y.down_zeros, H, I)) return DK_ERR_CUDA;
+    map += 3;
+    dn.x = act;
+    dn.bias = static_cast<const __half*>(y.down_bias);
+    dn.y = down;
+    place(dn);
+    ops.push_back(dn);
+  }
+  Op hd = {};
+  hd.kind = OP_HEAD;
+  hd.layer = L;
+  hd.units = m->vocab / 32;
+  hd.stages = H / 64;
+  hd.K = H;
+  hd.N = m->vocab;
+  hd.map = map;
+  if (!make_tensor_map_2d(&maps[map], m->lm_head, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, H, m->vocab, H * 2, 64, 32,
+                          CU_TENSOR_MAP_SWIZZLE_128B))
+    return DK_ERR_CUDA;
+  map += 1;
+  hd.x = down;
+  hd.res_in = res[r_in];
+  hd.norm_w = static_cast<const __half*>(m->final_norm);
+  hd.y = nullptr;  // the logits pointer is per call (dk_step_run)
+  hd.ncta = G;
+  hd.cta0 = 0;
+  ops.push_back(hd);
+  for (const Op& op : ops)
+    if (op.kind != OP_ATTN && op.kind != OP_HEAD &&
+        (op.units + op.ncta - 1) / op.ncta > kMaxChunks)
+      return set_error(DK_ERR_UNSUPPORTED, "step: an op needs more than %d chunks per CTA", kMaxChunks);
+  const uint64_t rows = static_cast<uint64_t>(L) * M * m->n_kv * m->max_len;
+  const int kmap = map, vmap = map + 1;
+  if (!make_tensor_map_2d(&maps[kmap], m->k_cache, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, kHd, rows, kHd * 2, 64, 16,
+                          CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_tensor_map_2d(&maps[vmap], m->v_cache, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, kHd, rows, kHd * 2, 64, 16,
+                          CU_TENSOR_MAP_SWIZZLE_128B))
+    return DK_ERR_CUDA;
+
+  // set-up copies (synchronous: before any capture)
+  cudaError_t e = cudaMemset(ws + w.counters, 0, w.ops - w.counters);
+  if (e == cudaSuccess) e = cudaMemcpy(ws + w.ops, ops.data(), sizeof(Op) * ops.size(), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(ws + w.maps, maps.data(), sizeof(CUtensorMap) * maps.size(), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return set_error(DK_ERR_CUDA, "step: set-up copies: %s", cudaGetErrorString(e));
+
+  static std::mutex mu;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    const int limit = opt_in_dynamic_smem(decode_step_kernel);
+    if (limit < static_cast<int>(smem))
+      return set_error(DK_ERR_UNSUPPORTED, "step: %zu bytes of shared memory do not fit", smem);
+  }
+  int occ = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_step_kernel, kThreads, smem) != cudaSuccess || occ < 1) {
+    cudaGetLastError();
+    return set_error(DK_ERR_UNSUPPORTED, "step: the kernel does not fit on an SM");
+  }
+
+  dk_step_plan* plan = new dk_step_plan();
+  Params& p = plan->params;
+  p.ops = reinterpret_cast<const Op*>(ws + w.ops);
+  p.n_ops = static_cast<int>(ops.size());
+  p.maps = reinterpret_cast<const CUtensorMap*>(ws + w.maps);
+  p.kmap = kmap;
+  p.vmap = vmap;
+  p.M = M;
+  p.H = H;
+  p.nq = m->n_heads;
+  p.nkv = m->n_kv;
+  p.max_len = m->max_len;
+  p.vocab = m->vocab;
+  p.nslots = nslots;
+  p.kmax = kmax;
+  p.xs_pitch = xs_pitch;
+  p.red_bytes = red_bytes;
+  p.eps = m->eps;
+  p.attn_scale = 1.0f / sqrtf(static_cast<float>(kHd));
+  p.embed = static_cast<const __half*>(m->embed);
+  p.rope_cos = static_cast<const __half*>(m->rope_cos);
+  p.rope_sin = static_cast<const __half*>(m->rope_sin);
+  p.k_cache = static_cast<__half*>(m->k_cache);
+  p.v_cache = static_cast<__half*>(m->v_cache);
+  unsigned* ctr = reinterpret_cast<unsigned*>(ws + w.counters);
+  p.done = ctr;
+  p.exit_count = ctr + w.n_ops;
+  p.head_count = ctr + w.n_ops + 1;
+  p.attn_count = ctr + w.n_ops + 4;
+  p.attn_part = reinterpret_cast<float*>(ws + w.attn_part);
+  p.attn_out = attn_out;
+  p.head_val = reinterpret_cast<float*>(ws + w.head_val);
+  p.head_idx = reinterpret_cast<int*>(ws + w.head_idx);
+  p.err = dev.err_word;
+  plan->grid = G;
+  plan->smem = smem;
+  cudaGetDevice(&plan->device);
+  *out = plan;
+  return DK_OK;
+}
+
+extern "C" int dk_step_run(const dk_step_plan* plan, int64_t* tokens, int64_t* pos, int64_t* history,
+                           int64_t history_ld, void* logits, dk_stream_t stream) {
+  if (plan == nullptr || tokens == nullptr || pos == nullptr)
+    return set_error(DK_ERR_INVALID, "step_run: plan, tokens and pos must be non-NULL");
+  if (history != nullptr && history_ld < plan->params.max_len)
+    return set_error(DK_ERR_INVALID, "step_run: history rows need at least max_len entries");
+  Params p = plan->params;
+  p.tok = tokens;
+  p.pos = pos;
+  p.hist = history;
+  p.hist_ld = history_ld;
+  p.logits = static_cast<__half*>(logits);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(plan->grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = plan->smem;
+  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, decode_step_kernel, p);
+  if (e != cudaSuccess) return set_error(DK_ERR_CUDA, "step_run launch: %s", cudaGetErrorString(e));
+  return DK_OK;
+}
+
+extern "C" int dk_step_destroy(dk_step_plan* plan) {
+  delete plan;
+  return DK_OK;
+}

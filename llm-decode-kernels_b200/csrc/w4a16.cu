@@ -1034,9 +1034,10 @@ int run_fast(const void* x, int64_t ldx, const int32_t* qweight, const void* sca
     int mc = static_cast<int>(std::min<int64_t>(rows_per_launch, M - m0));
     Choice c = choose(mc, units, static_cast<int>(K), swiglu_i > 0, cfg);
     // The staged x grows with the rows: when a long K slice leaves no tile for mc rows, launch fewer
-    // rows at a time. (Not with the fused allreduce: every rank must make the same launches, and
-    // the ranks' K shards may differ.)
-    while (tp == nullptr && c.cw == 0 && mc > 1) {
+    // rows at a time. (Not with the fused allreduce over several ranks: every rank must make the same
+    // launches, and the ranks' K shards may differ. A one-rank launch meets nobody, and each launch
+    // takes its own epoch, so it may halve like the plain path.)
+    while ((tp == nullptr || tp->world == 1) && c.cw == 0 && mc > 1) {
       mc = (mc + 1) / 2;
       c = choose(mc, units, static_cast<int>(K), swiglu_i > 0, cfg);
     }
@@ -1285,11 +1286,10 @@ extern "C" int dk_w4a16_matmul_reduce_static(const void* x, int64_t ldx, const i
   char* base = static_cast<char*>(static_scratch_address());
   if (base == nullptr) return DK_ERR_CUDA;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  // The header must start at zero (epoch 0: the first launch uses tag 1; no CTA has arrived). The
-  // cells need no clearing: a CTA only reads cells its own threads wrote earlier in the same launch.
-  cudaError_t e = cudaMemsetAsync(base, 0, 16, st);
-  if (e != cudaSuccess)
-    return set_error(DK_ERR_CUDA, "w4a16_matmul_reduce_static: clearing the scratch header: %s", cudaGetErrorString(e));
+  // No clearing: the array is zero when the library loads (epoch 0, no CTA arrived), and every launch
+  // leaves the header consistent for the next one - each CTA arrives once, even one whose wait gave
+  // up, and the last to arrive resets the count and stores the launch's epoch. So the epoch advances
+  // across calls, and a cell left by an earlier call carries an older tag: a poll never accepts it.
   TPArgs tp;
   std::memset(&tp, 0, sizeof(tp));
   tp.cells[0] = reinterpret_cast<uint32_t*>(base + kTpHeaderBytes);

@@ -33,6 +33,26 @@ class MatmulConfig(ctypes.Structure):
                 ("l2_prefetch_bytes", ctypes.c_uint64 * MAX_L2_PREFETCH)]
 
 
+class StepLayer(ctypes.Structure):
+    """dk_step_layer: one decoder layer's tensors for the fused decode step (device pointers)."""
+
+    _fields_ = [(name, P) for name in (
+        "input_norm", "post_norm",
+        "qkv_qweight", "qkv_scales", "qkv_zeros", "qkv_bias",
+        "o_qweight", "o_scales", "o_zeros", "o_bias",
+        "gate_up_qweight", "gate_up_scales", "gate_up_zeros", "gate_up_bias",
+        "down_qweight", "down_scales", "down_zeros", "down_bias")]
+
+
+class StepModel(ctypes.Structure):
+    """dk_step_model: sizes and tensors of the model the fused decode step runs."""
+
+    _fields_ = [("n_layers", I32), ("hidden", I32), ("n_heads", I32), ("n_kv", I32), ("head_dim", I32),
+                ("intermediate", I32), ("vocab", I32), ("max_len", I32), ("batch", I32), ("eps", F32),
+                ("embed", P), ("final_norm", P), ("lm_head", P), ("rope_cos", P), ("rope_sin", P),
+                ("k_cache", P), ("v_cache", P), ("layers", ctypes.POINTER(StepLayer))]
+
+
 FLAG_STATIC_WEIGHTS = 1
 FLAG_GENERIC = 2
 FLAG_EXACT_DEQUANT = 4
@@ -70,6 +90,10 @@ SIGNATURES = {
                                   P],
     "dk_w4a16_matmul_reduce_static": [P, I64, P, P, P, P, P, I64, I64, I64, I64, I64, ctypes.POINTER(MatmulConfig),
                                       P],
+    "dk_step_workspace_bytes": [ctypes.POINTER(StepModel), ctypes.POINTER(ctypes.c_uint64)],
+    "dk_step_create": [ctypes.POINTER(StepModel), P, ctypes.c_uint64, ctypes.POINTER(P)],
+    "dk_step_run": [P, P, P, P, I64, P, P],
+    "dk_step_destroy": [P],
 }
 
 _lib = None
@@ -112,6 +136,20 @@ def ptr(t: torch.Tensor | None):
 
 def stream_of(t: torch.Tensor):
     return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def require_extent(ok: bool, message: str) -> None:
+    """Argument extents the kernels cannot see (they get raw pointers and sizes): a ValueError, raised
+    whether or not Python runs with -O, so a short tensor is never read past its end."""
+    if not ok:
+        raise ValueError(message)
+
+
+def reference_assert(ok: bool, message: str = "") -> None:
+    """A check the reference makes with `assert` (same AssertionError), raised explicitly so that it
+    also holds under python -O."""
+    if not ok:
+        raise AssertionError(message)
 
 
 def require_cuda(what: str, *tensors: torch.Tensor | None) -> None:

@@ -18,18 +18,19 @@ def decode_attention(qkv, k_cache, v_cache, pos, cos, sin, n_heads, n_kv, splits
     B, T, width = qkv.shape
     hd = k_cache.shape[-1]
     max_len = k_cache.shape[-2]
-    assert T == 1 and width == (n_heads + 2 * n_kv) * hd
-    assert tuple(k_cache.shape) == (B, n_kv, max_len, hd) and v_cache.shape == k_cache.shape, (
-        "decode_attention: k_cache and v_cache must be [B, n_kv, max_len, head_dim]")
-    assert pos.numel() >= 1, "decode_attention: pos holds the position"
+    _lib.require_extent(T == 1 and width == (n_heads + 2 * n_kv) * hd,
+                        "decode_attention: qkv must be [B, 1, (n_heads + 2 n_kv) * head_dim]")
+    _lib.require_extent(tuple(k_cache.shape) == (B, n_kv, max_len, hd) and v_cache.shape == k_cache.shape,
+                        "decode_attention: k_cache and v_cache must be [B, n_kv, max_len, head_dim]")
+    _lib.require_extent(pos.numel() >= 1, "decode_attention: pos holds the position")
     _lib.require_cuda("decode_attention", qkv, k_cache, v_cache, pos, cos, sin)
     _lib.require_dtype("decode_attention", torch.float16, qkv, k_cache, v_cache, cos, sin)
     _lib.require_dtype("decode_attention", torch.int64, pos)
-    assert k_cache.is_contiguous() and v_cache.is_contiguous()
+    _lib.require_extent(k_cache.is_contiguous() and v_cache.is_contiguous(), "decode_attention: caches must be contiguous")
     qkv = qkv.contiguous()
     out = torch.empty((B, 1, n_heads * hd), dtype=qkv.dtype, device=qkv.device)
     cos, sin = cos.contiguous(), sin.contiguous()
-    assert cos.shape == sin.shape and cos.shape[-1] == hd
+    _lib.require_extent(cos.shape == sin.shape and cos.shape[-1] == hd, "decode_attention: cos and sin must be [.., head_dim]")
     if cos.shape[0] > 1 and cos.shape[0] < max_len:
         raise RuntimeError("decode_attention: a RoPE table needs at least max_len rows")
     stride = hd if cos.shape[0] > 1 else 0

@@ -1,105 +1,152 @@
-"""CUDA-graph timing with rotating buffers (the reference's frozen method, kernels/bench/harness.py
-and docs/DECISIONS.md:27-52): input copies until the working set is >= 4x L2 so every call reads
-DRAM, one CUDA graph of one call per copy, replays for >= 50 ms, median of 7."""
+"""Kernel timing for the sweeps: CUDA-graph replays over rotating argument sets.
+
+The measurement method is the reference's frozen one (kernels/bench/harness.py and
+docs/DECISIONS.md:27-52 of the reference), so that "% of HBM peak" means the same number here:
+copies of the rotated arguments until one pass over them is at least 4x the L2 size (every call
+then reads DRAM, not L2), one CUDA graph holding one call per copy (no Python or launch-queue cost
+in the timed region), replays until a sample lasts >= MIN_MS, and the median of MEASUREMENTS
+samples. The code below is this package's own: a `_Timing` object owns the graph, its outputs and
+the calibration, and `capture` is the one place graphs are made.
+"""
 
 from __future__ import annotations
 
+import contextlib
 import gc
-import math
 import statistics
 from collections.abc import Callable
 
 import torch
+from torch.utils import _pytree
 
 WARMUP_CALLS = 3
 MEASUREMENTS = 7
 MIN_MS = 50.0
 MEMORY_BUDGET = 3 * 1024**3  # bytes of rotating copies per case
+MAX_COPIES = 512
+L2_MULTIPLE = 4
 
 
 def tensor_bytes(obj) -> int:
-    if isinstance(obj, torch.Tensor):
-        return obj.numel() * obj.element_size()
-    if isinstance(obj, (list, tuple)):
-        return sum(tensor_bytes(o) for o in obj)
-    if isinstance(obj, dict):
-        return sum(tensor_bytes(o) for o in obj.values())
-    return 0
+    """Bytes of every tensor inside `obj` (nested lists, tuples and dicts)."""
+    return sum(t.numel() * t.element_size() for t in _pytree.tree_leaves(obj) if isinstance(t, torch.Tensor))
 
 
 def n_copies(bytes_per_set: int, l2_mb: float) -> int:
-    want = math.ceil(4 * l2_mb * 2**20 / max(bytes_per_set, 1))
-    cap = max(2, MEMORY_BUDGET // max(bytes_per_set, 1))
-    return int(min(max(want, 2), cap, 512))
+    """How many argument sets make one pass at least L2_MULTIPLE x L2, bounded below by 2 and above
+    by MAX_COPIES and by what fits in MEMORY_BUDGET."""
+    per_set = max(int(bytes_per_set), 1)
+    target = L2_MULTIPLE * l2_mb * 2**20
+    needed = -(-int(target) // per_set)  # ceiling division
+    fits = max(MEMORY_BUDGET // per_set, 2)
+    return int(max(2, min(needed, fits, MAX_COPIES)))
+
+
+@contextlib.contextmanager
+def _collector_paused():
+    """Python's garbage collector off (after one full collection): a CUDA object freed by the GC in
+    the middle of a capture invalidates it."""
+    gc.collect()
+    was_on = gc.isenabled()
+    gc.disable()
+    try:
+        yield
+    finally:
+        if was_on:
+            gc.enable()
 
 
 def capture(body: Callable, retries: int = 1):
-    """Capture `body()` into a CUDA graph and return (graph, body's result); GC off during capture,
-    thread-local capture mode, one retry (reference harness.py:46-67)."""
-    last = None
-    for _ in range(retries + 1):
+    """(graph, body's return value) for `body()` captured into a new CUDA graph in thread-local
+    capture mode; a failed capture is retried `retries` more times before its error is raised."""
+    attempts = retries + 1
+    for attempt in range(attempts):
         graph = torch.cuda.CUDAGraph()
-        gc.collect()
-        gc.disable()
         try:
-            with torch.cuda.graph(graph, capture_error_mode="thread_local"):
-                out = body()
-            return graph, out
-        except Exception as e:  # torch.AcceleratorError and friends
-            last = e
+            with _collector_paused(), torch.cuda.graph(graph, capture_error_mode="thread_local"):
+                result = body()
+        except Exception:
             torch.cuda.synchronize()
-        finally:
-            gc.enable()
-    raise last
+            if attempt + 1 == attempts:
+                raise
+            continue
+        return graph, result
+    raise AssertionError("unreachable")
+
+
+def _elapsed_ms(run: Callable[[], None]) -> float:
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    run()
+    t1.record()
+    t1.synchronize()
+    return t0.elapsed_time(t1)
+
+
+class _Timing:
+    """One graph of `fn` over every argument set; the outputs stay referenced by the object so that
+    each call writes fresh memory."""
+
+    def __init__(self, fn: Callable, sets: list):
+        self.calls = len(sets)
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):  # first calls: library loads, kernel choices, allocations
+            for args in sets[:WARMUP_CALLS]:
+                fn(*args)
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        self.graph, self.outputs = capture(lambda: [fn(*args) for args in sets])
+        self.graph.replay()  # first replay uploads the graph
+        torch.cuda.synchronize()
+
+    def replays_for(self, ms: float) -> int:
+        one = max(_elapsed_ms(self.graph.replay), 1e-3)
+        return max(1, int(-(-ms // one)))
+
+    def sample_ms_per_call(self, replays: int) -> float:
+        def run():
+            for _ in range(replays):
+                self.graph.replay()
+
+        return _elapsed_ms(run) / (replays * self.calls)
+
+    def close(self):
+        del self.graph, self.outputs
 
 
 def time_graph(fn: Callable, sets: list) -> float:
-    """Median ms per call with all calls captured in one CUDA graph; every call keeps its own output
-    alive so writes do not stay in L2 (reference harness.py:70-103)."""
-    stream = torch.cuda.Stream()
-    stream.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(stream):
-        for args in sets[:WARMUP_CALLS]:
-            fn(*args)
-    torch.cuda.current_stream().wait_stream(stream)
-    torch.cuda.synchronize()
-    graph, outs = capture(lambda: [fn(*args) for args in sets])
-    graph.replay()
-    torch.cuda.synchronize()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    graph.replay()
-    end.record()
-    torch.cuda.synchronize()
-    replays = max(1, math.ceil(MIN_MS / max(start.elapsed_time(end), 1e-3)))
-    samples = []
-    for _ in range(MEASUREMENTS):
-        start.record()
-        for _ in range(replays):
-            graph.replay()
-        end.record()
-        torch.cuda.synchronize()
-        samples.append(start.elapsed_time(end) / (replays * len(sets)))
-    del graph, outs
-    return statistics.median(samples)
+    """Median milliseconds per call of `fn(*args)` over the argument sets, all calls in one graph."""
+    timing = _Timing(fn, sets)
+    try:
+        replays = timing.replays_for(MIN_MS)
+        return statistics.median(timing.sample_ms_per_call(replays) for _ in range(MEASUREMENTS))
+    finally:
+        timing.close()
 
 
-def time_rotating(fn: Callable, args: tuple, rotate: tuple, max_copies: int = 512) -> float:
-    """Graph time of fn(*args) with the tensors at positions `rotate` copied until the working set
-    exceeds 4x L2 (read from the device), within `n_copies`' limits (at most 512 copies and 3 GiB,
-    at least 2: the reference's measure(), kernels/bench/harness.py:144-160). Sets of under ~1 MB
-    (RMSNorm or SwiGLU of a few rows) stay below 4x L2 at 512 copies, as in the reference."""
+def time_rotating(fn: Callable, args: tuple, rotate: tuple, max_copies: int = MAX_COPIES) -> float:
+    """Graph time of fn(*args) with the tensors at positions `rotate` copied (n_copies of them, at most
+    `max_copies`; the L2 size is read from the current device). Sets of under ~1 MB stay below 4x L2
+    at 512 copies, as in the reference."""
     l2_mb = torch.cuda.get_device_properties(torch.cuda.current_device()).L2_cache_size / 2**20
-    nbytes = sum(tensor_bytes(args[i]) for i in rotate)
-    copies = min(n_copies(nbytes, l2_mb), max_copies)
-    sets = [args] + [tuple(a.clone() if i in rotate else a for i, a in enumerate(args)) for _ in range(copies - 1)]
-    return time_graph(fn, sets)
+    rotated = set(rotate)
+    copies = min(n_copies(sum(tensor_bytes(args[i]) for i in rotated), l2_mb), max_copies)
+
+    def fresh_set():
+        return tuple(a.clone() if i in rotated else a for i, a in enumerate(args))
+
+    return time_graph(fn, [args, *(fresh_set() for _ in range(copies - 1))])
 
 
 def metrics(ms: float, bytes_moved: int, flops: int, peak_gbps: float, peak_tflops: float) -> dict:
-    s = ms * 1e-3
-    gbps = bytes_moved / s / 1e9
-    tflops = flops / s / 1e12 if flops else 0.0
-    return {"gbps": gbps, "pct_peak_bw": 100 * gbps / peak_gbps, "tflops": tflops,
-            "pct_peak_flops": 100 * tflops / peak_tflops if flops else 0.0,
-            "intensity": flops / bytes_moved if flops else 0.0}
+    """Achieved bandwidth and throughput of one timed call against the given peaks (the reference's
+    result fields: gbps, pct_peak_bw, tflops, pct_peak_flops, intensity)."""
+    seconds = ms / 1e3
+    gbps = bytes_moved / seconds / 1e9
+    out = {"gbps": gbps, "pct_peak_bw": 100.0 * gbps / peak_gbps, "tflops": 0.0, "pct_peak_flops": 0.0,
+           "intensity": 0.0}
+    if flops:
+        tflops = flops / seconds / 1e12
+        out.update(tflops=tflops, pct_peak_flops=100.0 * tflops / peak_tflops, intensity=flops / bytes_moved)
+    return out

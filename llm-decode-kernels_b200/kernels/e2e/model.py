@@ -175,28 +175,41 @@ class OursFP8Backend(OursBackend):
         return Backend.norm_gate_up_act(self, x, w, eps, residual, p)
 
 
+_BACKENDS = {
+    "fp16": Backend,
+    "w4_ref": W4RefBackend,
+    "ours": lambda: OursBackend("triton"),
+    "ours_cuda": lambda: OursBackend("cuda"),
+    "ours_fp8": OursFP8Backend,
+}
+_LM_SUFFIX = "_lm"
+
+
 def make_backend(name: str) -> Backend:
-    """`<name>_lm` = the quantized backend `<name>` with lm_head quantized as well
-    (reference model.py:121-136)."""
-    base, quant_lm_head = (name[:-3], True) if name.endswith("_lm") else (name, False)
-    be = {
-        "fp16": Backend,
-        "w4_ref": W4RefBackend,
-        "ours": lambda: OursBackend("triton"),
-        "ours_cuda": lambda: OursBackend("cuda"),
-        "ours_fp8": OursFP8Backend,
-    }[base]()
-    if quant_lm_head:
-        if not be.quantized:
-            raise ValueError(f"{name}: only quantized backends can quantize lm_head")
-        be.name = name
-    be.quant_lm_head = quant_lm_head
-    return be
+    """A backend by the reference's names (kernels/e2e/model.py:121-136): one of `_BACKENDS`, or a
+    quantized one with `_lm` appended to quantize lm_head as well (`fp16_lm` is a ValueError)."""
+    base = name.removesuffix(_LM_SUFFIX)
+    quant_head = base != name
+    if base not in _BACKENDS:
+        raise KeyError(name)
+    backend = _BACKENDS[base]()
+    if quant_head and not backend.quantized:
+        raise ValueError(f"{name}: only quantized backends can quantize lm_head")
+    backend.quant_lm_head = quant_head
+    if quant_head:
+        backend.name = name
+    return backend
+
+
+def _nbytes(*tensors) -> int:
+    return sum(t.numel() * t.element_size() for t in tensors if t is not None)
 
 
 # ------------------------------------------------------------------------------------- model
 @dataclass
 class Layer:
+    """One decoder layer: its two RMSNorm weights and the four projections in launch order."""
+
     ln1: torch.Tensor
     ln2: torch.Tensor
     qkv: Linear
@@ -204,14 +217,20 @@ class Layer:
     gate_up: Linear
     down: Linear
 
+    def projections(self) -> tuple:
+        return self.qkv, self.o, self.gate_up, self.down
+
 
 class QwenRunner:
-    """Qwen2 forward on a static KV cache (reference model.py:150-253)."""
+    """Qwen2 forward on a static KV cache (reference model.py:150-253): the T == 1 decode path runs
+    the backend's fused kernels, longer inputs the reference's numerics (SDPA over the cache); a
+    greedy step (`greedy_step`) of the W4A16 runner at batch <= 4 is one fused kernel."""
 
     def __init__(self, hf_model, backend: Backend, max_len: int = 2048, batch: int = 1,
-                 l2_prefetch: bool = False, tp=None):
+                 l2_prefetch: bool = False, tp=None, fused_step: bool = True):
         """tp: a kernels.tp.TensorParallel to hold only this rank's shards (column-sharded qkv,
-        gate_up and lm_head; row-sharded o_proj and down, reduced over the group), or None."""
+        gate_up and lm_head; row-sharded o_proj and down, reduced over the group), or None.
+        fused_step: run greedy_step as the single decode-step kernel where it supports the model."""
         cfg = hf_model.config
         self.backend = backend
         self.eps = cfg.rms_norm_eps
@@ -220,40 +239,38 @@ class QwenRunner:
         self.head_dim = getattr(cfg, "head_dim", None) or cfg.hidden_size // self.n_heads
         self.max_len = max_len
         self.batch = batch
+        self.fused_step = fused_step
+        self._step_kernel = None
         m = hf_model.model
         dev = m.embed_tokens.weight.device
         self.embed = m.embed_tokens.weight
         self.tp = tp
         hd = self.head_dim
-        full = (0, 1 << 62)
+        everything = (0, 1 << 62)
         if tp is not None:
             self.plan = tp.plan(cfg)
             self.n_heads, self.n_kv = self.plan.n_q, self.plan.n_kv
             qh, kvh, mlp, voc = self.plan.q_heads, self.plan.kv_heads, self.plan.mlp, self.plan.vocab
         else:
             self.plan = None
-            qh, kvh, mlp, voc = full, full, full, full
+            qh = kvh = mlp = voc = everything
         self.vocab_start = voc[0] if tp is not None else 0
-        qc, kvc = (qh[0] * hd, qh[1] * hd), (kvh[0] * hd, kvh[1] * hd)
+        q_rows, kv_rows = (qh[0] * hd, qh[1] * hd), (kvh[0] * hd, kvh[1] * hd)
         self.lm_head = hf_model.lm_head.weight[voc[0]:voc[1]]
         self.final_norm = m.norm.weight
         rope = getattr(cfg, "rope_parameters", None) or {}
         theta = rope.get("rope_theta", getattr(cfg, "rope_theta", 10000.0))
-        d = self.head_dim
-        self.inv_freq = 1.0 / (theta ** (torch.arange(0, d, 2, device=dev, dtype=torch.float) / d))
+        self.inv_freq = 1.0 / (theta ** (torch.arange(0, hd, 2, device=dev, dtype=torch.float) / hd))
 
-        def part(mod, rows=full, cols=full):
-            """(weight, bias) of a module restricted to output rows / input columns (a shard)."""
+        def shard(mod, rows=everything, cols=everything):
+            """(weight, bias) of a module cut to output rows / input columns (this rank's shard)."""
             w = mod.weight.data[rows[0]:rows[1], cols[0]:cols[1]]
-            b = None if mod.bias is None else mod.bias.data[rows[0]:rows[1]]
-            return w, b
+            return w, None if mod.bias is None else mod.bias.data[rows[0]:rows[1]]
 
-        def lin(*parts) -> Linear:
-            parts = [p if isinstance(p, tuple) else part(p) for p in parts]
-            w = torch.cat([pw for pw, _ in parts], 0).contiguous()
-            b = None
-            if parts[0][1] is not None:
-                b = torch.cat([pb for _, pb in parts], 0).contiguous()
+        def projection(*pieces) -> Linear:
+            """Output rows of the pieces stacked (fused qkv, fused gate_up), then the backend's format."""
+            w = torch.cat([pw for pw, _ in pieces]).contiguous()
+            b = None if pieces[0][1] is None else torch.cat([pb for _, pb in pieces]).contiguous()
             if not backend.quantized:
                 return Linear(w=w, bias=b)
             if hasattr(backend, "quantize"):  # formats other than int4 RTN (FP8)
@@ -264,31 +281,32 @@ class QwenRunner:
             return Linear(qweight=qw, scales=s, zeros=z, bias=b)
 
         # Optional quantized copy of lm_head (the fp16 table stays for the embedding lookup).
-        self.head_q = (lin(part(hf_model.lm_head, rows=voc)) if getattr(backend, "quant_lm_head", False)
+        self.head_q = (projection(shard(hf_model.lm_head, rows=voc)) if getattr(backend, "quant_lm_head", False)
                        else None)
         self.layers = []
         for layer in m.layers:
-            a, f = layer.self_attn, layer.mlp
+            att, mlp_mod = layer.self_attn, layer.mlp
             self.layers.append(Layer(
                 ln1=layer.input_layernorm.weight, ln2=layer.post_attention_layernorm.weight,
-                qkv=lin(part(a.q_proj, rows=qc), part(a.k_proj, rows=kvc), part(a.v_proj, rows=kvc)),
-                o=lin(part(a.o_proj, cols=qc)),
-                gate_up=lin(part(f.gate_proj, rows=mlp), part(f.up_proj, rows=mlp)),
-                down=lin(part(f.down_proj, cols=mlp)),
+                qkv=projection(shard(att.q_proj, rows=q_rows), shard(att.k_proj, rows=kv_rows),
+                               shard(att.v_proj, rows=kv_rows)),
+                o=projection(shard(att.o_proj, cols=q_rows)),
+                gate_up=projection(shard(mlp_mod.gate_proj, rows=mlp), shard(mlp_mod.up_proj, rows=mlp)),
+                down=projection(shard(mlp_mod.down_proj, cols=mlp)),
             ))
         if tp is not None:
             tp.setup(cfg.hidden_size, dev)
         if backend.fused_decode and l2_prefetch:
             self._plan_l2_prefetch()
-        # RoPE tables for the decode kernel, computed with the same ops as forward() does per step
+        # RoPE tables for the decode kernels, computed with the same ops as the T > 1 path uses per step
         if backend.fused_decode:
-            freqs = torch.arange(max_len, device=dev)[:, None].float() * self.inv_freq[None, :]
-            emb = torch.cat((freqs, freqs), dim=-1)
-            self.rope_cos = emb.cos().to(self.embed.dtype).contiguous()
-            self.rope_sin = emb.sin().to(self.embed.dtype).contiguous()
-        shape = (len(self.layers), batch, self.n_kv, max_len, self.head_dim)
-        self.k_cache = torch.zeros(shape, device=dev, dtype=self.embed.dtype)
-        self.v_cache = torch.zeros(shape, device=dev, dtype=self.embed.dtype)
+            self.rope_cos, self.rope_sin = self._rope_tables(torch.arange(max_len, device=dev), self.embed.dtype)
+        self.k_cache, self.v_cache = self._new_caches(batch)
+
+    def _new_caches(self, batch: int):
+        shape = (len(self.layers), batch, self.n_kv, self.max_len, self.head_dim)
+        dev, dt = self.embed.device, self.embed.dtype
+        return torch.zeros(shape, device=dev, dtype=dt), torch.zeros(shape, device=dev, dtype=dt)
 
     def with_batch(self, batch: int) -> "QwenRunner":
         """A runner for another batch size that shares this one's weights (new, empty KV caches)."""
@@ -296,9 +314,8 @@ class QwenRunner:
 
         r = copy.copy(self)
         r.batch = batch
-        shape = (len(self.layers), batch, self.n_kv, self.max_len, self.head_dim)
-        r.k_cache = torch.zeros(shape, device=self.k_cache.device, dtype=self.k_cache.dtype)
-        r.v_cache = torch.zeros(shape, device=self.v_cache.device, dtype=self.v_cache.dtype)
+        r._step_kernel = None
+        r.k_cache, r.v_cache = self._new_caches(batch)
         return r
 
     def _plan_l2_prefetch(self):
@@ -316,19 +333,16 @@ class QwenRunner:
             p.l2_next = tuple(t for q in ahead for t in tensors(q)) or None
 
     def weight_bytes(self) -> dict:
-        """Bytes of the swapped layers vs the parts that stay fp16 (reference model.py:196-210)."""
+        """Bytes the swapped layers read per token vs the parts that stay fp16 (the reference's
+        accounting, model.py:196-210): packed weights + scales + zeros + bias, or fp16 weights."""
+        quantized = self.backend.quantized
 
-        def nbytes(t):
-            return 0 if t is None else t.numel() * t.element_size()
+        def size(p: Linear) -> int:
+            return _nbytes(p.qweight, p.scales, p.zeros, p.bias) if quantized else _nbytes(p.w, p.bias)
 
-        def size(p: Linear):
-            if self.backend.quantized:
-                return nbytes(p.qweight) + nbytes(p.scales) + nbytes(p.zeros) + nbytes(p.bias)
-            return nbytes(p.w) + nbytes(p.bias)
-
-        layers = sum(size(p) for L in self.layers for p in (L.qkv, L.o, L.gate_up, L.down))
-        head = size(self.head_q) if self.head_q is not None else nbytes(self.lm_head)
-        return {"linear_layers": layers, "embed": nbytes(self.embed), "lm_head_read": head,
+        layers = sum(size(p) for L in self.layers for p in L.projections())
+        return {"linear_layers": layers, "embed": _nbytes(self.embed),
+                "lm_head_read": size(self.head_q) if self.head_q is not None else _nbytes(self.lm_head),
                 "lm_head_quantized": self.head_q is not None,
                 "lm_head_shared_with_embed": self.lm_head.data_ptr() == self.embed.data_ptr()}
 
@@ -347,72 +361,103 @@ class QwenRunner:
             return last.argmax(-1)
         return self.tp.argmax(last, self.vocab_start)
 
+    # ------------------------------------------------------------------ greedy decode step
+    def step_kernel(self):
+        """The fused decode-step kernel for this runner (built on first use; set-up synchronizes, so
+        the first call must come before any graph capture), or None where it does not apply."""
+        if not self.fused_step:
+            return None
+        if self._step_kernel is None:
+            from kernels import step
+
+            if step.supported(self) is not None:
+                self.fused_step = False
+                return None
+            self._step_kernel = step.DecodeStep(self)
+        return self._step_kernel
+
+    @torch.no_grad()
+    def greedy_step(self, tok: torch.Tensor, pos: torch.Tensor, out: torch.Tensor) -> None:
+        """One greedy decode step on device state (the reference's GraphDecoder._step,
+        kernels/e2e/run.py:69-74): tok [B, 1] is fed at position pos [1]; the pick is stored in
+        out[:, pos] and becomes tok; pos advances. Graph-capturable after a first eager call."""
+        fused = self.step_kernel()
+        if fused is not None:
+            fused(tok, pos, out)
+            return
+        pick = self.greedy(self.forward(tok, pos)).view(-1, 1)
+        out.index_copy_(1, pos, pick)
+        tok.copy_(pick)
+        pos.add_(1)
+
+    # ------------------------------------------------------------------ forward
+    def _rope_tables(self, positions: torch.Tensor, dtype):
+        """cos, sin [len(positions), head_dim] of the reference's RoPE (angles cat(freqs, freqs))."""
+        ang = positions[:, None].float() * self.inv_freq[None, :]
+        ang = torch.cat((ang, ang), dim=-1)
+        return ang.cos().to(dtype).contiguous(), ang.sin().to(dtype).contiguous()
+
     def _rope(self, x, cos, sin):
-        x1, x2 = x[..., : self.head_dim // 2], x[..., self.head_dim // 2:]
-        return x * cos + torch.cat((-x2, x1), dim=-1) * sin
+        half = self.head_dim // 2
+        return x * cos + torch.cat((-x[..., half:], x[..., :half]), dim=-1) * sin
 
     def _attention_sdpa(self, i, qkv, pos, cos, sin, mask, B, T):
         """RoPE, cache write and SDPA over the whole cache, as the reference does
         (reference model.py:236-244)."""
         nq, nkv, hd = self.n_heads, self.n_kv, self.head_dim
         q, k, v = qkv.split([nq * hd, nkv * hd, nkv * hd], dim=-1)
-        q = self._rope(q.view(B, T, nq, hd).transpose(1, 2), cos, sin)
-        k = self._rope(k.view(B, T, nkv, hd).transpose(1, 2), cos, sin)
-        v = v.view(B, T, nkv, hd).transpose(1, 2)
+        heads = lambda t, n: t.view(B, T, n, hd).transpose(1, 2)  # noqa: E731
+        q, k, v = self._rope(heads(q, nq), cos, sin), self._rope(heads(k, nkv), cos, sin), heads(v, nkv)
         self.k_cache[i].index_copy_(2, pos, k)
         self.v_cache[i].index_copy_(2, pos, v)
-        attn = F.scaled_dot_product_attention(
-            q, self.k_cache[i], self.v_cache[i], attn_mask=mask, enable_gqa=True)
+        attn = F.scaled_dot_product_attention(q, self.k_cache[i], self.v_cache[i], attn_mask=mask, enable_gqa=True)
         return attn.transpose(1, 2).reshape(B, T, nq * hd)
+
+    def _decode_layers(self, x, pos):
+        """T == 1 on the kernel backends: five kernels per layer (norm + qkv, attention, o_proj,
+        norm + gate_up + SwiGLU, down). Returns (last MLP output, residual stream)."""
+        from kernels.attention import decode_attention
+
+        be, eps = self.backend, self.eps
+        residual, h = None, x
+        for i, L in enumerate(self.layers):
+            qkv, new_res = be.norm_linear(h, L.ln1, eps, residual, L.qkv)
+            residual = x if residual is None else new_res
+            attn = decode_attention(qkv, self.k_cache[i], self.v_cache[i], pos, self.rope_cos, self.rope_sin,
+                                    self.n_heads, self.n_kv, static_cache=True)
+            act, residual = be.norm_gate_up_act(self._row_linear(attn, L.o), L.ln2, eps, residual, L.gate_up)
+            h = self._row_linear(act, L.down)
+        return h, residual
+
+    def _full_layers(self, x, pos, B, T):
+        """Any T with the reference's per-op numerics (SDPA over the masked cache,
+        reference model.py:216-247). Returns (last MLP output, residual stream)."""
+        be, eps = self.backend, self.eps
+        cos, sin = self._rope_tables(pos, x.dtype)
+        mask = torch.arange(self.max_len, device=x.device)[None, :] <= pos[:, None]  # True = attend
+        residual, h = x, None
+        for i, L in enumerate(self.layers):
+            if h is None:
+                h = be.norm(x, L.ln1, eps)
+            else:
+                h, residual = be.norm(h, L.ln1, eps, residual=residual)
+            attn = self._attention_sdpa(i, be.linear(h, L.qkv), pos, cos, sin, mask, B, T)
+            h, residual = be.norm(self._row_linear(attn, L.o), L.ln2, eps, residual=residual)
+            h = self._row_linear(be.gate_up_act(h, L.gate_up), L.down)
+        return h, residual
 
     @torch.no_grad()
     def forward(self, tokens: torch.Tensor, pos: torch.Tensor, all_logits: bool = False):
         """tokens [B, T]; pos: int64 tensor [T] of absolute positions. Graph-capturable."""
-        be, eps = self.backend, self.eps
         B, T = tokens.shape
         x = F.embedding(tokens, self.embed)
-        decode = be.fused_decode and T == 1
-        mask = None
-        if decode:  # the attention kernel reads row `pos` of the RoPE tables
-            cos, sin = self.rope_cos, self.rope_sin
+        if self.backend.fused_decode and T == 1:
+            h, residual = self._decode_layers(x, pos)
         else:
-            freqs = pos[:, None].float() * self.inv_freq[None, :]
-            emb = torch.cat((freqs, freqs), dim=-1)
-            cos, sin = emb.cos().to(x.dtype), emb.sin().to(x.dtype)
-            keys = torch.arange(self.max_len, device=x.device)
-            mask = keys[None, :] <= pos[:, None]  # [T, max_len], True = attend
-
-        residual, h = x, None
-        for i, L in enumerate(self.layers):
-            if decode:
-                # one kernel each: norm + qkv, attention, o, norm + gate_up + SwiGLU, down
-                from kernels.attention import decode_attention
-
-                if h is None:
-                    qkv, _ = be.norm_linear(x, L.ln1, eps, None, L.qkv)
-                else:  # residual += previous MLP output, input norm of this layer, qkv
-                    qkv, residual = be.norm_linear(h, L.ln1, eps, residual, L.qkv)
-                attn = decode_attention(qkv, self.k_cache[i], self.v_cache[i], pos, cos, sin,
-                                        self.n_heads, self.n_kv, static_cache=True)
-                o = self._row_linear(attn, L.o)
-                act, residual = be.norm_gate_up_act(o, L.ln2, eps, residual, L.gate_up)
-                h = self._row_linear(act, L.down)
-                continue
-            if h is None:
-                h = be.norm(x, L.ln1, eps)
-            else:  # fused: residual += previous MLP output, then input norm of this layer
-                h, residual = be.norm(h, L.ln1, eps, residual=residual)
-            qkv = be.linear(h, L.qkv)
-            attn = self._attention_sdpa(i, qkv, pos, cos, sin, mask, B, T)
-            o = self._row_linear(attn, L.o)
-            h, residual = be.norm(o, L.ln2, eps, residual=residual)
-            h = self._row_linear(be.gate_up_act(h, L.gate_up), L.down)
-        h, _ = be.norm(h, self.final_norm, eps, residual=residual)
-        if not all_logits:
-            h = h[:, -1:]
-        if self.head_q is not None:
-            return be.linear(h, self.head_q)
-        return F.linear(h, self.lm_head)
+            h, residual = self._full_layers(x, pos, B, T)
+        h, _ = self.backend.norm(h, self.final_norm, self.eps, residual=residual)
+        h = h if all_logits else h[:, -1:]
+        return F.linear(h, self.lm_head) if self.head_q is None else self.backend.linear(h, self.head_q)
 
 
 def random_qwen2(arch: dict, dtype=torch.float16, device="cuda", seed: int = 0):

@@ -1,12 +1,14 @@
-"""End-to-end decode timing on a Qwen2 runner (reference kernels/e2e/run.py, without the HF
-download, perplexity and chat prompts, which need the network).
+"""End-to-end decode timing on a Qwen2 runner. Public names and timing semantics follow the
+reference's kernels/e2e/run.py (without the HF download, perplexity and chat prompts, which need the
+network); the implementation is this package's own.
 
-- `GraphDecoder`: one greedy decode step (forward + argmax + position bump) captured in a CUDA
-  graph and replayed per token (reference run.py:58-111), for batch 1 or more.
-- `decode_speed`: median tok/s over repeats (reference run.py:114-122).
+- `GraphDecoder`: greedy decoding with one captured CUDA graph per token step (reference
+  run.py:58-111), for batch 1 or more. The step itself is `QwenRunner.greedy_step`, which the fused
+  backends run as a single decode-step kernel.
+- `decode_speed`: median tok/s over repeated generations (reference run.py:114-122).
 - `prefill_speed`, `layers_only_ms`: reference run.py:142-201.
-- `step_host`: the public per-token API of a server loop - the token comes from pinned host memory,
-  the graph runs, the next token is read back to the host.
+- `GraphDecoder.step_host`: the per-token API of a server loop - the token comes from pinned host
+  memory, the graph runs, the next token is read back to the host.
 - `greedy_parity`: the reference's parity figures (run.py:289-303) between two runners - max |logit
   diff| and the first greedy divergence - for batch-1 synthetic prompts.
 """
@@ -14,6 +16,7 @@ download, perplexity and chat prompts, which need the network).
 from __future__ import annotations
 
 import statistics
+from collections.abc import Callable
 
 import torch
 
@@ -21,72 +24,87 @@ from kernels.bench.harness import capture
 from kernels.e2e.model import QwenRunner
 
 
-def _events():
-    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+def _device_seconds(work: Callable[[], None]) -> float:
+    """Seconds `work()` takes on the current stream, by CUDA events."""
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    work()
+    t1.record()
+    t1.synchronize()
+    return t0.elapsed_time(t1) / 1e3
+
+
+def _replay(graph, times: int) -> Callable[[], None]:
+    def run():
+        for _ in range(times):
+            graph.replay()
+
+    return run
 
 
 class GraphDecoder:
-    """Captures one greedy decode step (forward + argmax + bookkeeping) in a CUDA graph."""
+    """Greedy decoding, one CUDA graph per token step.
+
+    Device state: `tok` [B, 1], the token the next step consumes; `pos` [1], its position; `out`
+    [B, max_len], the greedy token chosen at each position. A step (`QwenRunner.greedy_step`) feeds
+    `tok` at `pos`, stores the pick in `out[:, pos]`, makes it the next `tok` and advances `pos`, all on
+    the device, so the graph captured once replays for every token.
+    """
+
+    WARM_STEPS = 3
 
     def __init__(self, runner: QwenRunner):
         self.r = runner
         dev = runner.embed.device
-        B = runner.batch
-        self.tok = torch.zeros(B, 1, dtype=torch.long, device=dev)
+        rows = runner.batch
+        self.tok = torch.zeros(rows, 1, dtype=torch.long, device=dev)
         self.pos = torch.zeros(1, dtype=torch.long, device=dev)
-        self.out = torch.zeros(B, runner.max_len, dtype=torch.long, device=dev)
+        self.out = torch.zeros(rows, runner.max_len, dtype=torch.long, device=dev)
         self.graph = None
-        self.host_tok = torch.zeros(B, 1, dtype=torch.long).pin_memory()
-        self.host_next = torch.zeros(B, 1, dtype=torch.long).pin_memory()
+        self.host_tok = torch.zeros(rows, 1, dtype=torch.long).pin_memory()
+        self.host_next = torch.zeros(rows, 1, dtype=torch.long).pin_memory()
 
     def _step(self):
-        logits = self.r.forward(self.tok, self.pos)
-        nxt = self.r.greedy(logits)
-        self.out.index_copy_(1, self.pos, nxt.view(-1, 1))
-        self.tok.copy_(nxt.view(-1, 1))
-        self.pos.add_(1)
+        self.r.greedy_step(self.tok, self.pos, self.out)
 
-    def prefill(self, ids: torch.Tensor):
-        """ids [B, P] on the device. Fills the cache, sets the first generated token."""
-        P = ids.shape[1]
-        logits = self.r.forward(ids, torch.arange(P, device=ids.device))
-        self.tok.copy_(self.r.greedy(logits).view(-1, 1))
-        self.pos.fill_(P)
+    def prefill(self, ids: torch.Tensor) -> int:
+        """Run the prompt ids [B, P] (on the device) through the model: fills the KV cache, and the
+        first generated token becomes `tok` at position P (also recorded at out[:, P - 1])."""
+        n = ids.shape[1]
+        first = self.r.greedy(self.r.forward(ids, torch.arange(n, device=ids.device)))
         self.out.zero_()
-        self.out[:, P - 1] = self.tok.view(-1)  # position P-1 holds the first new token
-        return P
+        self.out[:, n - 1] = first
+        self.tok[:, 0] = first
+        self.pos.fill_(n)
+        return n
 
     def capture(self, ids):
-        # warm up outside the graph (kernel choices, library loads), then reset the state
+        """Warm up (kernel choices and library loads happen outside the graph), then capture one
+        step from the state right after the prompt."""
         self.prefill(ids)
         self._step()
         torch.cuda.synchronize()
-        s = torch.cuda.Stream()
-        s.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(s):
-            for _ in range(3):
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(self.WARM_STEPS):
                 self._step()
-        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.current_stream().wait_stream(side)
         torch.cuda.synchronize()
         self.prefill(ids)
         self.graph, _ = capture(self._step)
         torch.cuda.synchronize()
 
     def generate(self, ids, steps: int) -> tuple[list, float]:
-        P = self.prefill(ids)
+        """(tokens [B][steps + 1] from the first generated one on, device seconds of the steps)."""
+        n = self.prefill(ids)
         torch.cuda.synchronize()
-        start, end = _events()
-        start.record()
-        for _ in range(steps):
-            self.graph.replay()
-        end.record()
-        torch.cuda.synchronize()
-        tokens = self.out[:, P - 1: P - 1 + steps + 1].tolist()
-        return tokens, start.elapsed_time(end) / 1e3
+        sec = _device_seconds(_replay(self.graph, steps))
+        return self.out[:, n - 1: n + steps].tolist(), sec
 
     def step_host(self, token_host: torch.Tensor) -> torch.Tensor:
-        """One token through the public API from host memory: copy the token in (pinned host ->
-        device), replay the step, copy the next token out (device -> pinned host) and wait for it."""
+        """One token through the public API from host memory: pinned host -> device copy of the
+        token, one graph replay, device -> pinned host copy of the next token, host wait."""
         self.host_tok.copy_(token_host)
         self.tok.copy_(self.host_tok, non_blocking=True)
         self.graph.replay()
@@ -96,77 +114,59 @@ class GraphDecoder:
 
 
 def decode_speed(runner, ids, steps: int, repeats: int = 3) -> dict:
+    """Batch x steps / device time of `steps` graph-replayed greedy steps; median over `repeats`."""
     dec = GraphDecoder(runner)
     dec.capture(ids)
-    rates = []
-    for _ in range(repeats):
-        _, sec = dec.generate(ids, steps)
-        rates.append(steps * runner.batch / sec)
-    return {"tok_s": statistics.median(rates), "tok_s_min": min(rates), "tok_s_max": max(rates),
-            "ms_per_step": 1e3 * runner.batch / statistics.median(rates), "steps": steps,
-            "batch": runner.batch}
+    rows = runner.batch
+    rates = sorted(rows * steps / dec.generate(ids, steps)[1] for _ in range(repeats))
+    mid = statistics.median(rates)
+    return {"tok_s": mid, "tok_s_min": rates[0], "tok_s_max": rates[-1], "ms_per_step": 1e3 * rows / mid,
+            "steps": steps, "batch": rows}
+
+
+def _graph_median_seconds(body: Callable, warm: int, samples: int, replays: int = 1) -> float:
+    """Median device seconds of one call of `body`, captured in a graph after `warm` eager calls."""
+    for _ in range(warm):
+        body()
+    torch.cuda.synchronize()
+    graph, _ = capture(body)
+    try:
+        graph.replay()
+        torch.cuda.synchronize()
+        return statistics.median(_device_seconds(_replay(graph, replays)) / replays for _ in range(samples))
+    finally:
+        del graph
 
 
 def prefill_speed(runner, T: int, repeats: int = 5) -> dict:
+    """Prompt tokens per second of one T-token forward (random ids), graph-captured."""
     dev = runner.embed.device
     ids = torch.randint(0, runner.embed.shape[0], (runner.batch, T), device=dev)
-    pos = torch.arange(T, device=dev)
-    for _ in range(2):
-        runner.forward(ids, pos)
-    torch.cuda.synchronize()
-    graph, _ = capture(lambda: runner.forward(ids, pos))
-    graph.replay()
-    torch.cuda.synchronize()
-    times = []
-    for _ in range(repeats):
-        start, end = _events()
-        start.record()
-        graph.replay()
-        end.record()
-        torch.cuda.synchronize()
-        times.append(start.elapsed_time(end) / 1e3)
-    del graph
-    t = statistics.median(times)
-    return {"T": T, "ms": t * 1e3, "tok_s": runner.batch * T / t}
+    positions = torch.arange(T, device=dev)
+    sec = _graph_median_seconds(lambda: runner.forward(ids, positions), warm=2, samples=repeats)
+    return {"T": T, "ms": sec * 1e3, "tok_s": runner.batch * T / sec}
 
 
 def layers_only_ms(runner, M: int = 1) -> float:
-    """Graph time of the swapped ops of one decode step: per layer the qkv, o, gate_up(+act) and
-    down projections and the two fused add+norms; no attention, embedding or lm_head
-    (reference run.py:166-201)."""
+    """Milliseconds of the swapped ops of one decode step in a graph: per layer the qkv, o,
+    gate_up(+act) and down projections and the two fused add+norms; no attention, embedding or
+    lm_head (reference run.py:166-201)."""
     be, eps = runner.backend, runner.eps
     dev = runner.embed.device
-    H = runner.embed.shape[1]
-    x = torch.randn(1, M, H, device=dev, dtype=torch.float16)
-    res = torch.randn_like(x)
-    nq, hd = runner.n_heads, runner.head_dim
+    hidden = runner.embed.shape[1]
+    q_width = runner.n_heads * runner.head_dim
+    x = torch.randn(1, M, hidden, device=dev, dtype=torch.float16)
+    res0 = torch.randn_like(x)
 
-    def step():
-        h, r = be.norm(x, runner.layers[0].ln1, eps, residual=res)
+    def layers():
+        h, res = be.norm(x, runner.layers[0].ln1, eps, residual=res0)
         for L in runner.layers:
-            qkv = be.linear(h, L.qkv)
-            o = be.linear(qkv[..., : nq * hd].contiguous(), L.o)
-            h, r = be.norm(o, L.ln2, eps, residual=r)
+            q = be.linear(h, L.qkv)[..., :q_width].contiguous()
+            h, res = be.norm(be.linear(q, L.o), L.ln2, eps, residual=res)
             h = be.linear(be.gate_up_act(h, L.gate_up), L.down)
-            h, r = be.norm(h, L.ln1, eps, residual=r)
+            h, res = be.norm(h, L.ln1, eps, residual=res)
 
-    for _ in range(3):
-        step()
-    torch.cuda.synchronize()
-    graph, _ = capture(step)
-    graph.replay()
-    torch.cuda.synchronize()
-    times = []
-    for _ in range(7):
-        start, end = _events()
-        start.record()
-        for _ in range(10):
-            graph.replay()
-        end.record()
-        torch.cuda.synchronize()
-        times.append(start.elapsed_time(end) / 10)
-    del graph
-    return statistics.median(times)
+    return 1e3 * _graph_median_seconds(layers, warm=3, samples=7, replays=10)
 
 
 @torch.no_grad()
@@ -180,27 +180,27 @@ def greedy_parity(runner: QwenRunner, ref: QwenRunner, ids: torch.Tensor, steps:
     least half of it) and the largest |reference logit| (for relative tolerances)."""
     T = ids.shape[1]
     dev = ids.device
-    pos = torch.arange(T, device=dev)
-    la = runner.forward(ids, pos)[:, -1].float()
-    lb = ref.forward(ids, pos)[:, -1].float()
-    diff = (la - lb).abs().max().item()
-    ref_abs = lb.abs().max().item()
-    toks: list[int] = []
+
+    def last_logits(r, tokens, positions):
+        return r.forward(tokens, positions)[:, -1].float()
+
+    la = last_logits(runner, ids, torch.arange(T, device=dev))
+    lb = last_logits(ref, ids, torch.arange(T, device=dev))
+    worst, ref_abs = 0.0, 0.0
+    agreed: list[int] = []
     first, margin = steps, None
     for i in range(steps):
-        a, b = int(la[0].argmax()), int(lb[0].argmax())
-        if a != b:
-            top2 = lb[0].topk(2).values
-            first, margin = i, (top2[0] - top2[1]).item()
-            break
-        toks.append(b)
-        if i + 1 == steps:
-            break
-        tok = torch.tensor([[b]], device=dev)
-        p = torch.tensor([T + i], device=dev)
-        la = runner.forward(tok, p)[:, -1].float()
-        lb = ref.forward(tok, p)[:, -1].float()
-        diff = max(diff, (la - lb).abs().max().item())
+        worst = max(worst, (la - lb).abs().max().item())
         ref_abs = max(ref_abs, lb.abs().max().item())
-    return {"max_abs_logit_diff": diff, "max_abs_ref_logit": ref_abs, "first_divergence": first,
-            "compared_tokens": steps, "ref_margin_at_divergence": margin, "tokens": toks}
+        pick_a, pick_b = int(la[0].argmax()), int(lb[0].argmax())
+        if pick_a != pick_b:
+            top = lb[0].topk(2).values
+            first, margin = i, (top[0] - top[1]).item()
+            break
+        agreed.append(pick_b)
+        if i + 1 < steps:
+            tok = torch.tensor([[pick_b]], device=dev)
+            p = torch.tensor([T + i], device=dev)
+            la, lb = last_logits(runner, tok, p), last_logits(ref, tok, p)
+    return {"max_abs_logit_diff": worst, "max_abs_ref_logit": ref_abs, "first_divergence": first,
+            "compared_tokens": steps, "ref_margin_at_divergence": margin, "tokens": agreed}

@@ -55,9 +55,9 @@ def w8a16_matmul(x, wq, scale, bias=None, config=None):
     (reference kernels/fp8.py:200-223)."""
     K = x.shape[-1]
     N = wq.shape[1]
-    assert wq.shape[0] == K
-    assert tuple(scale.shape) == (N,), f"w8a16_matmul: scale must be [{N}]"
-    assert bias is None or tuple(bias.shape) == (N,), f"w8a16_matmul: bias must be [{N}]"
+    _lib.require_extent(wq.shape[0] == K, f"w8a16_matmul: wq must be [{K}, N]")
+    _lib.require_extent(tuple(scale.shape) == (N,), f"w8a16_matmul: scale must be [{N}]")
+    _lib.require_extent(bias is None or tuple(bias.shape) == (N,), f"w8a16_matmul: bias must be [{N}]")
     _lib.require_cuda("w8a16_matmul", x, wq, scale, bias)
     _lib.require_dtype("w8a16_matmul", torch.float16, x, scale, bias)
     _lib.require_dtype("w8a16_matmul", FP8, wq)

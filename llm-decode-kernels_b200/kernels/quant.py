@@ -21,7 +21,7 @@ PACK = 8  # int4 values per int32 (reference kernels/quant.py:17)
 def pack_int4(q: torch.Tensor) -> torch.Tensor:
     """[K, N] integers in 0..15 -> [K // 8, N] int32 (reference kernels/quant.py:20-28)."""
     K, N = q.shape
-    assert K % PACK == 0, "K must be a multiple of 8"
+    _lib.reference_assert(K % PACK == 0, "K must be a multiple of 8")
     _lib.require_cuda("pack_int4", q)
     q = q.to(torch.int32).contiguous()
     out = torch.empty((K // PACK, N), dtype=torch.int32, device=q.device)
@@ -46,7 +46,7 @@ def quantize_rtn(weight: torch.Tensor, group_size: int = 128):
     Returns (qweight int32 [K/8, N], scales fp16 [K/G, N], zeros fp16 [K/G, N]), bit-exact with the
     reference."""
     N, K = weight.shape
-    assert K % group_size == 0, f"K={K} must be a multiple of group_size={group_size}"
+    _lib.reference_assert(K % group_size == 0, f"K={K} must be a multiple of group_size={group_size}")
     _lib.require_cuda("quantize_rtn", weight)
     _lib.require_dtype("quantize_rtn", torch.float16, weight)
     if weight.stride(1) != 1:

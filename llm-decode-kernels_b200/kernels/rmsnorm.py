@@ -17,9 +17,9 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, residual=N
     shape = x.shape
     N = shape[-1]
     x2 = x.reshape(-1, N)
-    assert x2.stride(-1) == 1 and weight.is_contiguous()
-    assert weight.numel() == N, f"rmsnorm: weight must have {N} elements"
-    assert residual is None or residual.shape == shape, "rmsnorm: residual must have x's shape"
+    _lib.reference_assert(x2.stride(-1) == 1 and weight.is_contiguous())
+    _lib.require_extent(weight.numel() == N, f"rmsnorm: weight must have {N} elements")
+    _lib.require_extent(residual is None or residual.shape == shape, "rmsnorm: residual must have x's shape")
     _lib.require_cuda("rmsnorm", x, weight, residual)
     _lib.require_dtype("rmsnorm", torch.float16, x, weight, residual)
     out = torch.empty_like(x2)

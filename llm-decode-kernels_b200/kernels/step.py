@@ -1,0 +1,144 @@
+"""The fused decode step: one persistent libdecodek kernel per token (dk_step_run).
+
+For the W4A16 runner at batch 1..4 this replaces the ~146 launches of a decode step (five per layer,
+the final norm, the fp16 lm_head, argmax and the bookkeeping) with one cooperative launch: every SM's
+producer warp streams that SM's share of each projection's weights into shared memory ahead of the
+op that needs them, and the ops meet through arrival counters. The step is the reference runner's
+T == 1 forward plus the greedy pick of its graph decoder (kernels/e2e/model.py:216-253,
+kernels/e2e/run.py:69-74) with the numerics of the separate kernels.
+
+The workspace (op table, tensor maps, counters, activations) is a torch uint8 tensor owned by the
+`DecodeStep` object; the model's weights and KV caches are referenced, so the runner must outlive it.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from kernels import _lib
+
+MAX_ROWS = 4
+
+
+def _p(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def supported(runner) -> str | None:
+    """None if the fused step can run this runner, else why not."""
+    be = runner.backend
+    if getattr(be, "name", "") != "ours" or not getattr(be, "fused_decode", False):
+        return f"backend {getattr(be, 'name', be)!r} (the fused step runs the W4A16 'ours' backend)"
+    if runner.tp is not None:
+        return "tensor parallel runner"
+    if runner.batch > MAX_ROWS:
+        return f"batch {runner.batch} > {MAX_ROWS}"
+    if runner.head_q is not None:
+        return "quantized lm_head"
+    if runner.head_dim != 128 or runner.n_heads % runner.n_kv or runner.n_heads // runner.n_kv > 8:
+        return "attention shape"
+    H = runner.embed.shape[1]
+    I = runner.layers[0].down.qweight.shape[0] * 8
+    if H % 256 or I % 256 or (runner.n_heads * 128) % 256 or runner.embed.shape[0] % 32 or runner.max_len % 128:
+        return "layer sizes"
+    if runner.embed.dtype != torch.float16:
+        return "dtype"
+    return None
+
+
+class DecodeStep:
+    """One launch per greedy decode step of `runner` (a QwenRunner on the 'ours' backend)."""
+
+    def __init__(self, runner):
+        why = supported(runner)
+        if why is not None:
+            raise RuntimeError(f"fused decode step unavailable: {why}")
+        self.runner = runner
+        L0 = runner.layers[0]
+        H = runner.embed.shape[1]
+        I = L0.down.qweight.shape[0] * 8
+        self._keep = []  # tensors whose pointers the plan holds
+
+        def keep(t):
+            if t is None:
+                return None
+            t = t.contiguous()
+            self._keep.append(t)
+            return _p(t)
+
+        layers = (_lib.StepLayer * len(runner.layers))()
+        for i, L in enumerate(runner.layers):
+            y = layers[i]
+            y.input_norm, y.post_norm = keep(L.ln1), keep(L.ln2)
+            for name, lin in (("qkv", L.qkv), ("o", L.o), ("gate_up", L.gate_up), ("down", L.down)):
+                setattr(y, f"{name}_qweight", keep(lin.qweight))
+                setattr(y, f"{name}_scales", keep(lin.scales))
+                setattr(y, f"{name}_zeros", keep(lin.zeros))
+                setattr(y, f"{name}_bias", keep(lin.bias))
+        self._layers = layers
+        m = _lib.StepModel()
+        m.n_layers = len(runner.layers)
+        m.hidden = H
+        m.n_heads = runner.n_heads
+        m.n_kv = runner.n_kv
+        m.head_dim = runner.head_dim
+        m.intermediate = I
+        m.vocab = runner.embed.shape[0]
+        m.max_len = runner.max_len
+        m.batch = runner.batch
+        m.eps = float(runner.eps)
+        m.embed = keep(runner.embed)
+        m.final_norm = keep(runner.final_norm)
+        m.lm_head = keep(runner.lm_head)
+        m.rope_cos = keep(runner.rope_cos)
+        m.rope_sin = keep(runner.rope_sin)
+        for c in (runner.k_cache, runner.v_cache):
+            if not c.is_contiguous():
+                raise RuntimeError("fused decode step: the KV caches must be contiguous")
+        m.k_cache = _p(runner.k_cache)
+        m.v_cache = _p(runner.v_cache)
+        m.layers = ctypes.cast(layers, ctypes.POINTER(_lib.StepLayer))
+        self._model = m
+        nbytes = ctypes.c_uint64(0)
+        _lib.call("dk_step_workspace_bytes", ctypes.byref(m), ctypes.byref(nbytes))
+        # 256-byte aligned workspace from the caching allocator (its blocks are 512-byte aligned)
+        self.workspace = torch.zeros(int(nbytes.value), dtype=torch.uint8, device=runner.embed.device)
+        plan = ctypes.c_void_p()
+        _lib.call("dk_step_create", ctypes.byref(m), _p(self.workspace), nbytes.value, ctypes.byref(plan))
+        self._plan = plan
+
+    def __call__(self, tok: torch.Tensor, pos: torch.Tensor, hist: torch.Tensor | None = None,
+                 logits: torch.Tensor | None = None) -> None:
+        """tok int64 [B] or [B, 1] (in: this step's tokens; out: the greedy picks), pos int64 [1]
+        (incremented), hist int64 [B, >= max_len] or None (hist[:, pos] = pick), logits fp16 [B, vocab]
+        or None. Everything stays on the device (graph-capturable)."""
+        r = self.runner
+        B = r.batch
+        if tok.numel() != B or tok.dtype != torch.int64 or not tok.is_contiguous():
+            raise ValueError(f"fused decode step: tok must be a contiguous int64 tensor of {B} tokens")
+        if pos.numel() < 1 or pos.dtype != torch.int64:
+            raise ValueError("fused decode step: pos must be an int64 tensor holding the position")
+        ld = 0
+        if hist is not None:
+            if hist.dtype != torch.int64 or hist.dim() != 2 or hist.shape[0] != B or hist.stride(1) != 1 \
+                    or hist.shape[1] < r.max_len:
+                raise ValueError(f"fused decode step: hist must be int64 [{B}, >= {r.max_len}] with unit stride")
+            ld = hist.stride(0)
+        if logits is not None and (logits.dtype != torch.float16 or tuple(logits.shape) != (B, r.embed.shape[0])
+                                   or not logits.is_contiguous()):
+            raise ValueError("fused decode step: logits must be a contiguous fp16 [batch, vocab] tensor")
+        _lib.require_cuda("decode step", tok, pos, hist, logits)
+        _lib.call("dk_step_run", self._plan, _p(tok), _p(pos), _p(hist), ld, _p(logits), _lib.stream_of(tok))
+
+    def close(self):
+        if self._plan is not None and self._plan.value:
+            _lib.call("dk_step_destroy", self._plan)
+            self._plan = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

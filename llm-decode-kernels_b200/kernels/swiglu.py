@@ -12,7 +12,7 @@ from kernels import _lib
 
 def _launch(gate2: torch.Tensor, up2: torch.Tensor) -> torch.Tensor:
     M, I = gate2.shape
-    assert gate2.stride(-1) == 1 and up2.stride(-1) == 1
+    _lib.reference_assert(gate2.stride(-1) == 1 and up2.stride(-1) == 1)
     _lib.require_cuda("swiglu", gate2, up2)
     _lib.require_dtype("swiglu", torch.float16, gate2, up2)
     out = torch.empty((M, I), dtype=gate2.dtype, device=gate2.device)
@@ -23,7 +23,7 @@ def _launch(gate2: torch.Tensor, up2: torch.Tensor) -> torch.Tensor:
 
 def swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     """silu(gate) * up for two same-shape tensors (reference kernels/swiglu.py:49-53)."""
-    assert gate.shape == up.shape, "swiglu: gate and up must have the same shape"
+    _lib.require_extent(gate.shape == up.shape, "swiglu: gate and up must have the same shape")
     I = gate.shape[-1]
     out = _launch(gate.reshape(-1, I), up.reshape(-1, I))
     return out.view(gate.shape)

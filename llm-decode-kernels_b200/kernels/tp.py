@@ -198,7 +198,7 @@ def w4a16_matmul_allreduce(x, qweight, scales, zeros, comm: TPComm, group_size=1
 
     K = x.shape[-1]
     N = qweight.shape[1]
-    assert qweight.shape[0] * 8 == K and K % group_size == 0
+    _lib.reference_assert(qweight.shape[0] * 8 == K and K % group_size == 0)
     _check_weight_shapes("w4a16_matmul_allreduce", K, N, scales, zeros, group_size, bias)
     _lib.require_cuda("w4a16_matmul_allreduce", x, qweight, scales, zeros, bias)
     _lib.require_dtype("w4a16_matmul_allreduce", torch.float16, x, scales, zeros, bias)

@@ -41,9 +41,10 @@ def _check_weight_shapes(what, K, N, scales, zeros, group_size, bias):
     """The packed weight's scales / zeros are [K/group_size, N] and the bias [N]: the kernels read
     exactly those extents, so a smaller tensor would be read past its end."""
     g = K // group_size
-    assert tuple(scales.shape) == (g, N) and tuple(zeros.shape) == (g, N), (
-        f"{what}: scales and zeros must be [{g}, {N}], got {tuple(scales.shape)} and {tuple(zeros.shape)}")
-    assert bias is None or tuple(bias.shape) == (N,), f"{what}: bias must be [{N}]"
+    _lib.require_extent(tuple(scales.shape) == (g, N) and tuple(zeros.shape) == (g, N),
+                        f"{what}: scales and zeros must be [{g}, {N}], got {tuple(scales.shape)} and "
+                        f"{tuple(zeros.shape)}")
+    _lib.require_extent(bias is None or tuple(bias.shape) == (N,), f"{what}: bias must be [{N}]")
 
 
 def _config(config: dict | None) -> _lib.MatmulConfig:
@@ -78,7 +79,7 @@ def w4a16_matmul(x, qweight, scales, zeros, group_size=128, bias=None, config=No
     """y = x @ dequant(W).T (+ bias). x: [..., K] fp16. Returns [..., N] in x's dtype."""
     K = x.shape[-1]
     N = qweight.shape[1]
-    assert qweight.shape[0] * 8 == K and K % group_size == 0
+    _lib.reference_assert(qweight.shape[0] * 8 == K and K % group_size == 0)
     _check_weight_shapes("w4a16_matmul", K, N, scales, zeros, group_size, bias)
     _lib.require_cuda("w4a16_matmul", x, qweight, scales, zeros, bias)
     _lib.require_dtype("w4a16_matmul", torch.float16, x, scales, zeros, bias)
@@ -108,7 +109,8 @@ def w4a16_swiglu(x, qweight, scales, zeros, group_size=128, bias=None, config=No
     (I % 32 != 0, other group sizes, unaligned operands) run the two kernels instead."""
     K = x.shape[-1]
     N = qweight.shape[1]
-    assert qweight.shape[0] * 8 == K and K % group_size == 0 and N % 2 == 0
+    _lib.reference_assert(qweight.shape[0] * 8 == K and K % group_size == 0)
+    _lib.require_extent(N % 2 == 0, "w4a16_swiglu: the fused [gate; up] weight needs an even column count")
     _check_weight_shapes("w4a16_swiglu", K, N, scales, zeros, group_size, bias)
     I = N // 2
     _lib.require_cuda("w4a16_swiglu", x, qweight, scales, zeros, bias)
@@ -144,10 +146,10 @@ def w4a16_rmsnorm_matmul(x, norm_weight, eps, residual, qweight, scales, zeros, 
     fast path; shapes it does not cover run rmsnorm and the projection separately."""
     K = x.shape[-1]
     N = qweight.shape[1]
-    assert qweight.shape[0] * 8 == K and K % group_size == 0
+    _lib.reference_assert(qweight.shape[0] * 8 == K and K % group_size == 0)
     _check_weight_shapes("w4a16_rmsnorm_matmul", K, N, scales, zeros, group_size, bias)
-    assert norm_weight.numel() == K, f"w4a16_rmsnorm_matmul: norm_weight must have {K} elements"
-    assert residual is None or residual.shape == x.shape, "w4a16_rmsnorm_matmul: residual must match x"
+    _lib.require_extent(norm_weight.numel() == K, f"w4a16_rmsnorm_matmul: norm_weight must have {K} elements")
+    _lib.require_extent(residual is None or residual.shape == x.shape, "w4a16_rmsnorm_matmul: residual must match x")
     _lib.require_cuda("w4a16_rmsnorm_matmul", x, residual, norm_weight, qweight, scales, zeros, bias)
     _lib.require_dtype("w4a16_rmsnorm_matmul", torch.float16, x, residual, norm_weight, scales, zeros, bias)
     x2 = x.reshape(-1, K)
