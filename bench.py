@@ -49,8 +49,10 @@ def parse():
     ap.add_argument("--l2-prefetch", action="store_true",
                     help="runner with cross-launch L2 prefetch of the next projections' weights")
     ap.add_argument("--tp7b", choices=["auto", "on", "off"], default="auto",
-                    help="Qwen2.5-7B tensor-parallel decode over the N ranks (BASELINE configs[4]); "
-                         "auto = on when N > 1")
+                    help="Qwen2.5-7B tensor-parallel decode over the N ranks (BASELINE configs[4], TP=1 at N=1); "
+                         "auto = on unless --no-extras")
+    ap.add_argument("--per-op", action="store_true",
+                    help="run the decode step as the per-op kernels instead of the fused decode-step kernel")
     ap.add_argument("--tp-batches", default="1,8,32", help="batch sizes of the 7B tensor-parallel decode")
     return ap.parse_args()
 
@@ -200,6 +202,84 @@ def time_decode(dec, ids, steps: int, warmup: int, world: int) -> float:
     torch.cuda.synchronize()
     barrier(world)
     return start.elapsed_time(end) / 1e3
+
+
+def step_bytes(runner, pos: float) -> float:
+    """Algorithmic bytes of one greedy decode step at cache position `pos` (every weight once, the
+    KV-cache rows 0..pos once): packed linears with scales, zeros and biases, the fp16 lm_head, the
+    RMSNorm weights, the batch's embedding rows, K and V rows read (pos + 1 per sequence, kv head and
+    layer) and written (one each), and the RoPE rows. Activations between ops stay on chip or in L2
+    and are not counted."""
+    B, L, H = runner.batch, len(runner.layers), runner.embed.shape[1]
+    wb = runner.weight_bytes()
+    kv_row = runner.head_dim * 2
+    kv = 2 * L * B * runner.n_kv * kv_row * (pos + 1 + 1)
+    norms = (2 * L + 1) * H * 2
+    return wb["linear_layers"] + wb["lm_head_read"] + norms + B * H * 2 + kv + 2 * kv_row
+
+
+def step_roofline(runner, sec_per_step: float, first_pos: int, steps: int, peak_gbs: float) -> dict:
+    """The dominant kernel: the fused decode step (decode_step_kernel, one launch per token, the whole
+    step). achieved = algorithmic bytes of a step (at the mean position of the timed steps) / the
+    measured time per step (CUDA events around the timed graph replays, one launch each, so the
+    launch-to-launch gap is counted against the kernel)."""
+    pos = first_pos + (steps - 1) / 2
+    byts = step_bytes(runner, pos)
+    achieved = byts / sec_per_step / 1e9
+    return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
+            "frac": round(achieved / peak_gbs, 4), "traffic": step_traffic(),
+            "kernel": "decode_step_kernel (fused greedy decode step, 1 launch per token)",
+            "bytes_per_launch": round(byts), "us_per_launch": round(sec_per_step * 1e6, 3),
+            "mean_position": pos}
+
+
+def step_traffic():
+    """DRAM bytes per launch of the fused step from the committed ncu summary of the same workload."""
+    f = ROOT / "profiles" / "decode_step_kernel_traffic.json"
+    try:
+        return json.loads(f.read_text())["dram_bytes_per_launch"]
+    except Exception:
+        return None
+
+
+def parity_on_benchmark_model(model, ids, steps: int = 32) -> dict:
+    """The north star's greedy-stream bar on the benchmark model itself: `steps` greedy tokens of the
+    fused step against the reference numerics (w4_ref: dequantize, cuBLAS fp16, SDPA), with the
+    reference's parity figures (kernels/e2e/run.py:289-303)."""
+    from kernels.e2e.model import QwenRunner, make_backend
+    from kernels.e2e.run import greedy_parity
+    from kernels.step import StepLogits
+
+    ours = QwenRunner(model, make_backend("ours"), max_len=MAX_LEN)
+    ref = QwenRunner(model, make_backend("w4_ref"), max_len=MAX_LEN, fused_step=False)
+    r = greedy_parity(StepLogits(ours), ref, ids[:1], steps=steps)
+    del ours, ref
+    torch.cuda.empty_cache()
+    tol = 5e-2 + 5e-2 * r["max_abs_ref_logit"]
+    ok = r["max_abs_logit_diff"] <= tol and (r["first_divergence"] == steps or r["ref_margin_at_divergence"] <= 2 * tol)
+    return {"vs": "w4_ref (reference numerics)", "steps": steps, "prompt": ids.shape[1],
+            "max_abs_logit_diff": round(r["max_abs_logit_diff"], 5), "max_abs_ref_logit": round(r["max_abs_ref_logit"], 3),
+            "first_divergence": r["first_divergence"], "ref_margin_at_divergence": r["ref_margin_at_divergence"],
+            "tolerance": round(tol, 4), "pass": bool(ok)}
+
+
+def decode_variant(model, backend: str, batch: int, steps: int, warmup: int, fused: bool = True,
+                   l2_prefetch: bool = False) -> dict:
+    """tok/s of another configs[3] variant on the same model (same prompt method, graph decoder)."""
+    from kernels.e2e.model import QwenRunner, make_backend
+    from kernels.e2e.run import GraphDecoder
+
+    runner = QwenRunner(model, make_backend(backend), max_len=MAX_LEN, batch=batch, fused_step=fused,
+                        l2_prefetch=l2_prefetch)
+    ids = prompt_ids(model.config.vocab_size, batch)
+    dec = GraphDecoder(runner)
+    dec.capture(ids)
+    sec = time_decode(dec, ids, steps, warmup, 1)
+    path = "fused step" if runner.step_kernel() is not None else "per-op kernels"
+    del dec, runner
+    torch.cuda.empty_cache()
+    return {"backend": backend, "batch": batch, "path": path, "l2_prefetch": l2_prefetch,
+            "tok_s": round(batch * steps / sec, 1), "ms_per_step": round(sec / steps * 1e3, 4)}
 
 
 def gemv_roofline(runner, peak_gbs: float) -> dict:
@@ -429,13 +509,14 @@ def cpu_gemv_baseline(N: int = 17920, K: int = 1536, calls: int = 5) -> dict:
 
 
 def oracle_weights(model) -> dict:
-    """Packed int4 weights for the CPU oracle, quantized by libdecodek on the GPU (bit-exact with the
-    oracle's quantizer, tests/test_quant.py) to keep the setup short, then moved to the host."""
-    from kernels.quant import quantize_rtn
+    """Packed int4 weights for the CPU oracle, quantized by the oracle's own torch restatement of the
+    reference's RTN quantizer (oracle/torch_ref.py, kernels/quant.py:38-49) on the tensors' device,
+    then moved to the host: the reference arm never loads libdecodek."""
+    from oracle import torch_ref
 
     def q(*mods):
         w = torch.cat([mm.weight.data for mm in mods], 0)
-        qw, s, z = quantize_rtn(w, 128)
+        qw, s, z = torch_ref.quantize_rtn(w, 128)
         return (qw.cpu().numpy(), s.cpu().numpy(), z.cpu().numpy())
 
     def npy(t):
@@ -493,13 +574,15 @@ def run_ours(args, world, rank, local):
     peaks = config.peaks()
     model = build_model(args.batch)
     ids = prompt_ids(model.config.vocab_size, args.batch)
-    assert PROMPT + args.warmup + args.steps + 8 < MAX_LEN, "steps + warmup exceed the cache"
+    warmup = max(args.warmup, 3)
+    assert PROMPT + warmup + args.steps + 8 < MAX_LEN, "steps + warmup exceed the cache"
     runner = QwenRunner(model, make_backend(args.backend), max_len=MAX_LEN, batch=args.batch,
-                        l2_prefetch=args.l2_prefetch)
+                        l2_prefetch=args.l2_prefetch, fused_step=not args.per_op)
     dec = GraphDecoder(runner)
     dec.capture(ids)
+    fused = runner.step_kernel() is not None
     with ClockSampler(local) as clocks:
-        sec = time_decode(dec, ids, args.steps, max(args.warmup, 3), world)
+        sec = time_decode(dec, ids, args.steps, warmup, world)
     sec = max_over_ranks(sec, world)
     value = world * args.batch * args.steps / sec
 
@@ -517,9 +600,14 @@ def run_ours(args, world, rank, local):
     e2e_value = world * args.batch * args.steps / e2e_sec
 
     extras = {}
-    if not args.no_extras:
+    if fused:
+        roof = step_roofline(runner, sec / args.steps, PROMPT + warmup, args.steps, peaks["hbm_gbs"])
+    else:
         roof = gemv_roofline(runner, peaks["hbm_gbs"])
-        extras["roofline"] = {**roof, "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs, copy bandwidth)"}
+    extras["roofline"] = {**roof, "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs, copy bandwidth)"}
+    if not args.no_extras:
+        if fused:  # the per-op path's dominant kernel, for comparison with earlier measurements
+            extras["gemv_chain"] = gemv_roofline(runner, peaks["hbm_gbs"])
         if rank == 0:
             extras["gemv_sweep"] = gemv_sweep(peaks["hbm_gbs"])
         # fp16 cuBLAS baseline runner (the reference's fp16 backend) on the same model
@@ -534,31 +622,50 @@ def run_ours(args, world, rank, local):
         del bdec, base_runner
         torch.cuda.empty_cache()
         if world == 1 and rank == 0:
+            extras["parity"] = parity_on_benchmark_model(model, ids)
+            variants = []
+            for kw in ({"backend": "ours", "batch": 1, "fused": False},
+                       {"backend": "ours", "batch": 1, "fused": False, "l2_prefetch": True},
+                       {"backend": "ours", "batch": 4},
+                       {"backend": "ours", "batch": 16},
+                       {"backend": "ours_fp8", "batch": 1},
+                       {"backend": "ours_fp8", "batch": 16},
+                       {"backend": "ours_lm", "batch": 1}):
+                try:
+                    variants.append(decode_variant(model, steps=args.steps, warmup=warmup, **kw))
+                except Exception as e:  # recorded, not hidden
+                    variants.append({**kw, "error": f"{type(e).__name__}: {e}"[:200]})
+            extras["variants"] = variants
             extras["cpu_baseline"] = cpu_decode_rate(model, steps=4)
             try:
                 extras["cpu_gemv_baseline"] = cpu_gemv_baseline()
             except Exception as e:  # informational: never costs the benchmark line
                 extras["cpu_gemv_baseline"] = {"error": f"{type(e).__name__}: {e}"[:200]}
     assert _lib.device_error() == 0, "a kernel recorded a device-side error"
-    if args.tp7b == "on" or (args.tp7b == "auto" and world > 1):
+    if args.tp7b == "on" or (args.tp7b == "auto" and not args.no_extras):
         del dec, runner
         torch.cuda.empty_cache()
         extras["tp7b"] = run_tp7b(args, world, rank)
     if not args.no_extras and world == 1 and rank == 0:
         torch.cuda.empty_cache()
         extras["layer_sweep"] = layer_sweep(peaks)
-    # our kernels per token: per layer norm+qkv, attention, o_proj, norm+gate_up+SwiGLU, down (FP8:
-    # separate norm and SwiGLU kernels, 8 per layer), then the final norm and a quantized lm_head
-    per_layer = 8 if args.backend.startswith("ours_fp8") else 5
-    per_step_launches = per_layer * 28 + 1 + (1 if args.backend.endswith("_lm") else 0)
+    # our kernels per token: the fused step is one launch; the per-op path runs per layer norm+qkv,
+    # attention, o_proj, norm+gate_up+SwiGLU, down (FP8: separate norm and SwiGLU kernels, 8 per
+    # layer), then the final norm and a quantized lm_head
+    if fused:
+        per_step_launches = 1
+    else:
+        per_layer = 8 if args.backend.startswith("ours_fp8") else 5
+        per_step_launches = per_layer * 28 + 1 + (1 if args.backend.endswith("_lm") else 0)
     if rank != 0:
         return None
     metric = METRIC if args.batch == 1 else METRIC.replace("batch 1", f"batch {args.batch}")
     return {"metric": metric, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": max(args.warmup, 3), "ms_per_step": round(sec / args.steps * 1e3, 4), "higher_is_better": True,
+            "warmup": warmup, "ms_per_step": round(sec / args.steps * 1e3, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "w4a16 (fp16 activations, int4 weights, fp32 accumulation)",
             "data": "synthetic (random-init weights, uniform random prompt ids)",
-            "config": workload_config(args, world), **extras,
+            "config": {**workload_config(args, world), "path": "fused decode step" if fused else "per-op kernels"},
+            **extras,
             "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": 8 * args.batch,
                     "d2h_bytes_per_step": 8 * args.batch,
                     "what": "GraphDecoder.step_host: pinned-host token -> device, graph replay, next token -> host, "

@@ -288,6 +288,10 @@ int dk_tp_buffer_close(void* ptr);
 int dk_tp_comm_create(dk_tp_comm** comm, int32_t rank, int32_t world, void* const* bufs, int64_t max_m,
                       int64_t max_n);
 int dk_tp_comm_destroy(dk_tp_comm* comm);
+/* Bound of each wait of a fused-allreduce launch on this communicator for a peer's partial sums:
+ * 1 ms .. 10 s (default 2 s). A CTA whose wait runs out leaves its columns of y unwritten, sets
+ * DK_DEVERR_TP_WAIT and returns, so a rank that never launches cannot hang the others' kernels. */
+int dk_tp_comm_set_wait(dk_tp_comm* comm, uint64_t wait_ns);
 
 /* Row-sharded w4a16_matmul with the allreduce fused in:
  *   y[M, N] = fp16( sum over ranks r, in rank order, of x_r[M, K] @ dequant(W_r).T  + bias )

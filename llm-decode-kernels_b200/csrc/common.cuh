@@ -189,6 +189,7 @@ struct TPArgs {
   unsigned long long* epoch;         // this rank's header
   unsigned int* arrive;
   int rank, world, max_m, max_n;
+  uint64_t wait_ns;  // bound of each wait for a peer's partial sums (0: kWaitLimitNs)
 };
 
 __device__ __forceinline__ void st_volatile_v4(uint32_t* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {

@@ -14,6 +14,7 @@
 struct dk_tp_comm {
   int rank, world;
   int64_t max_m, max_n;
+  uint64_t wait_ns;
   void* bufs[DK_TP_MAX_WORLD];
 };
 
@@ -31,6 +32,7 @@ bool tp_args_from(const dk_tp_comm* c, TPArgs* a) {
   a->world = c->world;
   a->max_m = static_cast<int>(c->max_m);
   a->max_n = static_cast<int>(c->max_n);
+  a->wait_ns = c->wait_ns;
   return true;
 }
 
@@ -114,8 +116,19 @@ int dk_tp_comm_create(dk_tp_comm** comm, int32_t rank, int32_t world, void* cons
   c->world = world;
   c->max_m = max_m;
   c->max_n = max_n;
+  c->wait_ns = kWaitLimitNs;
   for (int q = 0; q < world; ++q) c->bufs[q] = bufs[q];
   *comm = c;
+  return DK_OK;
+}
+
+int dk_tp_comm_set_wait(dk_tp_comm* comm, uint64_t wait_ns) {
+  using namespace dk;
+  if (comm == nullptr) return set_error(DK_ERR_INVALID, "dk_tp_comm_set_wait: comm is NULL");
+  if (wait_ns < 1000000ull || wait_ns > 10000000000ull)
+    return set_error(DK_ERR_INVALID, "dk_tp_comm_set_wait: the bound must be 1 ms .. 10 s (got %llu ns)",
+                     (unsigned long long)wait_ns);
+  comm->wait_ns = wait_ns;
   return DK_OK;
 }
 

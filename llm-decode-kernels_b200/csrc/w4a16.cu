@@ -239,11 +239,12 @@ __device__ __forceinline__ void tp_push4(const TPArgs& tp, unsigned long long ep
 
 // Bounded polling: false once the CTA gave up (another thread timed out) or this wait passed the
 // limit (then it records the device error and makes the CTA give up).
-__device__ __forceinline__ bool tp_keep_waiting(int it, uint64_t& t0, volatile int* give_up, int* err) {
+__device__ __forceinline__ bool tp_keep_waiting(int it, uint64_t& t0, volatile int* give_up, int* err,
+                                                uint64_t limit) {
   if (*give_up) return false;
   if (it == 0) {
     t0 = globaltimer_ns();
-  } else if ((it & 63) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+  } else if ((it & 63) == 0 && globaltimer_ns() - t0 > (limit ? limit : kWaitLimitNs)) {
     record_device_error(err, DK_DEVERR_TP_WAIT);
     *give_up = 1;
     return false;
@@ -253,7 +254,7 @@ __device__ __forceinline__ bool tp_keep_waiting(int it, uint64_t& t0, volatile i
 
 // The four values of cells c[0..3] (32 bytes) once all four carry `tag`.
 __device__ __forceinline__ bool tp_poll4(const uint32_t* c, uint32_t tag, float (&out)[4], volatile int* give_up,
-                                         int* err) {
+                                         int* err, uint64_t limit) {
   uint64_t t0 = 0;
   for (int it = 0;; ++it) {
     const uint4 a = ld_volatile_v4(c), b = ld_volatile_v4(c + 4);
@@ -264,11 +265,12 @@ __device__ __forceinline__ bool tp_poll4(const uint32_t* c, uint32_t tag, float 
       out[3] = __uint_as_float(b.z);
       return true;
     }
-    if (!tp_keep_waiting(it, t0, give_up, err)) return false;
+    if (!tp_keep_waiting(it, t0, give_up, err, limit)) return false;
   }
 }
 
-__device__ __forceinline__ bool tp_poll1(const uint32_t* c, uint32_t tag, float& out, volatile int* give_up, int* err) {
+__device__ __forceinline__ bool tp_poll1(const uint32_t* c, uint32_t tag, float& out, volatile int* give_up, int* err,
+                                         uint64_t limit) {
   uint64_t t0 = 0;
   for (int it = 0;; ++it) {
     const uint2 a = ld_volatile_v2(c);
@@ -276,7 +278,7 @@ __device__ __forceinline__ bool tp_poll1(const uint32_t* c, uint32_t tag, float&
       out = __uint_as_float(a.x);
       return true;
     }
-    if (!tp_keep_waiting(it, t0, give_up, err)) return false;
+    if (!tp_keep_waiting(it, t0, give_up, err, limit)) return false;
   }
 }
 
@@ -300,7 +302,7 @@ __device__ void tp_finish(const GemvParams& p, unsigned long long ep, bool ok, i
         bool good = true;
         for (int q = 0; q < tp.world && good; ++q) {
           float v[4];
-          good = tp_poll4(tp_cell(tp, tp.rank, ep, q, m, n), tag, v, give_up, p.err);
+          good = tp_poll4(tp_cell(tp, tp.rank, ep, q, m, n), tag, v, give_up, p.err, tp.wait_ns);
 #pragma unroll
           for (int c = 0; c < 4; ++c) sum[c] += v[c];
         }
@@ -321,7 +323,7 @@ __device__ void tp_finish(const GemvParams& p, unsigned long long ep, bool ok, i
         bool good = true;
         for (int q = 0; q < tp.world && good; ++q) {
           float v = 0.f;
-          good = tp_poll1(tp_cell(tp, tp.rank, ep, q, m, n), tag, v, give_up, p.err);
+          good = tp_poll1(tp_cell(tp, tp.rank, ep, q, m, n), tag, v, give_up, p.err, tp.wait_ns);
           a += v;
         }
         if (!good) continue;

@@ -86,6 +86,7 @@ SIGNATURES = {
     "dk_tp_buffer_close": [P],
     "dk_tp_comm_create": [ctypes.POINTER(P), I32, I32, ctypes.POINTER(P), I64, I64],
     "dk_tp_comm_destroy": [P],
+    "dk_tp_comm_set_wait": [P, ctypes.c_uint64],
     "dk_w4a16_matmul_allreduce": [P, I64, P, P, P, P, P, I64, I64, I64, I64, I64, ctypes.POINTER(MatmulConfig), P,
                                   P],
     "dk_w4a16_matmul_reduce_static": [P, I64, P, P, P, P, P, I64, I64, I64, I64, I64, ctypes.POINTER(MatmulConfig),

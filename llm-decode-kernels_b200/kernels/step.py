@@ -142,3 +142,27 @@ class DecodeStep:
             self.close()
         except Exception:
             pass
+
+
+class StepLogits:
+    """A runner-like view (`forward(tokens, pos)`, `greedy`) whose one-token forward is the fused
+    step's logits, for parity checks (kernels.e2e.run.greedy_parity): prompts go through the runner's
+    own forward; a single token runs the step kernel on copies of the token and position, so the
+    caller's state is not advanced."""
+
+    def __init__(self, runner):
+        self.r = runner
+        self.kernel = runner.step_kernel()
+        if self.kernel is None:
+            raise RuntimeError("fused decode step unavailable for this runner")
+        self.logits = torch.empty(runner.batch, runner.embed.shape[0], dtype=torch.float16,
+                                  device=runner.embed.device)
+
+    def forward(self, tokens: torch.Tensor, pos: torch.Tensor, all_logits: bool = False):
+        if tokens.shape[1] > 1:
+            return self.r.forward(tokens, pos, all_logits)
+        self.kernel(tokens.clone().contiguous(), pos.clone(), None, self.logits)
+        return self.logits.view(self.r.batch, 1, -1)
+
+    def greedy(self, logits):
+        return self.r.greedy(logits)

@@ -143,24 +143,10 @@ def test_step_greedy_stream_on_benchmark_model():
     from kernels import config
     from kernels.e2e.model import QwenRunner, make_backend, random_qwen2
     from kernels.e2e.run import greedy_parity
+    from kernels.step import StepLogits
 
     model = random_qwen2(config.QWEN15, dtype=torch.float16, device="cuda", seed=0)
     ids = torch.randint(0, config.QWEN15["vocab_size"], (1, 512), generator=torch.Generator().manual_seed(1)).cuda()
-
-    class FusedSteps:
-        """greedy_parity's runner interface over the fused step: forward() of one token returns the
-        step kernel's logits (the prompt goes through the runner's own forward)."""
-
-        def __init__(self, runner):
-            self.r = runner
-            self.logits = torch.empty(1, runner.embed.shape[0], dtype=torch.float16, device="cuda")
-
-        def forward(self, tokens, pos):
-            if tokens.shape[1] > 1:
-                return self.r.forward(tokens, pos)
-            tok = tokens.clone().contiguous()
-            self.r.step_kernel()(tok, pos.clone(), None, self.logits)
-            return self.logits.view(1, 1, -1)
 
     fused = QwenRunner(model, make_backend("ours"), max_len=2048)
     assert fused.step_kernel() is not None
@@ -168,7 +154,7 @@ def test_step_greedy_stream_on_benchmark_model():
         ref = QwenRunner(model, make_backend(ref_name), max_len=2048, fused_step=False)
         fused.k_cache.zero_()
         fused.v_cache.zero_()
-        r = greedy_parity(FusedSteps(fused), ref, ids, steps=32)
+        r = greedy_parity(StepLogits(fused), ref, ids, steps=32)
         tol = DECODE_TOL + DECODE_TOL * r["max_abs_ref_logit"]
         assert r["max_abs_logit_diff"] <= tol, (ref_name, r)
         if r["first_divergence"] < 32:

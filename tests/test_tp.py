@@ -292,6 +292,65 @@ def _fused_worker(rank, world, port, q):
 
 
 @pytest.mark.gpu
+def test_allreduce_wait_runs_out_when_the_peer_never_launches():
+    """The fused allreduce's bounded wait, made to run out on ONE GPU with no second process: a
+    world-2 communicator whose rank-1 buffer is a second local buffer that no kernel ever pushes
+    into (a peer that never launches). With the bound set to 50 ms through the C ABI, every CTA
+    gives up waiting for rank 1's partial sums, leaves its columns unwritten, records
+    DK_DEVERR_TP_WAIT and returns; the context stays usable for the next launch."""
+    import ctypes
+    import time
+
+    from _util import to_cuda, w4_case
+    from kernels import _lib
+    from kernels.tp import TPComm, w4a16_matmul_allreduce
+
+    lib = _lib.lib()
+    N, K = 1024, 512
+    nbytes = ctypes.c_uint64(0)
+    _lib.check(lib.dk_tp_buffer_bytes(2, 16, N, ctypes.byref(nbytes)), "tp_buffer_bytes")
+    bufs = [ctypes.c_void_p(), ctypes.c_void_p()]
+    for b in bufs:
+        _lib.check(lib.dk_tp_buffer_alloc(nbytes.value, ctypes.byref(b), ctypes.create_string_buffer(64)), "alloc")
+    comm = ctypes.c_void_p()
+    try:
+        ptrs = (ctypes.c_void_p * 2)(bufs[0].value, bufs[1].value)
+        _lib.check(lib.dk_tp_comm_create(ctypes.byref(comm), 0, 2, ptrs, 16, N), "comm_create")
+        assert lib.dk_tp_comm_set_wait(comm, 100) == -1  # below 1 ms: rejected
+        _lib.check(lib.dk_tp_comm_set_wait(comm, 50_000_000), "comm_set_wait")
+
+        class Comm:
+            handle = comm
+
+        x, qw, s, z = to_cuda(*w4_case(2, N, K, seed=11)[:4])
+        _lib.clear_device_error()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        y = w4a16_matmul_allreduce(x, qw, s, z, Comm)
+        err = _lib.device_error()  # synchronizes: the launch has returned
+        elapsed = time.perf_counter() - t0
+        assert err == 4, err  # DK_DEVERR_TP_WAIT
+        assert elapsed < 5.0, elapsed
+        del y  # its columns were left unwritten
+        _lib.clear_device_error()
+    finally:
+        if comm.value:
+            lib.dk_tp_comm_destroy(comm)
+        for b in bufs:
+            lib.dk_tp_buffer_free(b)
+    # the context still runs kernels: a one-rank communicator gives the plain matmul's result
+    one = TPComm(max_n=N)
+    try:
+        from kernels.w4a16 import w4a16_matmul
+
+        torch.testing.assert_close(w4a16_matmul_allreduce(x, qw, s, z, one), w4a16_matmul(x, qw, s, z),
+                                   rtol=0, atol=0)
+    finally:
+        one.close()
+    assert _lib.device_error() == 0
+
+
+@pytest.mark.gpu
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_allreduce_world2_matches_unsharded():
     """Two processes on two GPUs, each with half of K: both get the unsharded matmul (within the
