@@ -258,6 +258,18 @@ int dk_step_create(const dk_step_model* model, void* workspace, uint64_t bytes, 
 int dk_step_run(const dk_step_plan* plan, int64_t* tokens, int64_t* pos, int64_t* history, int64_t history_ld,
                 void* logits, dk_stream_t stream);
 int dk_step_destroy(dk_step_plan* plan);
+/* Diagnostics. dk_step_trace runs dk_step_run and also records, per CTA and op of the program,
+ * %globaltimer nanoseconds [wait start, input ready, input staged, products done, work done, arrival]
+ * and clock cycles [most cycles a warp waited for its weights, one L2 load of the fresh input, the
+ * release fence before the arrival, 0, 0, 0] (zero where the CTA has no part in the op; attention
+ * records no staged / products stamps) and, in the slot after the last op, [kernel start, kernel end],
+ * into `trace` (device memory of dk_step_trace_bytes, 8-byte aligned; [grid][n_ops + 1][12] uint64).
+ * dk_step_ops gives the
+ * program's op kinds (1 qkv, 2 attention, 3 o_proj, 4 gate_up + SwiGLU, 5 down, 6 lm_head + argmax). */
+int dk_step_trace_bytes(const dk_step_plan* plan, uint64_t* bytes);
+int dk_step_trace(const dk_step_plan* plan, int64_t* tokens, int64_t* pos, int64_t* history, int64_t history_ld,
+                  void* logits, uint64_t* trace, dk_stream_t stream);
+int dk_step_ops(const dk_step_plan* plan, int32_t* kinds, int32_t capacity, int32_t* n_ops);
 
 /* ---- tensor parallelism: row-sharded W4A16 projection fused with its allreduce ------------
  * No reference counterpart: the reference runs on one GPU (README.md:249). These entry points serve

@@ -95,6 +95,9 @@ SIGNATURES = {
     "dk_step_create": [ctypes.POINTER(StepModel), P, ctypes.c_uint64, ctypes.POINTER(P)],
     "dk_step_run": [P, P, P, P, I64, P, P],
     "dk_step_destroy": [P],
+    "dk_step_trace_bytes": [P, ctypes.POINTER(ctypes.c_uint64)],
+    "dk_step_trace": [P, P, P, P, I64, P, P, P],
+    "dk_step_ops": [P, ctypes.POINTER(I32), I32, ctypes.POINTER(I32)],
 }
 
 _lib = None

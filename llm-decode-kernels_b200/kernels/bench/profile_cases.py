@@ -18,6 +18,10 @@
     python .../profile_cases.py config_sweep [M]
         the cost model's GEMV choice against every BLOCK_N x SPLIT_K of one decoder layer's four
         launches, and the lm_head-shaped GEMV at three widths.
+    python .../profile_cases.py step [layers] [steps] [batch]
+        the fused decode-step kernel on a Qwen2.5-1.5B-shaped model with `layers` layers (4 by
+        default: ~0.6 GB of weights incl. the fp16 lm_head) at context 512: 3 warm-up steps, then
+        `steps` steps (eager launches, inside the profiler range).
 
 Every case allocates at most a few hundred MB and ends by itself.
 """
@@ -27,7 +31,11 @@ from __future__ import annotations
 import os
 import sys
 
-sys.path.insert(0, os.path.abspath(os.path.join(os.path.dirname(__file__), "..", "..")))
+# run as a script, this directory would come first on sys.path and its profile.py would shadow the
+# standard library's `profile` (which torch imports through cProfile)
+_here = os.path.dirname(os.path.abspath(__file__))
+sys.path = [q for q in sys.path if os.path.abspath(q or ".") != _here]
+sys.path.insert(0, os.path.abspath(os.path.join(_here, "..", "..")))
 
 import torch  # noqa: E402
 
@@ -257,7 +265,32 @@ def config_sweep(M="1"):
         torch.cuda.empty_cache()
 
 
-CASES = {"decode": decode, "gemv_layer": gemv_layer, "gemv": gemv, "attention": attention, "gemm": gemm, "chain": chain, "attention_sweep": attention_sweep, "small_m": small_m, "config_sweep": config_sweep}
+def step(layers="4", steps="2", batch="1"):
+    from kernels.e2e.model import QwenRunner, make_backend, random_qwen2
+    from kernels.e2e.run import GraphDecoder
+    layers, steps, batch = int(layers), int(steps), int(batch)
+    arch = dict(config.QWEN15, num_hidden_layers=layers)
+    model = random_qwen2(arch, dtype=torch.float16, device="cuda", seed=0)
+    ids = torch.randint(0, arch["vocab_size"], (batch, 512), device="cuda")
+    runner = QwenRunner(model, make_backend("ours"), max_len=2048, batch=batch)
+    dec = GraphDecoder(runner)
+    dec.prefill(ids)
+    kernel = runner.step_kernel()
+    assert kernel is not None, "fused step unavailable"
+    for _ in range(3):
+        kernel(dec.tok, dec.pos, dec.out)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    for _ in range(steps):
+        kernel(dec.tok, dec.pos, dec.out)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    from kernels import _lib
+    assert _lib.device_error() == 0
+    print("step ok", dec.pos.item())
+
+
+CASES = {"step": step, "decode": decode, "gemv_layer": gemv_layer, "gemv": gemv, "attention": attention, "gemm": gemm, "chain": chain, "attention_sweep": attention_sweep, "small_m": small_m, "config_sweep": config_sweep}
 
 if __name__ == "__main__":
     if len(sys.argv) < 2 or sys.argv[1] not in CASES:

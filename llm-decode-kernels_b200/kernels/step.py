@@ -132,6 +132,67 @@ class DecodeStep:
         _lib.require_cuda("decode step", tok, pos, hist, logits)
         _lib.call("dk_step_run", self._plan, _p(tok), _p(pos), _p(hist), ld, _p(logits), _lib.stream_of(tok))
 
+    KINDS = {1: "qkv", 2: "attention", 3: "o_proj", 4: "gate_up", 5: "down", 6: "lm_head"}
+
+    def trace(self, tok: torch.Tensor, pos: torch.Tensor, hist: torch.Tensor | None = None) -> dict:
+        """Run one step with dk_step_trace and summarize where its time goes (synchronizes; not for
+        use under capture). Per op kind, averaged over its ops: `span_us` from the previous op's last
+        arrival to this op's last arrival (the op's share of the step), `hop_us` from the previous op's
+        last arrival to this op's first ready CTA (the dependency round trip), and for the slowest CTA
+        `work_us` from ready to work done, split into `stage_us` (input staging), `products_us`
+        (weights x input) and `epilogue_us` (reduction, stores); `arrive_us` the fence + arrival of the
+        slowest CTA; `ring_wait_kcycles` the most cycles (thousands) any warp spent waiting for its
+        weights to land; plus the whole step's `step_us`."""
+        nbytes = ctypes.c_uint64(0)
+        _lib.call("dk_step_trace_bytes", self._plan, ctypes.byref(nbytes))
+        buf = torch.zeros(int(nbytes.value) // 8, dtype=torch.int64, device=tok.device)
+        n = ctypes.c_int32(0)
+        _lib.call("dk_step_ops", self._plan, None, 0, ctypes.byref(n))
+        kinds = (ctypes.c_int32 * n.value)()
+        _lib.call("dk_step_ops", self._plan, kinds, n.value, ctypes.byref(n))
+        ld = 0 if hist is None else hist.stride(0)
+        _lib.call("dk_step_trace", self._plan, _p(tok), _p(pos), _p(hist), ld, None, _p(buf), _lib.stream_of(tok))
+        torch.cuda.synchronize()
+        t = buf.view(-1, n.value + 1, 12).cpu().double()
+        t0 = t[:, n.value, 0].min()
+        step_us = float((t[:, n.value, 1].max() - t0) / 1e3)
+        rows = {}
+        prev_last = t0
+        keys = ("span_us", "hop_us", "work_us", "stage_us", "products_us", "epilogue_us", "arrive_us",
+                "ring_wait_kcycles", "attn_prologue_us", "attn_blocks_us", "attn_cta_combine_us", "attn_arrive_us",
+                "attn_slice_combine_us", "ctas")
+        for j in range(n.value):
+            part = t[:, j, 1] > 0
+            tj = t[part, j]
+            last = tj[:, 5].max()
+            r = rows.setdefault(self.KINDS.get(kinds[j], str(kinds[j])), dict.fromkeys(keys, 0.0) | {"n": 0})
+            r["n"] += 1
+            r["span_us"] += float(last - prev_last) / 1e3
+            r["hop_us"] += float(tj[:, 1].min() - prev_last) / 1e3
+            slow = int((tj[:, 4] - tj[:, 1]).argmax())
+            w = tj[slow]
+            r["work_us"] += float(w[4] - w[1]) / 1e3
+            if w[2] > 0 and w[3] > 0:
+                r["stage_us"] += float(w[2] - w[1]) / 1e3
+                r["products_us"] += float(w[3] - w[2]) / 1e3
+                r["epilogue_us"] += float(w[4] - w[3]) / 1e3
+            r["arrive_us"] += float((tj[:, 5] - tj[:, 4]).max()) / 1e3
+            r["ring_wait_kcycles"] += float(tj[:, 6].max()) / 1e3  # slowest warp of any CTA
+            if kinds[j] == 2:  # attention phases of the slowest item CTA (first item of each CTA)
+                a = tj[(tj[:, 11] - tj[:, 1]).argmax()] if bool((tj[:, 11] > 0).any()) else tj[slow]
+                fin = a[11] if a[11] > 0 else a[10]
+                r["attn_prologue_us"] += float(a[7] - a[1]) / 1e3
+                r["attn_blocks_us"] += float(a[8] - a[7]) / 1e3
+                r["attn_cta_combine_us"] += float(a[9] - a[8]) / 1e3
+                r["attn_arrive_us"] += float(a[10] - a[9]) / 1e3
+                r["attn_slice_combine_us"] += float(fin - a[10]) / 1e3
+            r["ctas"] += int(part.sum())
+            prev_last = last
+        for r in rows.values():
+            for k in keys:
+                r[k] = round(r[k] / r["n"], 3)
+        return {"step_us": round(step_us, 2), "ops": rows}
+
     def close(self):
         if self._plan is not None and self._plan.value:
             _lib.call("dk_step_destroy", self._plan)

@@ -24,7 +24,7 @@ def ceil_div(a, b):
 
 
 def program(n_layers, hidden, n_heads, n_kv, inter, vocab, batch, G):
-    """The op list of dk_step_create: (kind, units, stages, cta0, ncta) per op."""
+    """The op list of dk_step_create: (kind, units, stages, cta0, ncta, ksplit) per op."""
     ops = []
     nxt = 0
 
@@ -35,24 +35,36 @@ def program(n_layers, hidden, n_heads, n_kv, inter, vocab, batch, G):
         nxt = (cta0 + ncta) % G
         return cta0, ncta
 
+    split = 1
+    while split < 4 and (hidden // 32) * (split + 1) <= G and (inter // 256) // (split + 1) >= 2:
+        split += 1
     nqkv = (n_heads + 2 * n_kv) * 128
     for _ in range(n_layers):
-        ops.append(("qkv", nqkv // 32, hidden // 256, *place(nqkv // 32)))
-        ops.append(("attn", 0, 0, nxt, 0))
+        ops.append(("qkv", nqkv // 32, hidden // 256, *place(nqkv // 32), 1))
+        ops.append(("attn", 0, 0, nxt, 0, 1))
         nxt = (nxt + batch * n_kv * 8) % G
-        ops.append(("o", hidden // 32, n_heads * 128 // 256, *place(hidden // 32)))
-        ops.append(("gate_up", inter // 32, hidden // 256, *place(inter // 32)))
-        ops.append(("down", hidden // 32, inter // 256, *place(hidden // 32)))
-    ops.append(("head", vocab // 32, hidden // 64, 0, G))
+        ops.append(("o", hidden // 32, n_heads * 128 // 256, *place(hidden // 32), 1))
+        ops.append(("gate_up", inter // 32, hidden // 256, *place(inter // 32), 1))
+        if split > 1:
+            cta0, ncta = nxt % G, (hidden // 32) * split
+            nxt = (cta0 + ncta) % G
+            ops.append(("down", hidden // 32, inter // 256, cta0, ncta, split))
+        else:
+            ops.append(("down", hidden // 32, inter // 256, *place(hidden // 32), 1))
+    ops.append(("head", vocab // 32, hidden // 64, 0, G, 1))
     return ops
 
 
 def chunk_range(op, cta, G):
-    kind, units, stages, cta0, ncta = op
+    """(c0, c1, st0, st1): this CTA's chunks and K stages of each (the kernel's op_work)."""
+    kind, units, stages, cta0, ncta, ksplit = op
     j = (cta - cta0 + G) % G
     if j >= ncta:
         return None
-    return j * units // ncta, (j + 1) * units // ncta
+    if ksplit > 1:
+        c, ks = divmod(j, ksplit)
+        return c, c + 1, ks * stages // ksplit, (ks + 1) * stages // ksplit
+    return j * units // ncta, (j + 1) * units // ncta, 0, stages
 
 
 def attn_items(op, cta, G, batch, n_kv, pos):
@@ -60,6 +72,14 @@ def attn_items(op, cta, G, batch, n_kv, pos):
     items = batch * n_kv * S
     j = (cta - op[3] + G) % G
     return list(range(j, items, G))
+
+
+def test_down_is_split_on_the_benchmark_model():
+    ops = program(batch=1, G=148, **QWEN15)
+    down = [op for op in ops if op[0] == "down"][0]
+    assert down[5] == 3 and down[4] == 144
+    small = [op for op in program(batch=1, G=148, **SMALL) if op[0] == "down"][0]
+    assert small[5] == 2  # the test model exercises the split path too
 
 
 def producer_walk(ops, cta, G, batch, n_kv, pos):
@@ -76,7 +96,7 @@ def producer_walk(ops, cta, G, batch, n_kv, pos):
         r = chunk_range(op, cta, G)
         if r is None:
             continue
-        c0, c1 = r
+        c0, c1, st0, st1 = r
         if kind == "head":
             nch = c1 - c0
             for rnd in range(ceil_div(nch, 8)):
@@ -86,9 +106,10 @@ def producer_walk(ops, cta, G, batch, n_kv, pos):
                         seq.append((j, c0 + 8 * rnd + w, k, 0))
             continue
         halves = 2 if kind == "gate_up" else 1
-        for u in range((c1 - c0) * stages):
+        nst = st1 - st0
+        for u in range((c1 - c0) * nst):
             for h in range(halves):
-                seq.append((j, c0 + u // stages, u % stages, h))
+                seq.append((j, c0 + u // nst, st0 + u % nst, h))
     return seq
 
 
@@ -110,7 +131,7 @@ def consumer_walk(ops, cta, G, batch, n_kv, pos, warp):
         r = chunk_range(op, cta, G)
         if r is None:
             continue
-        c0, c1 = r
+        c0, c1, st0, st1 = r
         if kind == "head":
             nch = c1 - c0
             rbase = base
@@ -123,10 +144,11 @@ def consumer_walk(ops, cta, G, batch, n_kv, pos, warp):
             base += nch * stages
             continue
         halves = 2 if kind == "gate_up" else 1
-        nunits = (c1 - c0) * stages
+        nst = st1 - st0
+        nunits = (c1 - c0) * nst
         for u in range(warp, nunits, CWARPS):
             for h in range(halves):
-                out.append((base + u * halves + h, (j, c0 + u // stages, u % stages, h)))
+                out.append((base + u * halves + h, (j, c0 + u // nst, st0 + u % nst, h)))
         base += nunits * halves
     return out
 
