@@ -10,7 +10,8 @@
 // Why one kernel. At batch 1 every op is a few MB or less: launches are latency chains (kernel
 // boundary, activation staging, the weight fetch, reduction, store), not bandwidth. The weights are
 // static, so they do not have to wait for the activations that multiply them:
-// * one CTA per SM (cooperative launch: all CTAs resident), 8 consumer warps and 1 producer warp;
+// * one CTA per SM (cooperative launch: all CTAs resident), 8 consumer warps and a producer warp
+//   (whose warpgroup hands most of its registers to the consumers: setmaxnreg);
 // * the producer warp walks the whole step's program and streams this CTA's share of every op's
 //   weights (and of the KV cache rows before `pos`) into a shared-memory ring with TMA, gated only by
 //   free ring slots - it runs ahead across op and layer boundaries, so an op's weights are usually
@@ -24,8 +25,8 @@
 //   in the ring (mma.m16n8k16, fp32 accumulation, the int4 "magic number" unpack of the standalone
 //   GEMV kernel), reduces across warps in a fixed order and stores its tagged output;
 // * attention is split over (sequence, kv head, 128-position slice) items; each CTA combines its 8
-//   warps' partials, and the last item of a (sequence, kv head) to arrive combines the slices.
-//   The greedy argmax is combined the same way: the last CTA to arrive picks the token.
+//   warps' partials into one tagged partial per head, and the o_proj CTAs combine the slices while
+//   they stage their input. The greedy argmax is combined by the last CTA to arrive on a counter.
 // Every wait is bounded (2 s); a CTA that gives up records DK_DEVERR_STEP_WAIT and skips the rest of
 // its work (the others then give up on its words in turn), but still arrives on the counters it uses,
 // so they stay consistent for the next launch. No TMA multicast.
@@ -44,7 +45,15 @@ namespace step {
 
 constexpr int kCWarps = 8;                    // consumer warps
 constexpr int kConsumers = kCWarps * 32;
-constexpr int kThreads = kConsumers + 32;     // + one producer warp
+constexpr int kThreads = kConsumers + 128;    // + one warpgroup: the producer warp and 3 idle warps
+// Register split (setmaxnreg): the kernel is compiled for 168 registers a thread (384 threads, one CTA
+// per SM: 64512 of the 65536), then the producer warpgroup gives registers back and the consumer
+// warpgroups take them: 128 x 40 + 256 x 232 = 64512, the launch's whole allocation, so the consumers'
+// increase is always satisfiable (dk_step_create checks the compiled count before any launch).
+constexpr int kLaunchRegs = 168;
+constexpr int kProducerRegs = 40;
+constexpr int kConsumerRegs = 232;
+static_assert(128 * kProducerRegs + kConsumers * kConsumerRegs <= kThreads * kLaunchRegs, "register split");
 constexpr int kMaxRows = 4;                   // batch rows of one step
 constexpr int kSlotW = 4096;                  // weight bytes of one ring slot (one TMA box)
 constexpr int kSlotSZ = 256;                  // scale + zero bytes of one int4 ring slot
@@ -53,6 +62,7 @@ constexpr int kHd = 128;                      // head_dim
 constexpr int kAttnPos = 128;                 // cache positions per attention item (8 warps x 16)
 constexpr int kMaxGroup = 8;                  // query heads per kv head
 constexpr int kPartFloats = 2 + kHd;          // attention partial per head: max, sum, output[hd]
+constexpr int kAttnBatch = 1;                 // attention slices whose partials one thread loads at once
 constexpr int kMaxKSplit = 4;                 // K slices of a split-K projection (partials in fp32)
 constexpr int kXsPad = 16;
 constexpr int kTraceSlots = 12;  // per op: wait start, ready, staged, products, work done, arrival, ring wait, probes
@@ -72,9 +82,10 @@ struct __align__(16) Op {
   int xsplit;       // > 0: the input is fp16(sum of xsplit fp32 partials xp + xbias), not x
   int xop, rop;     // program index of the op that wrote the input / the residual (their tags)
   int cache_row0;   // ATTN: first row of this layer's cache in the 2-D cache maps
-  int pad0;
+  int xattn;        // O: the input is the attention items' slice partials at xp (combined while staged)
   // activations are tagged words: fp16 value | 16-bit tag << 16 (LL16), fp32 bits | 32-bit tag << 32 (LL32)
-  const unsigned long long* xp;  // [xsplit, M, K] LL32 partial sums of the previous projection
+  const unsigned long long* xp;  // [xsplit, M, K] LL32 partial sums of the previous projection; xattn: the
+                                 // attention partials [M * nkv][max_len / 128][kMaxGroup][kPartFloats]
   const __half* xbias;  // [K] bias of that projection, or nullptr
   unsigned long long* yp;  // ksplit > 1: [ksplit, M, N] LL32 partial sums (no bias: the consumer adds it)
   const uint32_t* x;    // LL16 input [M, K] (not read when from_embed or xsplit)
@@ -116,10 +127,8 @@ struct Params {
   unsigned long long* trace;  // [grid][n_ops + 1][kTraceSlots] %globaltimer stamps, or nullptr (dk_step_trace)
   unsigned* epoch;         // launches so far (tags of this launch's words), advanced by the last CTA
   unsigned* exit_count;
-  unsigned* attn_count;    // [M * nkv]
   unsigned* head_count;
   unsigned long long* attn_part;  // LL32 [M * nkv * max_splits][group][kPartFloats]
-  uint32_t* attn_out;      // LL16 [M, nq * head_dim]
   float* head_val;         // [grid][kMaxRows]
   int* head_idx;           // [grid][kMaxRows]
   int* err;
@@ -213,6 +222,16 @@ __device__ __forceinline__ uint4 ll16_load8(const uint32_t* src, uint32_t tag, P
 // Release of this thread's (and, after a CTA barrier, the CTA's) earlier writes to the GPU before an
 // arrival: acq_rel is enough for the acquire loads that pair with it (no total order needed).
 __device__ __forceinline__ void fence_release_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
+// 16-byte word w of an op descriptor, global -> shared without stalling the issuing thread
+__device__ __forceinline__ void cp_async16(Op* dst, int w, const Op* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(reinterpret_cast<uint4*>(dst) + w)),
+               "l"(reinterpret_cast<const uint4*>(src) + w)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_group1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 __device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"r"(kConsumers) : "memory"); }
 
@@ -430,24 +449,34 @@ __device__ __forceinline__ void gemv_stage(uint32_t wbox, uint32_t szb, uint32_t
 
 // Block v (8 values) of input row m when the input is the sum of a split-K projection's fp32 partials:
 // fp16(partial 0 + partial 1 + ... (+ bias)), partials added in slice order (deterministic), the same
-// fp16 rounding the projection's own epilogue applies.
+// fp16 rounding the projection's own epilogue applies. Two partials' words are in flight at a time
+// (partial q + 2 is requested once partial q is in): three partials cost two round trips to L2, not
+// three, without holding every partial's 64-bit words in registers at once.
 __device__ __forceinline__ uint4 split_input(const Op& op, int M, int K, int m, int v, uint32_t tag, Poller& pl) {
-  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  for (int q = 0; q < op.xsplit; ++q) {
-    const unsigned long long* src = op.xp + (static_cast<int64_t>(q) * M + m) * K + 8 * v;
-    unsigned long long w[8];
+  const int nsplit = op.xsplit;
+  const int64_t qstride = static_cast<int64_t>(M) * K;
+  const unsigned long long* src = op.xp + static_cast<int64_t>(m) * K + 8 * v;
+  unsigned long long w[2][8];
+  auto request = [&](int q) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) ldv_u64x2(src + 2 * i, w[2 * i], w[2 * i + 1]);
+    for (int i = 0; i < 4; ++i) ldv_u64x2(src + q * qstride + 2 * i, w[q & 1][2 * i], w[q & 1][2 * i + 1]);
+  };
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  request(0);
+  if (nsplit > 1) request(1);
+#pragma unroll
+  for (int q = 0; q < kMaxKSplit; ++q) {
+    if (q >= nsplit) break;
     for (;;) {
       bool ok = true;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) ok &= static_cast<uint32_t>(w[i] >> 32) == tag;
+      for (int i = 0; i < 8; ++i) ok &= static_cast<uint32_t>(w[q & 1][i] >> 32) == tag;
       if (ok || !pl.again()) break;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) ldv_u64x2(src + 2 * i, w[2 * i], w[2 * i + 1]);
+      request(q);
     }
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] += __uint_as_float(static_cast<uint32_t>(w[i]));
+    for (int i = 0; i < 8; ++i) acc[i] += __uint_as_float(static_cast<uint32_t>(w[q & 1][i]));
+    if (q + 2 < nsplit) request(q + 2);
   }
   if (op.xbias != nullptr) {
     const uint4 bb = __ldg(reinterpret_cast<const uint4*>(op.xbias) + v);
@@ -459,6 +488,59 @@ __device__ __forceinline__ uint4 split_input(const Op& op, int M, int K, int m, 
   __half2* oh = reinterpret_cast<__half2*>(&out);
 #pragma unroll
   for (int i = 0; i < 4; ++i) oh[i] = __floats2half2_rn(acc[2 * i], acc[2 * i + 1]);
+  return out;
+}
+
+// Block v (8 dims of one query head) of row b of the attention output, combined from the attention
+// items' slice partials (per slice q: max score M_q, sum of weights L_q, unnormalized output O_q) in
+// slice order, flash-decoding style: out = sum_q e^(M_q - M) O_q / sum_q e^(M_q - M) L_q with the
+// running maximum M, rounded to fp16. The words of kAttnBatch slices are requested at once.
+__device__ __forceinline__ uint4 attn_input(const Params& p, const Op& op, int b, int v, int S, uint32_t tag, Poller& pl) {
+  const int G = p.nq / p.nkv;
+  const int head = v >> 4, d0 = (v & 15) * 8;
+  const int h = head / G, hh = head - h * G;
+  const unsigned long long* parts =
+      op.xp + (static_cast<int64_t>(b) * p.nkv + h) * (p.max_len / kAttnPos) * kMaxGroup * kPartFloats + hh * kPartFloats;
+  float mx = -INFINITY, l = 0.f;
+  float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int q0 = 0; q0 < S; q0 += kAttnBatch) {
+    unsigned long long w[kAttnBatch][10];
+    auto request = [&](int u) {
+      const unsigned long long* src = parts + static_cast<int64_t>(q0 + u) * kMaxGroup * kPartFloats;
+      ldv_u64x2(src, w[u][0], w[u][1]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) ldv_u64x2(src + 2 + d0 + 2 * i, w[u][2 + 2 * i], w[u][3 + 2 * i]);
+    };
+#pragma unroll
+    for (int u = 0; u < kAttnBatch; ++u)
+      if (q0 + u < S) request(u);
+#pragma unroll
+    for (int u = 0; u < kAttnBatch; ++u) {
+      if (q0 + u >= S) break;
+      for (;;) {
+        bool ok = true;
+#pragma unroll
+        for (int i = 0; i < 10; ++i) ok &= static_cast<uint32_t>(w[u][i] >> 32) == tag;
+        if (ok || !pl.again()) break;
+        request(u);
+      }
+      const float mq = __uint_as_float(static_cast<uint32_t>(w[u][0]));
+      const float lq = __uint_as_float(static_cast<uint32_t>(w[u][1]));
+      if (lq > 0.f) {
+        const float mn = fmaxf(mx, mq);
+        const float a = __expf(mx - mn), c = __expf(mq - mn);  // a = 0 while nothing is summed (mx = -inf)
+        l = fmaf(l, a, lq * c);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = fmaf(o[i], a, __uint_as_float(static_cast<uint32_t>(w[u][2 + i])) * c);
+        mx = mn;
+      }
+    }
+  }
+  if (!(l > 0.f)) l = 1.f;  // only after a give-up (slice 0 always holds position 0)
+  uint4 out;
+  __half2* oh = reinterpret_cast<__half2*>(&out);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) oh[i] = __floats2half2_rn(o[2 * i] / l, o[2 * i + 1] / l);
   return out;
 }
 
@@ -507,7 +589,7 @@ __device__ __forceinline__ void stage_block(const Params& p, const Smem& s, uint
 // MMA fragments, odd K divided by 16 (exact) for the magic-number operands, and {C, X} per
 // (128-group, row). `writer`: this CTA stores h as the new residual.
 __device__ void stage_int4_input(const Params& p, const Op& op, const Tags& tg, const Smem& s, bool writer,
-                                 float* inv_s, float (*part)[kCWarps], int st0, int st1, Poller& pl) {
+                                 float* inv_s, float (*part)[kCWarps], int st0, int st1, int pos, Poller& pl) {
   const int tid = threadIdx.x;
   const int K = op.K;
   const int nblk = K / 8;  // K % 256 == 0: a multiple of 32 blocks, so a warp's 32 items share a row
@@ -520,17 +602,14 @@ __device__ void stage_int4_input(const Params& p, const Op& op, const Tags& tg, 
     }
     return p.embed + t * static_cast<int64_t>(p.H);
   };
-  auto add_res = [&](uint4 a, int m, int v) -> uint4 {  // a + residual (fp16 add) at block v of row m
-    if (op.res_in != nullptr) {
-      const uint4 r = ll16_load8(op.res_in + (static_cast<int64_t>(m) * K + 8 * v), tg.r16, pl);
-      __half2* ah = reinterpret_cast<__half2*>(&a);
-      const __half2* rh = reinterpret_cast<const __half2*>(&r);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) ah[j] = __hadd2_rn(ah[j], rh[j]);
-    }
-    return a;
-  };
   auto load_h = [&](int m, int v) -> uint4 {  // 8 values of h = x (+ residual) at block v of row m
+    // the residual's words are requested first, in flight together with the input's
+    const uint32_t* rsrc = op.res_in != nullptr ? op.res_in + (static_cast<int64_t>(m) * K + 8 * v) : nullptr;
+    uint4 ra = make_uint4(0, 0, 0, 0), rb = ra;
+    if (rsrc != nullptr) {
+      ra = ldv_u32x4(rsrc);
+      rb = ldv_u32x4(rsrc + 4);
+    }
     uint4 a;
     if (op.xsplit > 0)
       a = split_input(op, p.M, K, m, v, tg.x32, pl);
@@ -538,7 +617,14 @@ __device__ void stage_int4_input(const Params& p, const Op& op, const Tags& tg, 
       a = __ldg(reinterpret_cast<const uint4*>(embed_row(m)) + v);
     else
       a = ll16_load8(op.x + (static_cast<int64_t>(m) * K + 8 * v), tg.x16, pl);
-    return add_res(a, m, v);
+    if (rsrc != nullptr) {  // a + residual (fp16 add)
+      const uint4 r = ll16_finish(rsrc, ra, rb, tg.r16, pl);
+      __half2* ah = reinterpret_cast<__half2*>(&a);
+      const __half2* rh = reinterpret_cast<const __half2*>(&r);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) ah[j] = __hadd2_rn(ah[j], rh[j]);
+    }
+    return a;
   };
   // One block of 8 values per thread and row (K <= 2048, every norm op of Qwen2.5-1.5B): one L2 read
   // of the row, held in registers from the sum of squares to the staging.
@@ -604,17 +690,26 @@ __device__ void stage_int4_input(const Params& p, const Op& op, const Tags& tg, 
     }
     consumers_sync();
   }
-  // Up to kBatch blocks per thread in flight at once: their loads are issued back to back, then the
-  // blocks are staged (a long row such as down's 8960 values takes several rounds per thread).
-  // Only this CTA's K stages [st0, st1) are staged, at stage positions 0 .. st1 - st0. A plain tagged
-  // input (down_proj's, o_proj's) has the first attempt of kBatch blocks' loads in flight at once.
-  constexpr int kBatch = 4;
+  // Only this CTA's K stages [st0, st1) are staged, at stage positions 0 .. st1 - st0. Block i of the
+  // staged rows goes to thread i % kConsumers (sblk is a multiple of 32: warps are whole in every
+  // round, as stage_block's half-warp sums need).
   const int sblk = (st1 - st0) * 32, b0 = st0 * 32;
-  const int total = p.M * sblk;  // a multiple of 32: warps are whole in every round
-  const bool plain = op.xsplit == 0 && !op.from_embed && op.res_in == nullptr;
-  for (int base0 = (tid & ~31); base0 < total; base0 += kBatch * kConsumers) {
-    uint4 v[kBatch];
-    if (plain) {
+  const int total = p.M * sblk;
+  auto stage_one = [&](int i, uint4 v) {
+    const int m = i / sblk, b = i % sblk;
+    if (!norm && writer && op.res_out != nullptr)
+      ll16_store8(op.res_out + (static_cast<int64_t>(m) * K + 8 * (b0 + b)), v, tg.o16);
+    const uint4 wv = norm ? __ldg(reinterpret_cast<const uint4*>(op.norm_w) + b0 + b) : make_uint4(0, 0, 0, 0);
+    stage_block(p, s, v, wv, norm ? inv_s[m] : 0.f, m, b);
+  };
+  if (op.xattn) {  // o_proj: the attention output, combined from the slice partials (no norm, no residual)
+    const int S = attn_splits(pos);
+    for (int i = tid; i < total; i += kConsumers) stage_one(i, attn_input(p, op, i / sblk, b0 + i % sblk, S, tg.x32, pl));
+  } else if (op.xsplit == 0 && !op.from_embed && op.res_in == nullptr) {
+    // a plain tagged input (down_proj's, a long row such as down's 8960 values): up to kBatch blocks
+    // per thread with their first loads in flight at once, then checked and staged
+    constexpr int kBatch = 4;
+    for (int base0 = (tid & ~31); base0 < total; base0 += kBatch * kConsumers) {
       uint4 wa[kBatch], wb[kBatch];
 #pragma unroll
       for (int q = 0; q < kBatch; ++q) {
@@ -628,26 +723,13 @@ __device__ void stage_int4_input(const Params& p, const Op& op, const Tags& tg, 
 #pragma unroll
       for (int q = 0; q < kBatch; ++q) {
         const int i = base0 + q * kConsumers + (tid & 31);
-        if (i < total)
-          v[q] = ll16_finish(op.x + (static_cast<int64_t>(i / sblk) * K + 8 * (b0 + i % sblk)), wa[q], wb[q], tg.x16, pl);
-      }
-    } else {
-#pragma unroll
-      for (int q = 0; q < kBatch; ++q) {
-        const int i = base0 + q * kConsumers + (tid & 31);
-        if (i < total) v[q] = load_h(i / sblk, b0 + i % sblk);
+        if (base0 + q * kConsumers >= total) break;
+        const uint4 v = ll16_finish(op.x + (static_cast<int64_t>(i / sblk) * K + 8 * (b0 + i % sblk)), wa[q], wb[q], tg.x16, pl);
+        stage_one(i, v);
       }
     }
-#pragma unroll
-    for (int q = 0; q < kBatch; ++q) {
-      const int i = base0 + q * kConsumers + (tid & 31);
-      if (base0 + q * kConsumers >= total) break;
-      const int m = i / sblk, b = i % sblk;
-      if (!norm && writer && op.res_out != nullptr)
-        ll16_store8(op.res_out + (static_cast<int64_t>(m) * K + 8 * (b0 + b)), v[q], tg.o16);
-      const uint4 wv = norm ? __ldg(reinterpret_cast<const uint4*>(op.norm_w) + b0 + b) : make_uint4(0, 0, 0, 0);
-      stage_block(p, s, v[q], wv, norm ? inv_s[m] : 0.f, m, b);
-    }
+  } else {
+    for (int i = tid; i < total; i += kConsumers) stage_one(i, load_h(i / sblk, b0 + i % sblk));
   }
   consumers_sync();
 }
@@ -664,11 +746,12 @@ __device__ __forceinline__ __half swiglu_pick(float g, float u, const __half* bi
 
 // An int4 projection (QKV, O, GATEUP, DOWN) of this CTA's chunk range [c0, c1). Unit u of the range
 // (chunk c0 + u / stages, stage u % stages) sits at ring slot base + u (gate_up: 2u and 2u + 1, the
-// gate and the up box) and belongs to consumer warp u % kCWarps, which keeps its sum in registers
-// while consecutive units stay in one chunk and parks it in red[chunk][warp] when the chunk changes.
+// gate and the up box). Boxes are dealt to the consumer warps one by one (box b to warp b % kCWarps),
+// so the warps' box counts differ by at most one; a warp keeps its sum in registers while its boxes
+// stay in one chunk (and half) and parks it in red[chunk][warp][half] when that changes.
 __device__ void run_int4(const Params& p, const Op& op, const Tags& tg, Ring& ring, int base, const Work& wk,
                          int ks, unsigned long long* stamp) {
-  const int c0 = wk.c0, c1 = wk.c1, st0 = wk.st0, nst = wk.st1 - wk.st0;
+  const int c0 = wk.c0, c1 = wk.c1, nst = wk.st1 - wk.st0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const bool pair = op.kind == OP_GATEUP;
@@ -681,54 +764,66 @@ __device__ void run_int4(const Params& p, const Op& op, const Tags& tg, Ring& ri
   for (int cl = 0; cl < c1 - c0; ++cl)
     for (int h = 0; h < halves; ++h)
       for (int m = 0; m < M; ++m) cell(cl, warp, h, m)[lane] = 0.f;
-  float acc[2][2][4];
-  int cur = -1;
+  float acc[2][4];
+  int cur = -1, cur_h = 0;
   auto flush = [&]() {
     if (cur < 0) return;
-    for (int h = 0; h < halves; ++h)
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int m = 2 * t + e;
-        if (m < M) {
-          float* dst = cell(cur, warp, h, m) + 4 * g;
-          dst[0] = acc[h][0][e];
-          dst[1] = acc[h][0][2 + e];
-          dst[2] = acc[h][1][e];
-          dst[3] = acc[h][1][2 + e];
-        }
+    for (int e = 0; e < 2; ++e) {
+      const int m = 2 * t + e;
+      if (m < M) {
+        float* dst = cell(cur, warp, cur_h, m) + 4 * g;
+        dst[0] = acc[0][e];
+        dst[1] = acc[0][2 + e];
+        dst[2] = acc[1][e];
+        dst[3] = acc[1][2 + e];
       }
+    }
   };
+  // the epilogue's bias values, fetched now so that their latency hides behind the products
+  const int ncols = (c1 - c0) * 32;
+  float bias_pre[2] = {0.f, 0.f};
+  if (!pair && op.ksplit <= 1 && op.bias != nullptr)
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int e = threadIdx.x + q * kConsumers;
+      if (e < M * ncols) bias_pre[q] = __half2float(__ldg(op.bias + c0 * 32 + e % ncols));
+    }
   const uint32_t w_base = smem_addr(ring.s.w), sz_base = smem_addr(ring.s.sz);
   const uint32_t xs_base = smem_addr(ring.s.xs), cx_base = smem_addr(ring.s.cx);
-  for (int u = warp; u < nunits; u += kCWarps) {
+  // tracing (thread 0): clock cycles to the start of its second box and to the end of its last
+  const long long clk0 = stamp ? clock64() : 0;
+  for (int b = warp; b < nunits * halves; b += kCWarps) {
+    if (stamp && b == warp + kCWarps) stamp[5] = static_cast<unsigned long long>(clock64() - clk0);
+    const int u = pair ? b >> 1 : b, h = pair ? b & 1 : 0;
     const int cl = u / nst, st = u % nst;  // st: position in the staged K slice
-    if (cl != cur) {
+    if (cl != cur || h != cur_h) {
       flush();
       cur = cl;
+      cur_h = h;
 #pragma unroll
-      for (int h = 0; h < 2; ++h)
+      for (int a2 = 0; a2 < 2; ++a2)
 #pragma unroll
-        for (int a = 0; a < 2; ++a)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) acc[h][a][e] = 0.f;
+        for (int e = 0; e < 4; ++e) acc[a2][e] = 0.f;
     }
     const uint32_t xrow = xs_base + st * 512, cxg = cx_base + st * 2 * 64;
-    for (int h = 0; h < halves; ++h) {
-      const int it = base + u * halves + h;
-      if (!ring.warp_wait(it)) break;
-      const int slot = ring.slot_of(it);
-      gemv_stage(w_base + slot * kSlotW, sz_base + slot * kSlotSZ, xrow, cxg, p.xs_pitch, M, g, t, acc[h]);
-      __syncwarp();
-      if (lane == 0) ring.release(it);
-    }
+    const int it = base + b;
+    if (!ring.warp_wait(it)) break;
+    const int slot = ring.slot_of(it);
+    gemv_stage(w_base + slot * kSlotW, sz_base + slot * kSlotSZ, xrow, cxg, p.xs_pitch, M, g, t, acc);
+    __syncwarp();
+    if (lane == 0) ring.release(it);
     if (__any_sync(0xffffffffu, *ring.abort)) break;
   }
+  if (stamp) stamp[6] = static_cast<unsigned long long>(clock64() - clk0);
   flush();
   consumers_sync();
-  if (stamp) *stamp = globaltimer_ns();
+  if (stamp) {
+    stamp[0] = globaltimer_ns();
+    stamp[7] = static_cast<unsigned long long>(clock64() - clk0);
+  }
   if (*ring.abort) return;
   // fixed-order reduction over the warps, epilogue, store
-  const int ncols = (c1 - c0) * 32;
   for (int e = threadIdx.x; e < M * ncols; e += kConsumers) {
     const int m = e / ncols, col = e % ncols;
     const int cl = col / 32, cc = col % 32;
@@ -743,7 +838,8 @@ __device__ void run_int4(const Params& p, const Op& op, const Tags& tg, Ring& ri
       op.y[static_cast<int64_t>(m) * op.N + n] = ll16_word(swiglu_pick(v[0], v[1], op.bias, n, op.N), tg.o16);
     } else {
       float a = v[0];
-      if (op.bias != nullptr) a += __half2float(__ldg(op.bias + n));
+      if (op.bias != nullptr)
+        a += e < kConsumers ? bias_pre[0] : e < 2 * kConsumers ? bias_pre[1] : __half2float(__ldg(op.bias + n));
       op.y[static_cast<int64_t>(m) * op.N + n] = ll16_word(__float2half_rn(a), tg.o16);
     }
   }
@@ -799,7 +895,7 @@ struct AttnSmem {
 // head; the last item of (b, h) to arrive combines every slice into the attention output.
 __device__ void run_attention_item(const Params& p, const Op& op, const Tags& tg, Ring& ring, AttnSmem& as,
                                    int base, int item, int pos, int S, Poller& pl, unsigned long long* stamps) {
-  // stamps (tracing, thread 0): [prologue done, blocks done, CTA combine done, arrival done, slice combine done]
+  // stamps (tracing, thread 0): [prologue done, blocks done, partial written]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
   const int g = lane >> 2, t = lane & 3;
   const int G = p.nq / p.nkv;
@@ -968,59 +1064,6 @@ __device__ void run_attention_item(const Params& p, const Op& op, const Tags& tg
     part[hh * kPartFloats + k] = ll32_word(v, tg.o32);
   }
   if (stamps) stamps[2] = globaltimer_ns();
-  if (s != 0) return;  // slice 0 of (b, h) combines every slice (no barrier below depends on others)
-  consumers_sync();    // this CTA's own partial words are written (visible to its threads)
-  if (stamps) stamps[3] = globaltimer_ns();
-  // (1) every slice's (M, L) per head, polled; (2) per head the slice weights exp(M_q - M) and the
-  // denominator; (3) each output dim sums its slices' values, the loads of 4 slices in flight at once
-  float* sw = red;                             // [max slices][kMaxGroup]
-  float* sl = red + kMaxGroup * (p.max_len / kAttnPos);  // [max slices][kMaxGroup]
-  float* den = sl + kMaxGroup * (p.max_len / kAttnPos);  // [kMaxGroup]
-  for (int e = tid; e < S * G; e += kConsumers) {
-    const int q = e / G, hh = e % G;
-    const unsigned long long* src = parts + (q * kMaxGroup + hh) * kPartFloats;
-    unsigned long long mw, lw;
-    ldv_u64x2(src, mw, lw);
-    while ((static_cast<uint32_t>(mw >> 32) != tg.o32 || static_cast<uint32_t>(lw >> 32) != tg.o32) && pl.again())
-      ldv_u64x2(src, mw, lw);
-    const float l = __uint_as_float(static_cast<uint32_t>(lw));
-    sw[q * kMaxGroup + hh] = l > 0.f ? __uint_as_float(static_cast<uint32_t>(mw)) : -INFINITY;
-    sl[q * kMaxGroup + hh] = l;
-  }
-  consumers_sync();
-  if (tid < G) {
-    float mx = -INFINITY;
-    for (int q = 0; q < S; ++q) mx = fmaxf(mx, sw[q * kMaxGroup + tid]);
-    float dsum = 0.f;
-    for (int q = 0; q < S; ++q) {
-      const float w = sw[q * kMaxGroup + tid] == -INFINITY ? 0.f : __expf(sw[q * kMaxGroup + tid] - mx);
-      sw[q * kMaxGroup + tid] = w;
-      dsum = fmaf(w, sl[q * kMaxGroup + tid], dsum);
-    }
-    den[tid] = dsum;
-  }
-  consumers_sync();
-  for (int e = tid; e < G * kHd; e += kConsumers) {
-    const int hh = e / kHd, d = e % kHd;
-    const unsigned long long* src = parts + hh * kPartFloats + 2 + d;
-    float num = 0.f;
-    for (int q0 = 0; q0 < S; q0 += 4) {
-      unsigned long long w4[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-        if (q0 + u < S) w4[u] = *reinterpret_cast<const volatile unsigned long long*>(src + (q0 + u) * kMaxGroup * kPartFloats);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        if (q0 + u >= S) break;
-        const volatile unsigned long long* at = src + (q0 + u) * kMaxGroup * kPartFloats;
-        while (static_cast<uint32_t>(w4[u] >> 32) != tg.o32 && pl.again()) w4[u] = *at;
-        num = fmaf(sw[(q0 + u) * kMaxGroup + hh], __uint_as_float(static_cast<uint32_t>(w4[u])), num);
-      }
-    }
-    p.attn_out[static_cast<int64_t>(b) * p.nq * kHd + (h * G + hh) * kHd + d] =
-        ll16_word(__float2half_rn(num / den[hh]), tg.o16);
-  }
-  if (stamps) stamps[4] = globaltimer_ns();
 }
 
 // ------------------------------------------------------------------------------ lm_head + argmax
@@ -1182,7 +1225,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
   s.full = reinterpret_cast<uint64_t*>(base + L.bars);
   s.empty = s.full + p.nslots;
   Ctl* ctl = reinterpret_cast<Ctl*>(base + L.ctl);
-  __shared__ __align__(16) Op s_op;  // the current op of the consumers (participants only)
+  __shared__ __align__(16) Op s_ops[2];  // the consumers' current op and the next one they take part in
 
   __shared__ int s_issued, s_abort, s_pos;
   __shared__ uint32_t s_epoch;
@@ -1228,6 +1271,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
   volatile int* abort = &s_abort;
   if (pos < 0) *abort = 1;  // every CTA decides the same: nothing is written, counters still move
 
+  if (warp >= kCWarps) {  // the producer's warpgroup (warps 9-11 only wait for the exit)
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
+  }
   if (warp == kCWarps) {
     // ================================================================ producer warp
     // kPLanes lanes arm kPLanes consecutive slots in lockstep (each waits for its own slot's release,
@@ -1340,7 +1386,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
       }
     }
     __syncwarp();
-  } else {
+  } else if (warp < kCWarps) {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kConsumerRegs));
     // ================================================================ consumer warps
     Ring ring;
     ring.s = s;
@@ -1358,21 +1405,35 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     int base_it = 0;
     unsigned long long* trace = p.trace ? p.trace + static_cast<size_t>(cta) * (p.n_ops + 1) * kTraceSlots : nullptr;
     if (trace && tid == 0) trace[p.n_ops * kTraceSlots] = globaltimer_ns();
+    // does this CTA take part in op j (attention: has it an item; others: is it a participant)
+    auto takes_part = [&](int j) {
+      const Ctl cj = ctl[j];
+      return cj.kind == OP_ATTN ? (pos >= 0 && op_slots(cj, cta, G, p.M, p.nkv, pos) > 0)
+                                : participant(cta, cj.cta0, cj.ncta, G) >= 0;
+    };
+    constexpr int kOpWords = static_cast<int>(sizeof(Op) / 16);
+    static_assert(sizeof(Op) % 16 == 0 && kOpWords <= 32, "Op is copied in 16-byte words by one warp");
+    int cur = 0;       // s_ops[cur] holds the op being run
+    int fetched = -1;  // (warp 0) the op whose descriptor is in flight to s_ops[cur]
     for (int j = 0; j < p.n_ops; ++j) {
       const Ctl cj = ctl[j];
       const int nslots_op = pos >= 0 ? op_slots(cj, cta, G, p.M, p.nkv, pos) : 0;
-      const bool part = cj.kind == OP_ATTN ? nslots_op > 0 : participant(cta, cj.cta0, cj.ncta, G) >= 0;
-      if (!part) continue;
+      if (!takes_part(j)) continue;
       if (trace && tid == 0) trace[j * kTraceSlots] = globaltimer_ns();
-      // this op's descriptor into shared memory while its input is awaited (the previous op's readers
-      // of s_op passed the barrier that ended that op)
+      // The descriptors come from global memory asynchronously: op j's was requested while the
+      // previous op ran (the first one now), the next op's is requested here into the other buffer,
+      // whose readers passed the barrier that ended the previous op.
       if (warp == 0) {
-        constexpr int kWords = static_cast<int>(sizeof(Op) / 16);
-        static_assert(sizeof(Op) % 16 == 0, "Op is copied in 16-byte words");
-        for (int w = lane; w < kWords; w += 32)
-          reinterpret_cast<uint4*>(&s_op)[w] = __ldg(reinterpret_cast<const uint4*>(p.ops + j) + w);
+        if (fetched != j && lane < kOpWords) cp_async16(&s_ops[cur], lane, p.ops + j);
+        int jn = j + 1;
+        while (jn < p.n_ops && !takes_part(jn)) ++jn;
+        cp_async_commit();
+        if (jn < p.n_ops && lane < kOpWords) cp_async16(&s_ops[cur ^ 1], lane, p.ops + jn);
+        cp_async_commit();
+        cp_async_wait_group1();  // op j's copy landed; op jn's stays in flight
+        fetched = jn;
       }
-      const Op& op = s_op;
+      const Op& op = s_ops[cur];
       if (tid == 0) {
         s_stop = *abort;
         if (trace) trace[j * kTraceSlots + 1] = globaltimer_ns();
@@ -1456,7 +1517,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
             consumers_sync();
             if (s_head_last && tid == 0) *p.pos = pos + 1;
           } else {
-            stage_int4_input(p, op, tg, s, jj == 0, s_inv, s_part, wk.st0, wk.st1, pl);
+            stage_int4_input(p, op, tg, s, jj == 0, s_inv, s_part, wk.st0, wk.st1, pos, pl);
             if (trace && tid == 0) trace[j * kTraceSlots + 2] = globaltimer_ns();
             run_int4(p, op, tg, ring, base_it, wk, op.ksplit > 1 ? jj % op.ksplit : 0,
                      trace && tid == 0 ? trace + j * kTraceSlots + 3 : nullptr);
@@ -1477,7 +1538,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
         trace[j * kTraceSlots + 6] = s_waited;
       }
       base_it += nslots_op;
+      cur ^= 1;
     }
+    if (warp == 0) cp_async_wait_all();  // no copy into shared memory outlives the kernel
   }
 
   // ---------------------------------------------------------------- exit: the last CTA resets the counters
@@ -1487,7 +1550,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     const unsigned prev = atomicAdd(p.exit_count, 1u);
     if (p.trace) p.trace[static_cast<size_t>(cta) * (p.n_ops + 1) * kTraceSlots + p.n_ops * kTraceSlots + 1] = globaltimer_ns();
     if (prev == static_cast<unsigned>(G - 1)) {  // every CTA has left: the next launch takes new tags
-      for (int i = 0; i < p.M * p.nkv; ++i) p.attn_count[i] = 0;
       *p.head_count = 0;
       *p.exit_count = 0;
       *p.epoch = s_epoch + 1;
@@ -1517,7 +1579,7 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // Offsets of the pieces of a step workspace (all from its 256-byte aligned start).
 struct Workspace {
-  size_t counters, ops, maps, attn_out, qkv, o, act, down, down_part, res0, res1, attn_part, head_val, head_idx, total;
+  size_t counters, ops, maps, qkv, o, act, down, down_part, res0, res1, attn_part, head_val, head_idx, total;
   int n_ops, n_maps, max_splits;
 };
 
@@ -1529,15 +1591,13 @@ Workspace workspace_layout(const dk_step_model* m, int grid) {
   w.max_splits = m->max_len / kAttnPos;
   const int64_t M = m->batch, H = m->hidden, nqkv = (m->n_heads + 2 * m->n_kv) * m->head_dim;
   size_t off = 0;
-  w.counters = off;  // epoch, exit count, argmax count, attention counts [M * nkv]
-  off = align_up(off + 4 * (4 + M * m->n_kv), 256);
+  w.counters = off;  // epoch, exit count, argmax count
+  off = align_up(off + 4 * 4, 256);
   w.ops = off;
   off = align_up(off + sizeof(Op) * w.n_ops, 256);
   w.maps = off;
   off = align_up(off + sizeof(CUtensorMap) * w.n_maps, 256);
   // activations between ops: tagged words, 4 bytes per fp16 value, 8 per fp32 partial
-  w.attn_out = off;
-  off = align_up(off + 4 * M * m->n_heads * m->head_dim, 256);
   w.qkv = off;
   off = align_up(off + 4 * M * nqkv, 256);
   w.o = off;
@@ -1574,10 +1634,6 @@ int check_model(const dk_step_model* m) {
     return set_error(DK_ERR_UNSUPPORTED, "step: hidden, intermediate and n_heads * head_dim must be multiples of 256");
   if (m->vocab % 32 || m->max_len % kAttnPos)
     return set_error(DK_ERR_UNSUPPORTED, "step: vocab %% 32 == 0 and max_len %% 128 == 0 needed");
-  // every attention item (sequence, kv head, 128-position slice) on its own CTA: slice 0 waits for the
-  // others' partials, so two slices of one head must never queue on one CTA
-  if (static_cast<int64_t>(m->batch) * m->n_kv * (m->max_len / kAttnPos) > device_info().num_sms)
-    return set_error(DK_ERR_UNSUPPORTED, "step: batch x kv heads x max_len / 128 exceeds the SM count");
   if (static_cast<int64_t>(m->n_layers) * m->batch * m->n_kv * m->max_len >= (int64_t(1) << 31))
     return set_error(DK_ERR_INVALID, "step: the KV cache has too many rows");
   const void* ptrs[] = {m->embed, m->final_norm, m->lm_head, m->rope_cos, m->rope_sin, m->k_cache, m->v_cache};
@@ -1658,7 +1714,6 @@ extern "C" int dk_step_create(const dk_step_model* m, void* workspace, uint64_t 
            make_tensor_map_2d(&maps[idx + 2], z, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, N, K / 128, N * 2, 32, 2,
                               CU_TENSOR_MAP_SWIZZLE_NONE);
   };
-  uint32_t* attn_out = reinterpret_cast<uint32_t*>(ws + w.attn_out);
   uint32_t* qkv = reinterpret_cast<uint32_t*>(ws + w.qkv);
   uint32_t* o = reinterpret_cast<uint32_t*>(ws + w.o);
   uint32_t* act = reinterpret_cast<uint32_t*>(ws + w.act);
@@ -1722,7 +1777,6 @@ extern "C" int dk_step_create(const dk_step_model* m, void* workspace, uint64_t 
     a.kind = OP_ATTN;
     a.layer = l;
     a.x = qkv;
-    a.y = attn_out;
     a.cta0 = next_cta;
     a.ncta = 0;
     a.cache_row0 = l * M * m->n_kv * m->max_len;
@@ -1742,7 +1796,8 @@ extern "C" int dk_step_create(const dk_step_model* m, void* workspace, uint64_t 
     op.map = map;
     if (!int4_maps(map, y.o_qweight, y.o_scales, y.o_zeros, H, nqd)) return DK_ERR_CUDA;
     map += 3;
-    op.x = attn_out;
+    op.xattn = 1;
+    op.xp = reinterpret_cast<const unsigned long long*>(ws + w.attn_part);
     op.bias = static_cast<const __half*>(y.o_bias);
     op.y = o;
     op.xop = attn_op;
@@ -1863,6 +1918,15 @@ extern "C" int dk_step_create(const dk_step_model* m, void* workspace, uint64_t 
     cudaGetLastError();
     return set_error(DK_ERR_UNSUPPORTED, "step: the kernel does not fit on an SM");
   }
+  // the consumers' setmaxnreg.inc waits for registers the producer's warpgroup released: the launch
+  // must hold at least the split's total, or that wait would never end
+  cudaFuncAttributes fa{};
+  if (cudaFuncGetAttributes(&fa, decode_step_kernel) != cudaSuccess ||
+      fa.numRegs * kThreads < 128 * kProducerRegs + kConsumers * kConsumerRegs) {
+    cudaGetLastError();
+    return set_error(DK_ERR_UNSUPPORTED, "step: compiled with %d registers a thread, the register split needs %d",
+                     fa.numRegs, kLaunchRegs);
+  }
 
   dk_step_plan* plan = new dk_step_plan();
   Params& p = plan->params;
@@ -1893,9 +1957,7 @@ extern "C" int dk_step_create(const dk_step_model* m, void* workspace, uint64_t 
   p.epoch = ctr;
   p.exit_count = ctr + 1;
   p.head_count = ctr + 2;
-  p.attn_count = ctr + 4;
   p.attn_part = reinterpret_cast<unsigned long long*>(ws + w.attn_part);
-  p.attn_out = attn_out;
   p.head_val = reinterpret_cast<float*>(ws + w.head_val);
   p.head_idx = reinterpret_cast<int*>(ws + w.head_idx);
   p.err = dev.err_word;

@@ -136,13 +136,14 @@ class DecodeStep:
 
     def trace(self, tok: torch.Tensor, pos: torch.Tensor, hist: torch.Tensor | None = None) -> dict:
         """Run one step with dk_step_trace and summarize where its time goes (synchronizes; not for
-        use under capture). Per op kind, averaged over its ops: `span_us` from the previous op's last
-        arrival to this op's last arrival (the op's share of the step), `hop_us` from the previous op's
-        last arrival to this op's first ready CTA (the dependency round trip), and for the slowest CTA
-        `work_us` from ready to work done, split into `stage_us` (input staging), `products_us`
-        (weights x input) and `epilogue_us` (reduction, stores); `arrive_us` the fence + arrival of the
-        slowest CTA; `ring_wait_kcycles` the most cycles (thousands) any warp spent waiting for its
-        weights to land; plus the whole step's `step_us`."""
+        use under capture). Per op kind, averaged over its ops, in microseconds:
+        `span` - from the previous op's last finished CTA to this op's last (the op's share of the step);
+        for the median participating CTA: `input` - from the previous op's last CTA until this CTA had
+        its input staged (polling the tagged words plus staging), `staging` - from having the op's
+        descriptor to the input staged (includes waiting when the CTA was early), `products` - weights
+        x input, `epilogue` - reduction and stores; `tail` - last CTA minus the median CTA (stragglers);
+        `ring_wait_kcycles` - the most cycles any warp waited for its weights; `box_kcycles` - the median
+        CTA's first consumer warp's cycles for its boxes; plus `step_us`."""
         nbytes = ctypes.c_uint64(0)
         _lib.call("dk_step_trace_bytes", self._plan, ctypes.byref(nbytes))
         buf = torch.zeros(int(nbytes.value) // 8, dtype=torch.int64, device=tok.device)
@@ -158,34 +159,29 @@ class DecodeStep:
         step_us = float((t[:, n.value, 1].max() - t0) / 1e3)
         rows = {}
         prev_last = t0
-        keys = ("span_us", "hop_us", "work_us", "stage_us", "products_us", "epilogue_us", "arrive_us",
-                "ring_wait_kcycles", "attn_prologue_us", "attn_blocks_us", "attn_cta_combine_us", "attn_arrive_us",
-                "attn_slice_combine_us", "ctas")
+        keys = ("span", "input", "staging", "products", "epilogue", "tail", "ring_wait_kcycles", "box_kcycles", "ctas")
         for j in range(n.value):
             part = t[:, j, 1] > 0
             tj = t[part, j]
-            last = tj[:, 5].max()
+            done = tj[:, 4]
+            last = done.max()
+            med = float(done.median())
             r = rows.setdefault(self.KINDS.get(kinds[j], str(kinds[j])), dict.fromkeys(keys, 0.0) | {"n": 0})
             r["n"] += 1
-            r["span_us"] += float(last - prev_last) / 1e3
-            r["hop_us"] += float(tj[:, 1].min() - prev_last) / 1e3
-            slow = int((tj[:, 4] - tj[:, 1]).argmax())
-            w = tj[slow]
-            r["work_us"] += float(w[4] - w[1]) / 1e3
-            if w[2] > 0 and w[3] > 0:
-                r["stage_us"] += float(w[2] - w[1]) / 1e3
-                r["products_us"] += float(w[3] - w[2]) / 1e3
-                r["epilogue_us"] += float(w[4] - w[3]) / 1e3
-            r["arrive_us"] += float((tj[:, 5] - tj[:, 4]).max()) / 1e3
-            r["ring_wait_kcycles"] += float(tj[:, 6].max()) / 1e3  # slowest warp of any CTA
-            if kinds[j] == 2:  # attention phases of the slowest item CTA (first item of each CTA)
-                a = tj[(tj[:, 11] - tj[:, 1]).argmax()] if bool((tj[:, 11] > 0).any()) else tj[slow]
-                fin = a[11] if a[11] > 0 else a[10]
-                r["attn_prologue_us"] += float(a[7] - a[1]) / 1e3
-                r["attn_blocks_us"] += float(a[8] - a[7]) / 1e3
-                r["attn_cta_combine_us"] += float(a[9] - a[8]) / 1e3
-                r["attn_arrive_us"] += float(a[10] - a[9]) / 1e3
-                r["attn_slice_combine_us"] += float(fin - a[10]) / 1e3
+            r["span"] += float(last - prev_last) / 1e3
+            has_stage = tj[:, 2] > 0
+            if bool(has_stage.any()):
+                ts = tj[has_stage]
+                r["input"] += float((ts[:, 2] - prev_last).median()) / 1e3
+                r["staging"] += float((ts[:, 2] - ts[:, 1]).median()) / 1e3
+                r["products"] += float((ts[:, 3] - ts[:, 2]).median()) / 1e3
+                r["epilogue"] += float((ts[:, 4] - ts[:, 3]).median()) / 1e3
+                if kinds[j] not in (2, 6):
+                    r["box_kcycles"] += float(ts[:, 9].median()) / 1e3
+            else:  # attention: from the previous op to the median CTA's end
+                r["input"] += float(med - float(prev_last)) / 1e3
+            r["tail"] += float(last - med) / 1e3
+            r["ring_wait_kcycles"] += float(tj[:, 6].max()) / 1e3
             r["ctas"] += int(part.sum())
             prev_last = last
         for r in rows.values():

@@ -146,9 +146,9 @@ def consumer_walk(ops, cta, G, batch, n_kv, pos, warp):
         halves = 2 if kind == "gate_up" else 1
         nst = st1 - st0
         nunits = (c1 - c0) * nst
-        for u in range(warp, nunits, CWARPS):
-            for h in range(halves):
-                out.append((base + u * halves + h, (j, c0 + u // nst, st0 + u % nst, h)))
+        for b in range(warp, nunits * halves, CWARPS):  # boxes dealt to the warps one by one
+            u, h = divmod(b, halves)
+            out.append((base + b, (j, c0 + u // nst, st0 + u % nst, h)))
         base += nunits * halves
     return out
 
