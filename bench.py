@@ -51,8 +51,8 @@ def parse():
     ap.add_argument("--tp7b", choices=["auto", "on", "off"], default="auto",
                     help="Qwen2.5-7B tensor-parallel decode over the N ranks (BASELINE configs[4], TP=1 at N=1); "
                          "auto = on unless --no-extras")
-    ap.add_argument("--per-op", action="store_true",
-                    help="run the decode step as the per-op kernels instead of the fused decode-step kernel")
+    ap.add_argument("--fused-step", action="store_true",
+                    help="run the decode step as the single fused decode-step kernel instead of the per-op kernels")
     ap.add_argument("--tp-batches", default="1,8,32", help="batch sizes of the 7B tensor-parallel decode")
     return ap.parse_args()
 
@@ -244,26 +244,36 @@ def step_traffic():
 
 def parity_on_benchmark_model(model, ids, steps: int = 32) -> dict:
     """The north star's greedy-stream bar on the benchmark model itself: `steps` greedy tokens of the
-    fused step against the reference numerics (w4_ref: dequantize, cuBLAS fp16, SDPA), with the
-    reference's parity figures (kernels/e2e/run.py:289-303)."""
+    benchmarked per-op step (its layers and its lm_head + greedy-pick kernel) and of the fused step,
+    each against the reference numerics (w4_ref: dequantize, cuBLAS fp16, SDPA), with the reference's
+    parity figures (kernels/e2e/run.py:289-303)."""
     from kernels.e2e.model import QwenRunner, make_backend
     from kernels.e2e.run import greedy_parity
+    from kernels.head import KernelHeadLogits
     from kernels.step import StepLogits
 
-    ours = QwenRunner(model, make_backend("ours"), max_len=MAX_LEN)
-    ref = QwenRunner(model, make_backend("w4_ref"), max_len=MAX_LEN, fused_step=False)
-    r = greedy_parity(StepLogits(ours), ref, ids[:1], steps=steps)
-    del ours, ref
+    out = {"vs": "w4_ref (reference numerics)", "steps": steps, "prompt": ids.shape[1]}
+    ref = QwenRunner(model, make_backend("w4_ref"), max_len=MAX_LEN)
+    for name, fused, view in (("per_op", False, KernelHeadLogits), ("fused_step", True, StepLogits)):
+        ours = QwenRunner(model, make_backend("ours"), max_len=MAX_LEN, fused_step=fused)
+        ref.k_cache.zero_()
+        ref.v_cache.zero_()
+        r = greedy_parity(view(ours), ref, ids[:1], steps=steps)
+        del ours
+        torch.cuda.empty_cache()
+        tol = 5e-2 + 5e-2 * r["max_abs_ref_logit"]
+        ok = r["max_abs_logit_diff"] <= tol and (r["first_divergence"] == steps or r["ref_margin_at_divergence"] <= 2 * tol)
+        out[name] = {"max_abs_logit_diff": round(r["max_abs_logit_diff"], 5),
+                     "max_abs_ref_logit": round(r["max_abs_ref_logit"], 3), "first_divergence": r["first_divergence"],
+                     "ref_margin_at_divergence": r["ref_margin_at_divergence"], "tolerance": round(tol, 4),
+                     "pass": bool(ok)}
+    del ref
     torch.cuda.empty_cache()
-    tol = 5e-2 + 5e-2 * r["max_abs_ref_logit"]
-    ok = r["max_abs_logit_diff"] <= tol and (r["first_divergence"] == steps or r["ref_margin_at_divergence"] <= 2 * tol)
-    return {"vs": "w4_ref (reference numerics)", "steps": steps, "prompt": ids.shape[1],
-            "max_abs_logit_diff": round(r["max_abs_logit_diff"], 5), "max_abs_ref_logit": round(r["max_abs_ref_logit"], 3),
-            "first_divergence": r["first_divergence"], "ref_margin_at_divergence": r["ref_margin_at_divergence"],
-            "tolerance": round(tol, 4), "pass": bool(ok)}
+    out["pass"] = all(out[k]["pass"] for k in ("per_op", "fused_step"))
+    return out
 
 
-def decode_variant(model, backend: str, batch: int, steps: int, warmup: int, fused: bool = True,
+def decode_variant(model, backend: str, batch: int, steps: int, warmup: int, fused: bool = False,
                    l2_prefetch: bool = False) -> dict:
     """tok/s of another configs[3] variant on the same model (same prompt method, graph decoder)."""
     from kernels.e2e.model import QwenRunner, make_backend
@@ -577,10 +587,11 @@ def run_ours(args, world, rank, local):
     warmup = max(args.warmup, 3)
     assert PROMPT + warmup + args.steps + 8 < MAX_LEN, "steps + warmup exceed the cache"
     runner = QwenRunner(model, make_backend(args.backend), max_len=MAX_LEN, batch=args.batch,
-                        l2_prefetch=args.l2_prefetch, fused_step=not args.per_op)
+                        l2_prefetch=args.l2_prefetch, fused_step=args.fused_step)
     dec = GraphDecoder(runner)
     dec.capture(ids)
     fused = runner.step_kernel() is not None
+    runner_head = not fused and runner._kernel_head()
     with ClockSampler(local) as clocks:
         sec = time_decode(dec, ids, args.steps, warmup, world)
     sec = max_over_ranks(sec, world)
@@ -624,9 +635,10 @@ def run_ours(args, world, rank, local):
         if world == 1 and rank == 0:
             extras["parity"] = parity_on_benchmark_model(model, ids)
             variants = []
-            for kw in ({"backend": "ours", "batch": 1, "fused": False},
-                       {"backend": "ours", "batch": 1, "fused": False, "l2_prefetch": True},
+            for kw in ({"backend": "ours", "batch": 1, "fused": True},
+                       {"backend": "ours", "batch": 1, "l2_prefetch": True},
                        {"backend": "ours", "batch": 4},
+                       {"backend": "ours", "batch": 4, "fused": True},
                        {"backend": "ours", "batch": 16},
                        {"backend": "ours_fp8", "batch": 1},
                        {"backend": "ours_fp8", "batch": 16},
@@ -649,14 +661,15 @@ def run_ours(args, world, rank, local):
     if not args.no_extras and world == 1 and rank == 0:
         torch.cuda.empty_cache()
         extras["layer_sweep"] = layer_sweep(peaks)
-    # our kernels per token: the fused step is one launch; the per-op path runs per layer norm+qkv,
-    # attention, o_proj, norm+gate_up+SwiGLU, down (FP8: separate norm and SwiGLU kernels, 8 per
-    # layer), then the final norm and a quantized lm_head
+    # our kernels per token: the fused step is one launch; the per-op path runs the embedding kernel,
+    # per layer norm+qkv, attention, o_proj, norm+gate_up+SwiGLU, down (FP8: separate norm and SwiGLU
+    # kernels, 8 per layer), then the lm_head + greedy-pick kernel (a quantized lm_head instead: the
+    # final norm and its GEMV, with torch's embedding and argmax)
     if fused:
         per_step_launches = 1
     else:
         per_layer = 8 if args.backend.startswith("ours_fp8") else 5
-        per_step_launches = per_layer * 28 + 1 + (1 if args.backend.endswith("_lm") else 0)
+        per_step_launches = per_layer * 28 + (2 if runner_head else 2 if args.backend.endswith("_lm") else 1)
     if rank != 0:
         return None
     metric = METRIC if args.batch == 1 else METRIC.replace("batch 1", f"batch {args.batch}")

@@ -26,7 +26,7 @@ extern "C" {
 
 typedef struct CUstream_st* dk_stream_t; /* same type as cudaStream_t */
 
-#define DK_ABI_VERSION 4
+#define DK_ABI_VERSION 5
 
 /* status codes */
 #define DK_OK 0
@@ -39,10 +39,10 @@ typedef struct CUstream_st* dk_stream_t; /* same type as cudaStream_t */
 #define DK_DEVERR_NONE 0
 #define DK_DEVERR_WAIT_FULL 1  /* a consumer gave up waiting for a stage's copies */
 #define DK_DEVERR_WAIT_EMPTY 2 /* the producer gave up waiting for a stage to be released */
-#define DK_DEVERR_BAD_POSITION 3 /* decode attention: position outside [0, max_len) (no write done) */
+#define DK_DEVERR_BAD_POSITION 3 /* decode attention / lm_head greedy: position outside the cache or history (no write done) */
 #define DK_DEVERR_TP_WAIT 4      /* a fused-allreduce CTA gave up waiting for a peer's partial sums */
 #define DK_DEVERR_STEP_WAIT 5    /* decode step: a CTA gave up waiting for another CTA or for its weight ring */
-#define DK_DEVERR_BAD_TOKEN 6    /* decode step: a token id outside [0, vocab) (row 0 used instead) */
+#define DK_DEVERR_BAD_TOKEN 6    /* decode step / embed tokens: a token id outside [0, vocab) (row 0 used instead) */
 
 /* dk_matmul_config.flags */
 #define DK_FLAG_STATIC_WEIGHTS 1 /* weights are not written by any kernel still in flight on the
@@ -193,6 +193,29 @@ int dk_decode_attention(const void* qkv, void* k_cache, void* v_cache, const int
                         int64_t nkv, int64_t head_dim, int64_t max_len, int64_t rope_stride,
                         int32_t splits, int32_t flags, dk_stream_t stream);
 
+/* ---- lm_head + greedy pick of a decode step: kernels/e2e/model.py:248-253, run.py:69-74 ---- */
+/* The tail of the reference's T == 1 forward and its graph decoder's greedy bookkeeping in one
+ * kernel: the final RMSNorm (h = x + residual in fp16 with the rounding of kernels/rmsnorm.py:28-37;
+ * residual and norm_weight may be NULL: no add, no norm), logits = fp16(h lm_head^T) accumulated in
+ * fp32 (lm_head fp16 [vocab, hidden], tied to the embedding or not), and the greedy pick of every row
+ * - the first maximum of its fp16 logits, torch.argmax's rule - stored to tokens[M] (device int64).
+ * With history != NULL also history[m * history_ld + *pos] = pick, and with pos != NULL *pos += 1 (a
+ * position outside [0, history_len) writes no history, leaves *pos and sets DK_DEVERR_BAD_POSITION);
+ * logits [M, vocab] fp16 or NULL. 1 <= M <= 8, hidden % 8 == 0, 16-byte aligned x, residual, norm weight and
+ * lm_head. The workspace (dk_lm_head_greedy_workspace_bytes, 256-byte aligned, zeroed once before the
+ * first call) holds an arrival counter that each call leaves at zero, so calls sharing a workspace
+ * must be ordered on one stream. */
+int dk_lm_head_greedy_workspace_bytes(uint64_t* bytes);
+int dk_lm_head_greedy(const void* x, const void* residual, const void* norm_weight, float eps,
+                      const void* lm_head, int64_t vocab, int64_t hidden, int64_t M, int64_t* tokens,
+                      int64_t* pos, int64_t* history, int64_t history_ld, int64_t history_len,
+                      void* logits, void* workspace, uint64_t workspace_bytes, dk_stream_t stream);
+/* The embedding lookup at the head of the forward (kernels/e2e/model.py:227, F.embedding):
+ * out[m] = embed[tokens[m]] for device int64 tokens [M]; an id outside [0, vocab) takes row 0 and
+ * sets DK_DEVERR_BAD_TOKEN. hidden % 8 == 0, 16-byte aligned embed and out. */
+int dk_embed_tokens(const int64_t* tokens, const void* embed, int64_t vocab, int64_t hidden, int64_t M,
+                    void* out, dk_stream_t stream);
+
 /* ---- fused decode step: one persistent kernel per token ------------------------------------
  * One greedy decode step of a Qwen2 model with W4A16 linears and a tied or untied fp16 lm_head, for
  * 1..4 sequences: the reference runner's T == 1 forward (kernels/e2e/model.py:216-253: embedding,
@@ -201,7 +224,8 @@ int dk_decode_attention(const void* qkv, void* k_cache, void* v_cache, const int
  * greedy step of its graph decoder (kernels/e2e/run.py:69-74: argmax, token feedback, position
  * bump), as ONE cooperative kernel with one CTA per SM. Each CTA's producer warp streams its share
  * of every op's weights into shared memory ahead of the op's input (the weights are constant), and
- * the ops meet through arrival counters in the workspace. Numerics are those of the separate
+ * the ops meet through tagged activation words in the workspace (each value carries the step and op
+ * that wrote it; readers poll until the tags match). Numerics are those of the separate
  * kernels: dk_w4a16_rmsnorm_matmul / dk_w4a16_matmul (factored int4), dk_decode_attention,
  * dk_rmsnorm, and an fp16 lm_head with fp32 accumulation rounded to fp16 before the argmax (ties to
  * the lowest index, like torch.argmax). No reference counterpart as one kernel.

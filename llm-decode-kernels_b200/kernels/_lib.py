@@ -79,6 +79,9 @@ SIGNATURES = {
     "dk_rmsnorm": [P, I64, P, I64, P, P, I64, P, I64, I64, I64, F32, P],
     "dk_swiglu": [P, I64, P, I64, P, I64, I64, I64, P],
     "dk_decode_attention": [P, P, P, P, P, P, P, I64, I64, I64, I64, I64, I64, I32, I32, P],
+    "dk_lm_head_greedy_workspace_bytes": [ctypes.POINTER(ctypes.c_uint64)],
+    "dk_lm_head_greedy": [P, P, P, F32, P, I64, I64, I64, P, P, P, I64, I64, P, P, ctypes.c_uint64, P],
+    "dk_embed_tokens": [P, P, I64, I64, I64, P, P],
     "dk_tp_buffer_bytes": [I32, I64, I64, ctypes.POINTER(ctypes.c_uint64)],
     "dk_tp_buffer_alloc": [ctypes.c_uint64, ctypes.POINTER(P), P],
     "dk_tp_buffer_free": [P],

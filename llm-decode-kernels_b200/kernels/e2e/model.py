@@ -223,11 +223,13 @@ class Layer:
 
 class QwenRunner:
     """Qwen2 forward on a static KV cache (reference model.py:150-253): the T == 1 decode path runs
-    the backend's fused kernels, longer inputs the reference's numerics (SDPA over the cache); a
-    greedy step (`greedy_step`) of the W4A16 runner at batch <= 4 is one fused kernel."""
+    the backend's fused kernels, longer inputs the reference's numerics (SDPA over the cache). A
+    greedy step (`greedy_step`) on the kernel backends is the embedding kernel, five kernels per layer
+    and one lm_head + greedy-pick kernel (batch <= 8, fp16 lm_head), or with fused_step=True the
+    single decode-step kernel of the W4A16 runner at batch <= 4."""
 
     def __init__(self, hf_model, backend: Backend, max_len: int = 2048, batch: int = 1,
-                 l2_prefetch: bool = False, tp=None, fused_step: bool = True):
+                 l2_prefetch: bool = False, tp=None, fused_step: bool = False):
         """tp: a kernels.tp.TensorParallel to hold only this rank's shards (column-sharded qkv,
         gate_up and lm_head; row-sharded o_proj and down, reduced over the group), or None.
         fused_step: run greedy_step as the single decode-step kernel where it supports the model."""
@@ -241,6 +243,7 @@ class QwenRunner:
         self.batch = batch
         self.fused_step = fused_step
         self._step_kernel = None
+        self._head_ws = None  # workspace of the lm_head + greedy-pick kernel (made on first use)
         m = hf_model.model
         dev = m.embed_tokens.weight.device
         self.embed = m.embed_tokens.weight
@@ -376,6 +379,18 @@ class QwenRunner:
             self._step_kernel = step.DecodeStep(self)
         return self._step_kernel
 
+    def _kernel_head(self) -> bool:
+        """Does the per-op greedy step end in the lm_head + greedy-pick kernel (kernel backend, one
+        rank, fp16 lm_head, batch <= 8)? Makes its workspace on first use (before any capture)."""
+        from kernels import head
+
+        ok = (self.backend.fused_decode and self.tp is None and self.head_q is None and self.batch <= head.MAX_ROWS
+              and self.embed.dtype == torch.float16 and self.lm_head.dtype == torch.float16
+              and self.embed.shape[1] % 8 == 0)
+        if ok and self._head_ws is None:
+            self._head_ws = head.workspace(self.embed.device)
+        return ok
+
     @torch.no_grad()
     def greedy_step(self, tok: torch.Tensor, pos: torch.Tensor, out: torch.Tensor) -> None:
         """One greedy decode step on device state (the reference's GraphDecoder._step,
@@ -384,6 +399,15 @@ class QwenRunner:
         fused = self.step_kernel()
         if fused is not None:
             fused(tok, pos, out)
+            return
+        if self._kernel_head():
+            from kernels import head
+
+            B, H = tok.shape[0], self.embed.shape[1]
+            x = head.embed_tokens(tok, self.embed)
+            h, residual = self._decode_layers(x, pos)
+            head.lm_head_greedy(h.reshape(B, H), residual.reshape(B, H), self.final_norm, self.eps, self.lm_head,
+                                tok, self._head_ws, pos=pos, history=out)
             return
         pick = self.greedy(self.forward(tok, pos)).view(-1, 1)
         out.index_copy_(1, pos, pick)

@@ -36,8 +36,8 @@ def small_model(seed=0, layers=2):
 def _pair(model, batch, max_len):
     from kernels.e2e.model import QwenRunner, make_backend
 
-    fused = QwenRunner(model, make_backend("ours"), max_len=max_len, batch=batch)
-    plain = QwenRunner(model, make_backend("ours"), max_len=max_len, batch=batch, fused_step=False)
+    fused = QwenRunner(model, make_backend("ours"), max_len=max_len, batch=batch, fused_step=True)
+    plain = QwenRunner(model, make_backend("ours"), max_len=max_len, batch=batch)
     assert fused.step_kernel() is not None and plain.step_kernel() is None
     return fused, plain
 
@@ -104,11 +104,11 @@ def test_step_rejects_unsupported_runners():
     from kernels.e2e.model import QwenRunner, make_backend
 
     model = small_model(seed=2)
-    assert step.supported(QwenRunner(model, make_backend("ours"), max_len=256, batch=8)) is not None
-    assert step.supported(QwenRunner(model, make_backend("ours_lm"), max_len=256)) is not None
-    assert step.supported(QwenRunner(model, make_backend("ours"), max_len=200)) is not None
+    assert step.supported(QwenRunner(model, make_backend("ours"), max_len=256, batch=8, fused_step=True)) is not None
+    assert step.supported(QwenRunner(model, make_backend("ours_lm"), max_len=256, fused_step=True)) is not None
+    assert step.supported(QwenRunner(model, make_backend("ours"), max_len=200, fused_step=True)) is not None
     with pytest.raises(RuntimeError, match="unavailable"):
-        step.DecodeStep(QwenRunner(model, make_backend("fp16"), max_len=256))
+        step.DecodeStep(QwenRunner(model, make_backend("fp16"), max_len=256, fused_step=True))
 
 
 def test_step_bad_position_writes_nothing():
@@ -148,10 +148,10 @@ def test_step_greedy_stream_on_benchmark_model():
     model = random_qwen2(config.QWEN15, dtype=torch.float16, device="cuda", seed=0)
     ids = torch.randint(0, config.QWEN15["vocab_size"], (1, 512), generator=torch.Generator().manual_seed(1)).cuda()
 
-    fused = QwenRunner(model, make_backend("ours"), max_len=2048)
+    fused = QwenRunner(model, make_backend("ours"), max_len=2048, fused_step=True)
     assert fused.step_kernel() is not None
     for ref_name in ("ours", "w4_ref"):
-        ref = QwenRunner(model, make_backend(ref_name), max_len=2048, fused_step=False)
+        ref = QwenRunner(model, make_backend(ref_name), max_len=2048)
         fused.k_cache.zero_()
         fused.v_cache.zero_()
         r = greedy_parity(StepLogits(fused), ref, ids, steps=32)
