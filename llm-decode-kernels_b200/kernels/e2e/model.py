@@ -225,7 +225,7 @@ class QwenRunner:
     """Qwen2 forward on a static KV cache (reference model.py:150-253): the T == 1 decode path runs
     the backend's fused kernels, longer inputs the reference's numerics (SDPA over the cache). A
     greedy step (`greedy_step`) on the kernel backends is the embedding kernel, five kernels per layer
-    and one lm_head + greedy-pick kernel (batch <= 8, fp16 lm_head), or with fused_step=True the
+    and one lm_head + greedy-pick kernel (batch 1, fp16 lm_head), or with fused_step=True the
     single decode-step kernel of the W4A16 runner at batch <= 4."""
 
     def __init__(self, hf_model, backend: Backend, max_len: int = 2048, batch: int = 1,
@@ -381,10 +381,10 @@ class QwenRunner:
 
     def _kernel_head(self) -> bool:
         """Does the per-op greedy step end in the lm_head + greedy-pick kernel (kernel backend, one
-        rank, fp16 lm_head, batch <= 8)? Makes its workspace on first use (before any capture)."""
+        rank, fp16 lm_head, batch 1)? Makes its workspace on first use (before any capture)."""
         from kernels import head
 
-        ok = (self.backend.fused_decode and self.tp is None and self.head_q is None and self.batch <= head.MAX_ROWS
+        ok = (self.backend.fused_decode and self.tp is None and self.head_q is None and self.batch <= head.RUNNER_ROWS
               and self.embed.dtype == torch.float16 and self.lm_head.dtype == torch.float16
               and self.embed.shape[1] % 8 == 0)
         if ok and self._head_ws is None:

@@ -17,6 +17,9 @@ import torch
 from kernels import _lib
 
 MAX_ROWS = 8
+# rows up to which the runner's per-op step ends in lm_head_greedy: its fp32 FMA form streams the
+# lm_head at ~98% of HBM bandwidth for one row, but more rows make it compute-bound (cuBLAS then wins)
+RUNNER_ROWS = 1
 
 
 def workspace(device) -> torch.Tensor:

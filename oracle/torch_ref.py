@@ -19,7 +19,7 @@ def pack_int4(q: torch.Tensor) -> torch.Tensor:
     32-bit word, read as a signed int32 (kernels/quant.py:20-28)."""
     K, N = q.shape
     rows = q.to(torch.int64).reshape(K // 8, 8, N)
-    word = (rows << torch.arange(0, 32, 4, dtype=torch.int64).view(1, 8, 1)).sum(dim=1)
+    word = (rows << torch.arange(0, 32, 4, dtype=torch.int64, device=q.device).view(1, 8, 1)).sum(dim=1)
     return (word - ((word >> 31) << 32)).to(torch.int32)
 
 
@@ -39,7 +39,7 @@ def quantize_rtn(weight: torch.Tensor, group_size: int = 128):
 
 def unpack_int4(packed: torch.Tensor) -> torch.Tensor:
     """int32 [K/8, N] -> int32 [K, N]: nibble i of each word is K index 8r + i."""
-    shifts = torch.arange(0, 32, 4, dtype=torch.int32).view(1, 8, 1)
+    shifts = torch.arange(0, 32, 4, dtype=torch.int32, device=packed.device).view(1, 8, 1)
     return ((packed.unsqueeze(1) >> shifts) & 0xF).reshape(-1, packed.shape[1])
 
 
