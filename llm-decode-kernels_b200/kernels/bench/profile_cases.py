@@ -18,6 +18,9 @@
     python .../profile_cases.py config_sweep [M]
         the cost model's GEMV choice against every BLOCK_N x SPLIT_K of one decoder layer's four
         launches, and the lm_head-shaped GEMV at three widths.
+    python .../profile_cases.py head [rows] [launches]
+        the lm_head + greedy-pick kernel on the tied Qwen2.5-1.5B lm_head, timed (CUDA events) against
+        cuBLAS F.linear + torch.argmax; the profiler range holds the kernel's timed launches.
     python .../profile_cases.py step [layers] [steps] [batch]
         the fused decode-step kernel on a Qwen2.5-1.5B-shaped model with `layers` layers (4 by
         default: ~0.6 GB of weights incl. the fp16 lm_head) at context 512: 3 warm-up steps, then
@@ -272,7 +275,7 @@ def step(layers="4", steps="2", batch="1"):
     arch = dict(config.QWEN15, num_hidden_layers=layers)
     model = random_qwen2(arch, dtype=torch.float16, device="cuda", seed=0)
     ids = torch.randint(0, arch["vocab_size"], (batch, 512), device="cuda")
-    runner = QwenRunner(model, make_backend("ours"), max_len=2048, batch=batch)
+    runner = QwenRunner(model, make_backend("ours"), max_len=2048, batch=batch, fused_step=True)
     dec = GraphDecoder(runner)
     dec.prefill(ids)
     kernel = runner.step_kernel()
@@ -290,7 +293,43 @@ def step(layers="4", steps="2", batch="1"):
     print("step ok", dec.pos.item())
 
 
-CASES = {"step": step, "decode": decode, "gemv_layer": gemv_layer, "gemv": gemv, "attention": attention, "gemm": gemm, "chain": chain, "attention_sweep": attention_sweep, "small_m": small_m, "config_sweep": config_sweep}
+def head(rows="1", launches="50"):
+    """The lm_head + greedy-pick kernel on the tied Qwen2.5-1.5B lm_head (151936 x 1536 fp16,
+    467 MB: larger than L2 by itself): 3 warm-up launches, then `launches` timed with CUDA events
+    inside the profiler range, against cuBLAS F.linear + torch.argmax on the same operands."""
+    from kernels import _lib
+    from kernels import head as hd
+    import torch.nn.functional as F
+
+    M, n = int(rows), int(launches)
+    V, H = config.QWEN15["vocab_size"], config.QWEN15["hidden_size"]
+    W = (torch.randn(V, H, device="cuda") * 0.05).half()
+    x, res = torch.randn(M, H, device="cuda").half(), torch.randn(M, H, device="cuda").half()
+    w = torch.ones(H, device="cuda").half()
+    ws, tok = hd.workspace("cuda"), torch.empty(M, dtype=torch.int64, device="cuda")
+    out = {}
+    for name, fn in (("lm_head_greedy", lambda: hd.lm_head_greedy(x, res, w, 1e-6, W, tok, ws)),
+                     ("cublas_linear_argmax", lambda: F.linear(x, W).argmax(-1))):
+        for _ in range(3):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        if name == "lm_head_greedy":
+            torch.cuda.profiler.start()
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        if name == "lm_head_greedy":
+            torch.cuda.profiler.stop()
+        us = e0.elapsed_time(e1) / n * 1e3
+        out[name] = f"{us:.2f} us, {V * H * 2 / us / 1e3:.0f} GB/s"
+    assert _lib.device_error() == 0
+    print(f"rows {M}:", out)
+
+
+CASES = {"head": head, "step": step, "decode": decode, "gemv_layer": gemv_layer, "gemv": gemv, "attention": attention, "gemm": gemm, "chain": chain, "attention_sweep": attention_sweep, "small_m": small_m, "config_sweep": config_sweep}
 
 if __name__ == "__main__":
     if len(sys.argv) < 2 or sys.argv[1] not in CASES:
