@@ -35,6 +35,11 @@ TC_MIN_ROWS = 128  # rows from which dk_w4a16_matmul runs the tensor-core GEMM
 # rows above which the fused norm / SwiGLU entry points run as separate kernels around the tcgen05
 # small-M GEMM (16 < M < 128) or the prefill GEMM instead of looping the fused decode GEMV per 16 rows
 SPLIT_FUSED_ROWS = 16
+# rows up to which w4a16_rmsnorm_matmul runs the norm inside the projection's kernel: every CTA of that
+# kernel reduces all rows itself, which beats a separate RMSNorm launch (one CTA per row) only for one
+# or two rows (B200, Qwen2.5-1.5B shapes: at 4 rows the two kernels are 1.0-1.8 us faster, at 16 rows
+# 5.9-6.1 us); config {"FUSED_NORM": True} keeps the single kernel at any row count it supports
+FUSED_NORM_ROWS = 2
 
 
 def _check_weight_shapes(what, K, N, scales, zeros, group_size, bias):
@@ -163,6 +168,8 @@ def w4a16_rmsnorm_matmul(x, norm_weight, eps, residual, qweight, scales, zeros, 
     I = N // 2
     tensors = [x2, qweight, scales, zeros, norm_weight] + ([r2] if r2 is not None else [])
     big = M > SPLIT_FUSED_ROWS and not cfg.flags & _lib.FLAG_GEMV
+    if M > FUSED_NORM_ROWS and not (config or {}).get("FUSED_NORM"):
+        big = True
     fast = (group_size == 128 and N % 8 == 0 and (not swiglu or I % 32 == 0) and not cfg.flags & _lib.FLAG_GENERIC
             and not big
             and all(t.data_ptr() % 16 == 0 for t in tensors) and x2.stride(0) % 8 == 0

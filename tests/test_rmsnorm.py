@@ -101,7 +101,9 @@ def test_rmsnorm_fused_into_matmul(M, N, K, swiglu, with_res):
     x, r, w = _inputs(M, K, seed=7)
     _, qw, s, z, b = w4_case(M, N, K, bias=not swiglu)
     xc, rc, wc, qc, sc, zc, bc = to_cuda(x, r, w, qw, s, z, b)
-    y, res = w4a16_rmsnorm_matmul(xc, wc, 1e-6, rc if with_res else None, qc, sc, zc, bias=bc, swiglu=swiglu)
+    # FUSED_NORM: the single kernel at every row count here (by default only up to 2 rows)
+    y, res = w4a16_rmsnorm_matmul(xc, wc, 1e-6, rc if with_res else None, qc, sc, zc, bias=bc, swiglu=swiglu,
+                                  config={"FUSED_NORM": True})
     if with_res:
         xn, r_ref = ref.rmsnorm_ref(x, w, 1e-6, residual=r)
         assert np.array_equal(bits16(res), bits16(r_ref))
