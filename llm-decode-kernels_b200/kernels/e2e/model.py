@@ -98,11 +98,13 @@ class OursBackend(Backend):
     fused_decode = True
     # weights of a runner never change: let each kernel prefetch them before the previous ends
     LINEAR_CFG = {"STATIC_WEIGHTS": True}
-    # the one-row norm + gate_up + SwiGLU launch in 64-column tiles (gate and up chunk pairs): in the
-    # decode step it then leaves room on the SMs for the down projection's CTAs to start early and
-    # stream their weights (B200, Qwen2.5-1.5B: 0.873 -> 0.827 ms per token; the cost model, which
-    # sees one launch at a time, picks a tiling that fills every SM)
-    GATE_UP_ONE_ROW = {"BLOCK_N": 64}
+    # the (norm +) gate_up + SwiGLU launch of up to 4 rows in 64-column tiles (gate and up chunk
+    # pairs): in the decode step it then leaves room on the SMs for the down projection's CTAs to
+    # start early and stream their weights (B200, Qwen2.5-1.5B, ms per step: batch 1 0.873 -> 0.827,
+    # batch 2 0.945 -> 0.911, batch 4 1.162 -> 1.137; the cost model, which sees one launch at a
+    # time, picks a tiling that fills every SM)
+    GATE_UP_SMALL_M = {"BLOCK_N": 64}
+    GATE_UP_SMALL_M_ROWS = 4
 
     def __init__(self, decode_kernel: str = "triton"):
         self.decode_kernel = decode_kernel
@@ -133,7 +135,7 @@ class OursBackend(Backend):
 
     def gate_up_cfg(self, x, p: Linear) -> dict:
         cfg = self.cfg(p)
-        return {**cfg, **self.GATE_UP_ONE_ROW} if x.numel() == x.shape[-1] else cfg
+        return {**cfg, **self.GATE_UP_SMALL_M} if x.numel() <= self.GATE_UP_SMALL_M_ROWS * x.shape[-1] else cfg
 
     def gate_up_act(self, x, p: Linear):
         from kernels.w4a16 import w4a16_swiglu
