@@ -1139,9 +1139,10 @@ extern "C" int dk_w4a16_matmul(const void* x, int64_t ldx, const int32_t* qweigh
   }
   if (!(flags & DK_FLAG_GEMV) && gemm_tc_ok(x, ldx, y, ldy, M, N, K, group_size))
     return launch_gemm_tc(x, ldx, qweight, scales, zeros, bias, y, ldy, M, N, K, st);
-  // batched decode: tcgen05 swap-AB for 16 <= M < 128; at exactly 16 rows with K < 4096 the decode GEMV
-  // measured 0.7 us faster (qkv, o_proj shapes), at K >= 4096 the tcgen05 kernel is ~2x faster (down)
-  if (!(flags & DK_FLAG_GEMV) && M >= 16 && N >= 128 && (M > 16 || K >= 4096)) {
+  // batched decode: tcgen05 swap-AB for 16 < M < 128; at 9-16 rows with K < 4096 the decode GEMV
+  // measured faster (qkv, o_proj shapes), at K >= 4096 the tcgen05 kernel is much faster (down at 12
+  // rows: 14 us against 22 us for the GEMV, which walks the long K with 16-row MMA tiles)
+  if (!(flags & DK_FLAG_GEMV) && M > 8 && N >= 128 && (M > 16 || K >= 4096)) {
     int mb = 0, split = 0;
     skinny_choice(M, N, K, &mb, &split);
     if (mb != 0)

@@ -98,11 +98,12 @@ def test_prefill_swiglu_and_norm_paths():
 
 
 # ----------------------------------------------------------- small-M (batched decode) tensor-core path
-@pytest.mark.parametrize("M", [16, 17, 24, 32, 40, 64, 65, 100, 127])
+@pytest.mark.parametrize("M", [9, 12, 16, 17, 24, 32, 40, 64, 65, 100, 127])
 @pytest.mark.parametrize("N,K", [(2048, 1536), (1536, 8960), (3584, 2432), (256, 4096)])
 def test_small_m_tcgen05_matches_oracle(M, N, K):
-    """16 <= M < 128 rows run the swap-AB tcgen05 kernel (batch rows as the MMA's N, cluster split-K):
-    the oracle's tolerance, deterministic."""
+    """16 < M < 128 rows, and 9-16 rows with K >= 4096, run the swap-AB tcgen05 kernel (batch rows as
+    the MMA's N, cluster split-K; the other shapes here the decode GEMV): the oracle's tolerance,
+    deterministic."""
     from kernels.w4a16 import w4a16_matmul
 
     x, qw, s, z, b = w4_case(M, N, K, seed=M * 3 + N, bias=True)
