@@ -212,6 +212,9 @@ __device__ __forceinline__ uint2 ld_volatile_v2(const uint32_t* p) {
   return v;
 }
 
+// Pull the 128-byte line holding p into L2 (a hint; no data returns to the thread).
+__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
 // ------------------------------------------------------------- programmatic dependent launch
 // Wait until the preceding kernel on the stream (if it was launched as our PDL primary) has
 // completed and its writes are visible. A no-op when there is no such kernel.

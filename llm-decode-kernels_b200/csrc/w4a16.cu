@@ -440,8 +440,27 @@ __device__ __forceinline__ void consume_chunk_stage_f(uint32_t wbox, uint32_t sz
 // of this library): h = x + residual (fp16 add), var = sum(h^2)/K in fp32, out = w * fp16(h / sqrt(
 // var + eps)); every CTA reads the whole row for the sum of squares (per-warp partials added in a
 // fixed order: deterministic), and `writer` (one CTA) stores h as the new residual stream.
+// The norm weights of the blocks this thread stages in a one-row launch (blocks kb0 + tid and
+// kb0 + tid + 256 of its K slice): constant, so they are loaded before the wait for the previous
+// kernel and are in registers when the normalization needs them.
+struct NormW {
+  uint4 w[2];
+};
+__device__ __forceinline__ NormW norm_w_prefetch(const GemvParams& p, int s_begin) {
+  constexpr int kThr = kWarps * 32;
+  NormW r;
+  r.w[0] = r.w[1] = make_uint4(0, 0, 0, 0);
+  if (p.norm_w == nullptr || p.M != 1) return r;
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int k = (s_begin * kStageRows + static_cast<int>(threadIdx.x) + j * kThr) * 8;
+    if (k < p.K) r.w[j] = __ldg(reinterpret_cast<const uint4*>(p.norm_w + k));
+  }
+  return r;
+}
+
 __device__ __forceinline__ void stage_x(const GemvParams& p, uint8_t* xs, float* cx, int s_begin, int nst, bool writer,
-                                        bool factored) {
+                                        bool factored, const NormW& nwp) {
   constexpr int kThr = kWarps * 32;
   const int tid = threadIdx.x;
   const int kb0 = s_begin * kStageRows;  // first packed row (block of 8 K values)
@@ -517,7 +536,9 @@ __device__ __forceinline__ void stage_x(const GemvParams& p, uint8_t* xs, float*
 #pragma unroll
           for (int j = 0; j < 4; ++j) vh[j] = __hadd2_rn(vh[j], rh[j]);
         }
-        const uint4 wv = __ldg(reinterpret_cast<const uint4*>(p.norm_w + k));
+        // one row: block b of the slice is this thread's block tid + j * kThr (prefetched above)
+        const uint4 wv = (p.M == 1 && b < 2 * kThr) ? (b < kThr ? nwp.w[0] : nwp.w[1])
+                                                    : __ldg(reinterpret_cast<const uint4*>(p.norm_w + k));
         const __half2* wh = reinterpret_cast<const __half2*>(&wv);
         const float s = inv[m];
 #pragma unroll
@@ -639,10 +660,18 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 3 - NT)  // M <= 8: two CTA
     __syncwarp();
   } else {
     // ---------------------------------------------------------------- consumer warps
+    const NormW nwp = norm_w_prefetch(p, s_begin);
+    if (p.bias != nullptr) {  // this CTA's bias columns into L2 while the previous kernel finishes
+      const int n_lo = c_begin * 32, n_hi = min(c_end * 32, swiglu ? p.swiglu_i : p.N);
+      for (int n = n_lo + 64 * static_cast<int>(threadIdx.x); n < n_hi; n += 64 * kWarps * 32) {
+        prefetch_l2(p.bias + n);
+        if (swiglu) prefetch_l2(p.bias + p.swiglu_i + n);
+      }
+    }
     pdl_wait();  // x (and the residual) come from the previous kernels
     if (p.tp.world > 0 && threadIdx.x == 0) s_ep = *reinterpret_cast<volatile unsigned long long*>(p.tp.epoch) + 1;
     stage_x(p, smem + L.xs_off, reinterpret_cast<float*>(smem + L.cx_off), s_begin, nst,
-            blockIdx.x == 0 && blockIdx.y == 0, !EXACT);  // ends with a barrier
+            blockIdx.x == 0 && blockIdx.y == 0, !EXACT, nwp);  // ends with a barrier
     const unsigned long long ep = s_ep;
     const int g = lane >> 2;  // MMA group: A rows g, g+8 ; B column g
     const int t = lane & 3;   // thread in group: K slots 2t.., 2t+8..
