@@ -26,7 +26,7 @@ extern "C" {
 
 typedef struct CUstream_st* dk_stream_t; /* same type as cudaStream_t */
 
-#define DK_ABI_VERSION 5
+#define DK_ABI_VERSION 6
 
 /* status codes */
 #define DK_OK 0
@@ -138,6 +138,28 @@ int dk_w4a16_rmsnorm_matmul(const void* x, int64_t ldx, const void* residual, in
                             const void* bias, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
                             int64_t group_size, int32_t swiglu, const dk_matmul_config* cfg,
                             dk_stream_t stream);
+
+/* A split-K projection handing its partial sums to the next projection, instead of reducing them
+ * itself (the reference's decode step, kernels/e2e/model.py:247 then :231-235, passes the complete
+ * fp16 down_proj output to the next layer's norm + qkv; no single-function counterpart):
+ * dk_w4a16_matmul_partials writes x[M, K] @ dequant(W)^T as the fp32 partial sums of the launch's K
+ * slices, partials[s][m][n] for s < *nparts (the split the library chose for this shape, set on the
+ * host before the call returns; 1 = the whole sum), without bias; capacity is the buffer's size in
+ * floats (8 * M * N always suffices). dk_w4a16_rmsnorm_matmul_partials is dk_w4a16_rmsnorm_matmul
+ * with x = fp16(parts[0] + ... + parts[nparts - 1] (+ part_bias)), the additions in slice order, as
+ * the projection's own reduction makes them: the pair computes the same values as dk_w4a16_matmul
+ * followed by dk_w4a16_rmsnorm_matmul, in one dependency step fewer (no cluster reduction).
+ * 1 <= M <= 16 rows in one launch, the fast path's conditions, 16-byte aligned buffers. */
+int dk_w4a16_matmul_partials(const void* x, int64_t ldx, const int32_t* qweight, const void* scales,
+                             const void* zeros, int64_t M, int64_t N, int64_t K, int64_t group_size,
+                             float* partials, int64_t capacity, int32_t* nparts,
+                             const dk_matmul_config* cfg, dk_stream_t stream);
+int dk_w4a16_rmsnorm_matmul_partials(const float* parts, int32_t nparts, const void* part_bias,
+                                     const void* residual, int64_t ldr, const void* norm_weight, float eps,
+                                     void* residual_out, int64_t ldro, const int32_t* qweight,
+                                     const void* scales, const void* zeros, const void* bias, void* y,
+                                     int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group_size,
+                                     int32_t swiglu, const dk_matmul_config* cfg, dk_stream_t stream);
 
 /* ---- FP8 e4m3 weight-only format: kernels/fp8.py ------------------------------------------ */
 /* quantize_fp8 (kernels/fp8.py:25-30): w fp16 [N, K] (row stride ldw) -> wq e4m3 [K, N],

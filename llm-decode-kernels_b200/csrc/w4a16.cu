@@ -76,6 +76,13 @@ struct GemvParams {
   float eps;
   int* err;
   L2Prefetch pf;  // ranges to pull into L2 for a later launch (a hint)
+  // x given as the fp32 K-slice partial sums of the previous projection (xp != nullptr): x = fp16(
+  // xp[0] + ... + xp[xparts - 1] (+ xbias)), each [M, K], added in slice order
+  const float* xp;
+  int xparts;
+  const __half* xbias;
+  // this launch's K-slice partial sums instead of y (yp != nullptr, no bias): yp[slice][M][N] fp32
+  float* yp;
   TPArgs tp;      // tp.world > 0: row-sharded launch with the allreduce fused in (see tp_finish)
 };
 
@@ -459,6 +466,36 @@ __device__ __forceinline__ NormW norm_w_prefetch(const GemvParams& p, int s_begi
   return r;
 }
 
+// 8 values of x at row m, K offset k (k % 8 == 0): the activations, or the rounded sum of the
+// previous projection's partial sums (the same additions in the same order as its cluster reduction).
+__device__ __forceinline__ uint4 load_x8(const GemvParams& p, int m, int k) {
+  if (p.xp == nullptr) return __ldcg(reinterpret_cast<const uint4*>(p.x + m * p.ldx + k));
+  float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int q = 0; q < p.xparts; ++q) {
+    const float4* src = reinterpret_cast<const float4*>(p.xp + (static_cast<int64_t>(q) * p.M + m) * p.K + k);
+    const float4 u = __ldcg(src), w = __ldcg(src + 1);
+    a[0] += u.x;
+    a[1] += u.y;
+    a[2] += u.z;
+    a[3] += u.w;
+    a[4] += w.x;
+    a[5] += w.y;
+    a[6] += w.z;
+    a[7] += w.w;
+  }
+  if (p.xbias != nullptr) {
+    const uint4 bb = __ldg(reinterpret_cast<const uint4*>(p.xbias + k));
+    const __half* bh = reinterpret_cast<const __half*>(&bb);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a[i] += __half2float(bh[i]);
+  }
+  uint4 out;
+  __half2* oh = reinterpret_cast<__half2*>(&out);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) oh[i] = __floats2half2_rn(a[2 * i], a[2 * i + 1]);
+  return out;
+}
+
 __device__ __forceinline__ void stage_x(const GemvParams& p, uint8_t* xs, float* cx, int s_begin, int nst, bool writer,
                                         bool factored, const NormW& nwp) {
   constexpr int kThr = kWarps * 32;
@@ -479,7 +516,7 @@ __device__ __forceinline__ void stage_x(const GemvParams& p, uint8_t* xs, float*
     for (int m = 0; m < p.M; ++m) {
       float acc = 0.f;
       for (int v = tid; v < nv; v += kThr) {
-        uint4 a = __ldcg(reinterpret_cast<const uint4*>(p.x + m * p.ldx) + v);
+        uint4 a = load_x8(p, m, 8 * v);
         if (p.res != nullptr) {
           const uint4 r = __ldcg(reinterpret_cast<const uint4*>(p.res + m * p.ldr) + v);
           __half2* ah = reinterpret_cast<__half2*>(&a);
@@ -527,7 +564,7 @@ __device__ __forceinline__ void stage_x(const GemvParams& p, uint8_t* xs, float*
       if (keep)  // this thread read block kb0 + b (= tid + j * 256) in the pass above
         v = (kb0 + b) < kThr ? keep0 : keep1;
       else
-        v = __ldcg(reinterpret_cast<const uint4*>(p.x + m * p.ldx + k));
+        v = load_x8(p, m, k);
       if (norm) {
         __half2* vh = reinterpret_cast<__half2*>(&v);
         if (p.res != nullptr && !keep) {
@@ -715,7 +752,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 3 - NT)  // M <= 8: two CTA
       }
 
       // ---------------------------------------------------------------- tile epilogue
-      if (WPC == 1 && S == 1 && !swiglu) {
+      if (WPC == 1 && S == 1 && !swiglu && p.yp == nullptr) {
         if (active && ok) {
           const int n0 = (tile + slot) * 32 + 4 * g;
 #pragma unroll
@@ -766,7 +803,10 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 3 - NT)  // M <= 8: two CTA
             for (int j = 1; j < WPC; ++j) a += red[(j * p.M + m) * CW * 32 + rc];
             v[hh] = a;
           }
-          if (S == 1) {
+          if (p.yp != nullptr) {  // this K slice's partial sums (no bias), read by the next kernel
+            const int n = tile * 32 + col;
+            if (n < p.N) p.yp[(static_cast<int64_t>(rank) * p.M + m) * p.N + n] = v[0];
+          } else if (S == 1) {
             const int n = tile * 32 + col;
             if (!swiglu && n < p.N) {
               float a = v[0];
@@ -799,14 +839,14 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 3 - NT)  // M <= 8: two CTA
                globaltimer_ns() - t0 < 500000000ull) {
         }
     }
-    if (S > 1) {
+    if (S > 1 && p.yp == nullptr) {
       cluster_sync();
       cluster_sync();
     }
     if (p.tp.world > 0) tp_finish(p, s_ep, false, c_begin, c_end, UPT, S, rank);
     return;
   }
-  if (S > 1) {
+  if (S > 1 && p.yp == nullptr) {
     cluster_sync();
     const float* red = reinterpret_cast<const float*>(smem + L.red_off);
     const int ncols = min(UPT, c_end - c_begin) * 32;
@@ -1030,7 +1070,9 @@ int launch_gemv(const CUtensorMap& mq, const CUtensorMap& ms, const CUtensorMap&
   const GemvKernel kernel = variant(p.M <= 8 ? 1 : 2, c.cw, exact);
   const dim3 grid(c.nctas, c.split, 1);
   const dim3 block((kWarps + 1) * 32, 1, 1);
-  cudaError_t e = launch(kernel, grid, block, c.smem, stream, pdl_enabled(), dim3(1, c.split, 1), mq, ms, mz, p);
+  // split-K partials written to global memory need no cluster: the slices run as independent CTAs
+  const dim3 cluster(1, p.yp != nullptr ? 1 : c.split, 1);
+  cudaError_t e = launch(kernel, grid, block, c.smem, stream, pdl_enabled(), cluster, mq, ms, mz, p);
   if (e != cudaSuccess) return set_error(DK_ERR_CUDA, "w4a16 gemv launch: %s", cudaGetErrorString(e));
   return DK_OK;
 }
@@ -1045,10 +1087,21 @@ struct NormArgs {
   float eps = 1e-6f;
 };
 
+// Split-K partial sums between two launches (dk_w4a16_matmul_partials and its consumer
+// dk_w4a16_rmsnorm_matmul_partials): one launch of at most 16 rows each.
+struct PartialIO {
+  const float* xp = nullptr;  // consumer: the previous projection's partial sums [xparts][M][K]
+  int xparts = 0;
+  const __half* xbias = nullptr;
+  float* yp = nullptr;        // producer: this projection's partial sums [split][M][N]
+  int64_t yp_capacity = 0;    // floats
+  int* nparts = nullptr;      // producer: receives the split (the number of partial sums written)
+};
+
 int run_fast(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const void* zeros,
              const void* bias, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group_size,
              const dk_matmul_config* cfg, int swiglu_i, const NormArgs& na, cudaStream_t st,
-             const TPArgs* tp = nullptr) {
+             const TPArgs* tp = nullptr, const PartialIO* pio = nullptr) {
   const int flags = cfg ? cfg->flags : 0;
   CUtensorMap mq, ms, mz;
   if (!make_tensor_map_2d(&mq, qweight, CU_TENSOR_MAP_DATA_TYPE_INT32, N, K / 8, N * 4, 32, kStageRows,
@@ -1075,6 +1128,14 @@ int run_fast(const void* x, int64_t ldx, const int32_t* qweight, const void* sca
     if (c.cw == 0) return set_error(DK_ERR_UNSUPPORTED, "w4a16: no tile fits (M=%d, K=%lld)", mc, (long long)K);
     if (tp != nullptr && mc > tp->max_m)
       return set_error(DK_ERR_UNSUPPORTED, "w4a16_matmul_allreduce: %d rows exceed the communicator", mc);
+    if (pio != nullptr && mc != M)
+      return set_error(DK_ERR_UNSUPPORTED, "w4a16 partial sums: %lld rows do not fit one launch", (long long)M);
+    if (pio != nullptr && pio->yp != nullptr) {
+      if (static_cast<int64_t>(c.split) * M * N > pio->yp_capacity)
+        return set_error(DK_ERR_INVALID, "w4a16_matmul_partials: %d partial sums of [%lld, %lld] exceed the buffer",
+                         c.split, (long long)M, (long long)N);
+      *pio->nparts = c.split;
+    }
     GemvParams p;
     p.x = static_cast<const __half*>(x) + m0 * ldx;
     p.ldx = ldx;
@@ -1100,6 +1161,10 @@ int run_fast(const void* x, int64_t ldx, const int32_t* qweight, const void* sca
     p.eps = na.eps;
     p.err = dev.err_word;
     p.pf = l2_prefetch_from(m0 == 0 ? cfg : nullptr);
+    p.xp = pio != nullptr ? pio->xp : nullptr;
+    p.xparts = pio != nullptr ? pio->xparts : 0;
+    p.xbias = pio != nullptr ? pio->xbias : nullptr;
+    p.yp = pio != nullptr ? pio->yp : nullptr;
     if (tp != nullptr)
       p.tp = *tp;
     else
@@ -1228,6 +1293,67 @@ extern "C" int dk_w4a16_rmsnorm_matmul(const void* x, int64_t ldx, const void* r
   na.eps = eps;
   return run_fast(x, ldx, qweight, scales, zeros, bias, y, ldy, M, N, K, group_size, cfg,
                   swiglu ? static_cast<int>(N / 2) : 0, na, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int dk_w4a16_matmul_partials(const void* x, int64_t ldx, const int32_t* qweight, const void* scales,
+                                        const void* zeros, int64_t M, int64_t N, int64_t K, int64_t group_size,
+                                        float* partials, int64_t capacity, int32_t* nparts,
+                                        const dk_matmul_config* cfg, dk_stream_t stream) {
+  using namespace dk;
+  int rc = check_w4a16_args("w4a16_matmul_partials", x, ldx, qweight, scales, zeros, partials, N, M, N, N, K,
+                            group_size);
+  if (rc != DK_OK) return rc;
+  if (nparts == nullptr) return set_error(DK_ERR_INVALID, "w4a16_matmul_partials: nparts is NULL");
+  if (M < 1 || M > 16) return set_error(DK_ERR_UNSUPPORTED, "w4a16_matmul_partials: 1..16 rows");
+  const int flags = cfg ? cfg->flags : 0;
+  if (!fast_ok(x, ldx, qweight, scales, zeros, N, K, group_size, flags) || !aligned16(partials))
+    return set_error(DK_ERR_UNSUPPORTED,
+                     "w4a16_matmul_partials: needs the fast path's conditions and a 16-byte aligned buffer");
+  PartialIO pio;
+  pio.yp = partials;
+  pio.yp_capacity = capacity;
+  pio.nparts = nparts;
+  return run_fast(x, ldx, qweight, scales, zeros, nullptr, nullptr, N, M, N, K, group_size, cfg, 0, NormArgs(),
+                  reinterpret_cast<cudaStream_t>(stream), nullptr, &pio);
+}
+
+extern "C" int dk_w4a16_rmsnorm_matmul_partials(const float* parts, int32_t nparts, const void* part_bias,
+                                                const void* residual, int64_t ldr, const void* norm_weight, float eps,
+                                                void* residual_out, int64_t ldro, const int32_t* qweight,
+                                                const void* scales, const void* zeros, const void* bias, void* y,
+                                                int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group_size,
+                                                int32_t swiglu, const dk_matmul_config* cfg, dk_stream_t stream) {
+  using namespace dk;
+  const int64_t ycols = swiglu ? N / 2 : N;
+  int rc = check_w4a16_args("w4a16_rmsnorm_matmul_partials", parts, K, qweight, scales, zeros, y, ldy, M, N, ycols, K,
+                            group_size);
+  if (rc != DK_OK) return rc;
+  if (nparts < 1 || nparts > 8) return set_error(DK_ERR_INVALID, "w4a16_rmsnorm_matmul_partials: 1..8 partial sums");
+  if (M < 1 || M > 16) return set_error(DK_ERR_UNSUPPORTED, "w4a16_rmsnorm_matmul_partials: 1..16 rows");
+  if (!norm_weight) return set_error(DK_ERR_INVALID, "w4a16_rmsnorm_matmul_partials: norm_weight is NULL");
+  if (residual && (!residual_out || ldr < K || ldro < K))
+    return set_error(DK_ERR_INVALID, "w4a16_rmsnorm_matmul_partials: residual needs residual_out and row strides >= K");
+  const int flags = cfg ? cfg->flags : 0;
+  const bool aligned = aligned16(norm_weight) && (!part_bias || aligned16(part_bias)) &&
+                       (!residual || (aligned16(residual) && aligned16(residual_out) && ldr % 8 == 0 && ldro % 8 == 0));
+  if (!aligned || K % 8 != 0 || (swiglu && (N % 2 != 0 || (N / 2) % 32 != 0)) ||
+      !fast_ok(parts, K, qweight, scales, zeros, N, K, group_size, flags))
+    return set_error(DK_ERR_UNSUPPORTED,
+                     "w4a16_rmsnorm_matmul_partials: needs group_size 128, N %% 8 == 0 (I %% 32 == 0 with swiglu) and "
+                     "16-byte aligned operands and strides");
+  NormArgs na;
+  na.w = norm_weight;
+  na.res = residual;
+  na.ldr = ldr;
+  na.res_out = residual_out;
+  na.ldro = ldro;
+  na.eps = eps;
+  PartialIO pio;
+  pio.xp = parts;
+  pio.xparts = nparts;
+  pio.xbias = static_cast<const __half*>(part_bias);
+  return run_fast(parts, K, qweight, scales, zeros, bias, y, ldy, M, N, K, group_size, cfg,
+                  swiglu ? static_cast<int>(N / 2) : 0, na, reinterpret_cast<cudaStream_t>(stream), nullptr, &pio);
 }
 
 namespace dk {

@@ -73,6 +73,10 @@ SIGNATURES = {
     "dk_w4a16_swiglu": [P, I64, P, P, P, P, P, I64, I64, I64, I64, I64, ctypes.POINTER(MatmulConfig), P],
     "dk_w4a16_rmsnorm_matmul": [P, I64, P, I64, P, F32, P, I64, P, P, P, P, P, I64, I64, I64, I64, I64, I32,
                                 ctypes.POINTER(MatmulConfig), P],
+    "dk_w4a16_matmul_partials": [P, I64, P, P, P, I64, I64, I64, I64, P, I64, ctypes.POINTER(I32),
+                                 ctypes.POINTER(MatmulConfig), P],
+    "dk_w4a16_rmsnorm_matmul_partials": [P, I32, P, P, I64, P, F32, P, I64, P, P, P, P, P, I64, I64, I64, I64, I64,
+                                         I32, ctypes.POINTER(MatmulConfig), P],
     "dk_quantize_fp8": [P, I64, P, P, I64, I64, P],
     "dk_dequantize_fp8": [P, P, P, I64, I64, P],
     "dk_w8a16_matmul": [P, I64, P, P, P, P, I64, I64, I64, I64, ctypes.POINTER(MatmulConfig), P],

@@ -44,6 +44,7 @@ class Backend:
     name = "fp16"
     quantized = False
     fused_decode = False  # True: the runner uses attention_decode / gate_up_act hooks
+    partials = False  # True: linear_partials / norm_linear_partials (split-K sums between launches)
 
     def linear(self, x, p: Linear):
         return F.linear(x, p.w, p.bias)
@@ -154,10 +155,30 @@ class OursBackend(Backend):
         return w4a16_rmsnorm_matmul(x, w, eps, residual, p.qweight, p.scales, p.zeros, bias=p.bias, swiglu=True,
                                     config=self.gate_up_cfg(x, p))
 
+    # The down projection of a one-row decode step hands its split-K partial sums to the next layer's
+    # norm + qkv launch, which adds them while staging its input (the same sums, one cluster
+    # reduction fewer per layer).
+    @property
+    def partials(self) -> bool:
+        return self.decode_kernel == "triton"
+
+    def linear_partials(self, x, p: Linear):
+        from kernels.w4a16 import w4a16_matmul_partials
+
+        return w4a16_matmul_partials(x, p.qweight, p.scales, p.zeros, config=self.cfg(p))
+
+    def norm_linear_partials(self, parts, part_bias, w, eps, residual, p: Linear):
+        from kernels.w4a16 import w4a16_rmsnorm_matmul_partials
+
+        return w4a16_rmsnorm_matmul_partials(parts, part_bias, w, eps, residual, p.qweight, p.scales, p.zeros,
+                                             bias=p.bias, config=self.cfg(p))
+
 
 class OursFP8Backend(OursBackend):
     """FP8 (e4m3) weight-only linears with the same fused norm/activation kernels
     (reference model.py:100-118)."""
+
+    partials = False
 
     name = "ours_fp8"
 
@@ -453,15 +474,27 @@ class QwenRunner:
         norm + gate_up + SwiGLU, down). Returns (last MLP output, residual stream)."""
         from kernels.attention import decode_attention
 
+        from kernels.w4a16 import FUSED_NORM_ROWS
+
         be, eps = self.backend, self.eps
         residual, h = None, x
+        # one or two rows on one GPU: down_proj's split-K partial sums go to the next norm + qkv as they are
+        split_sums = be.partials and self.tp is None and x.numel() // x.shape[-1] <= FUSED_NORM_ROWS
+        parts = part_bias = None
         for i, L in enumerate(self.layers):
-            qkv, new_res = be.norm_linear(h, L.ln1, eps, residual, L.qkv)
+            if parts is not None:
+                qkv, new_res = be.norm_linear_partials(parts, part_bias, L.ln1, eps, residual, L.qkv)
+                qkv, new_res = qkv.view(*x.shape[:-1], -1), new_res.view(x.shape)
+            else:
+                qkv, new_res = be.norm_linear(h, L.ln1, eps, residual, L.qkv)
             residual = x if residual is None else new_res
             attn = decode_attention(qkv, self.k_cache[i], self.v_cache[i], pos, self.rope_cos, self.rope_sin,
                                     self.n_heads, self.n_kv, static_cache=True)
             act, residual = be.norm_gate_up_act(self._row_linear(attn, L.o), L.ln2, eps, residual, L.gate_up)
-            h = self._row_linear(act, L.down)
+            if split_sums and i + 1 < len(self.layers):  # the last layer's output goes to the lm_head as fp16
+                parts, part_bias = be.linear_partials(act, L.down), L.down.bias
+            else:
+                h, parts = self._row_linear(act, L.down), None
         return h, residual
 
     def _full_layers(self, x, pos, B, T):

@@ -210,3 +210,60 @@ def import_choices(choices: dict) -> None:
 def best_configs() -> dict:
     """Choices so far, for results JSON (reference kernels/w4a16.py:345-355)."""
     return {"decode_path": {str(k): v for k, v in _choices.items()}}
+
+
+def w4a16_matmul_partials(x, qweight, scales, zeros, group_size=128, config=None) -> torch.Tensor:
+    """x [.., K] @ dequant(W).T as fp32 split-K partial sums [S, M, N] (no bias; S is the split the
+    library picks for this shape, 1 = the whole sum): the decode GEMV without its cluster reduction,
+    for `w4a16_rmsnorm_matmul_partials` to add while it stages its input. 1..16 rows. No reference
+    counterpart (the reference passes the complete fp16 output, kernels/e2e/model.py:247)."""
+    K = x.shape[-1]
+    N = qweight.shape[1]
+    _lib.reference_assert(qweight.shape[0] * 8 == K and K % group_size == 0)
+    _check_weight_shapes("w4a16_matmul_partials", K, N, scales, zeros, group_size, None)
+    _lib.require_cuda("w4a16_matmul_partials", x, qweight, scales, zeros)
+    _lib.require_dtype("w4a16_matmul_partials", torch.float16, x, scales, zeros)
+    x2 = x.reshape(-1, K)
+    if x2.stride(1) != 1:
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    _lib.require_extent(1 <= M <= 16, "w4a16_matmul_partials: 1..16 rows")
+    buf = torch.empty(8 * M * N, dtype=torch.float32, device=x.device)
+    n = ctypes.c_int32(0)
+    _lib.call("dk_w4a16_matmul_partials", _lib.ptr(x2), x2.stride(0), _lib.ptr(qweight.contiguous()),
+              _lib.ptr(scales.contiguous()), _lib.ptr(zeros.contiguous()), M, N, K, group_size, _lib.ptr(buf),
+              buf.numel(), ctypes.byref(n), ctypes.byref(_config(config)), _lib.stream_of(x))
+    return buf[: n.value * M * N].view(n.value, M, N)
+
+
+def w4a16_rmsnorm_matmul_partials(parts, part_bias, norm_weight, eps, residual, qweight, scales, zeros,
+                                  group_size=128, bias=None, swiglu=False, config=None):
+    """`w4a16_rmsnorm_matmul` whose input is fp16(parts[0] + ... + parts[S-1] (+ part_bias)) - the
+    previous projection's split-K partial sums [S, M, K] from `w4a16_matmul_partials`, added in slice
+    order as that projection's own reduction would - in one kernel. Returns (y, h_or_None)."""
+    S, M, K = parts.shape
+    N = qweight.shape[1]
+    _lib.reference_assert(qweight.shape[0] * 8 == K and K % group_size == 0)
+    _check_weight_shapes("w4a16_rmsnorm_matmul_partials", K, N, scales, zeros, group_size, bias)
+    _lib.require_extent(1 <= S <= 8 and 1 <= M <= 16 and parts.dtype == torch.float32 and parts.is_contiguous(),
+                        "w4a16_rmsnorm_matmul_partials: parts must be contiguous fp32 [1..8, 1..16, K]")
+    _lib.require_extent(part_bias is None or part_bias.numel() == K, "w4a16_rmsnorm_matmul_partials: part_bias [K]")
+    _lib.require_extent(norm_weight.numel() == K, f"w4a16_rmsnorm_matmul_partials: norm_weight must have {K} elements")
+    r2 = None if residual is None else residual.reshape(-1, K)
+    _lib.require_extent(r2 is None or r2.shape[0] == M, "w4a16_rmsnorm_matmul_partials: residual must be [M, K]")
+    _lib.require_cuda("w4a16_rmsnorm_matmul_partials", parts, part_bias, residual, norm_weight, qweight, scales, zeros,
+                      bias)
+    _lib.require_dtype("w4a16_rmsnorm_matmul_partials", torch.float16, residual, norm_weight, scales, zeros, bias,
+                       part_bias)
+    if r2 is not None and r2.stride(1) != 1:
+        r2 = r2.contiguous()
+    I = N // 2
+    out = torch.empty((M, I if swiglu else N), dtype=torch.float16, device=parts.device)
+    res_out = None if r2 is None else torch.empty((M, K), dtype=torch.float16, device=parts.device)
+    _lib.call("dk_w4a16_rmsnorm_matmul_partials", _lib.ptr(parts), S, _lib.ptr(part_bias), _lib.ptr(r2),
+              0 if r2 is None else r2.stride(0), _lib.ptr(norm_weight.contiguous()), float(eps), _lib.ptr(res_out),
+              0 if res_out is None else res_out.stride(0), _lib.ptr(qweight.contiguous()), _lib.ptr(scales.contiguous()),
+              _lib.ptr(zeros.contiguous()), _lib.ptr(None if bias is None else bias.contiguous()), _lib.ptr(out),
+              out.stride(0), M, N, K, group_size, 1 if swiglu else 0, ctypes.byref(_config(config)),
+              _lib.stream_of(parts))
+    return out, res_out

@@ -37,7 +37,7 @@ def test_library_loads_and_reports_version():
     from kernels import _lib
 
     h = _lib.lib()
-    assert h.dk_abi_version() == 5
+    assert h.dk_abi_version() == 6
     for name in declared_symbols():
         assert hasattr(h, name)
     # every declared symbol has a ctypes signature in the Python mirror
