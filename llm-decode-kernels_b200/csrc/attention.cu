@@ -363,33 +363,44 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // ------------------------------------------------------------------ combine this rank's dims
   if (warp < kCWarps) {
-    for (int gi = warp; gi < G; gi += kCWarps) {
-      float mx = -INFINITY;
-      for (int pp = lane; pp < nparts; pp += 32)
+    // one half-warp per head (G <= 8 = 2 * kCWarps): the heads' maxima, weights and denominators at
+    // once instead of two heads one after the other on one warp; every lane takes part in the
+    // shuffles (they stay inside a half-warp), lanes of a half without a head only compute
+    static_assert(G <= 2 * kCWarps, "a half-warp per head");
+    const int gi = warp * 2 + (lane >> 4), hl = lane & 15;
+    const bool head = gi < G;
+    float mx = -INFINITY;
+    if (head)
+      for (int pp = hl; pp < nparts; pp += 16)
         if (recv_ml[(pp * G + gi) * 2 + 1] > 0.f) mx = fmaxf(mx, recv_ml[(pp * G + gi) * 2]);
 #pragma unroll
-      for (int x = 16; x > 0; x >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, x));
-      float ds = 0.f;
-      for (int pp = lane; pp < nparts; pp += 32) {
+    for (int x = 8; x > 0; x >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, x));
+    float ds = 0.f;
+    if (head)
+      for (int pp = hl; pp < nparts; pp += 16) {
         const float l = recv_ml[(pp * G + gi) * 2 + 1];
         const float w = l > 0.f ? __expf(recv_ml[(pp * G + gi) * 2] - mx) : 0.f;
         wts[pp * G + gi] = w;
         ds = fmaf(w, l, ds);
       }
 #pragma unroll
-      for (int x = 16; x > 0; x >>= 1) ds += __shfl_xor_sync(0xffffffffu, ds, x);
-      if (lane == 0) den[gi] = ds;
-    }
+    for (int x = 8; x > 0; x >>= 1) ds += __shfl_xor_sync(0xffffffffu, ds, x);
+    if (head && hl == 0) den[gi] = ds;
     consumers_sync();
     __half* out = p.out + static_cast<int64_t>(b) * p.nq * kHd + h * G * kHd + rank * D;
     for (int e = tid; e < G * D; e += kCWarps * 32) {
       const int gi = e / D, dd = e % D;
-      float n0 = 0.f, n1 = 0.f;
-      for (int pp = 0; pp < nparts; pp += 2) {  // nparts = 4 S is even
-        n0 = fmaf(wts[pp * G + gi], recv_o[(pp * G + gi) * D + dd], n0);
-        n1 = fmaf(wts[(pp + 1) * G + gi], recv_o[((pp + 1) * G + gi) * D + dd], n1);
+      // 8 independent sums (partials pp = r mod 8), so the shared-memory loads of the up to 64
+      // partials overlap instead of forming one chain of dependent multiply-adds; nparts = 4 S is a
+      // multiple of 4, and of 8 from S = 2 on
+      float n[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int pp = 0; pp < nparts; pp += 8) {
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+          if (pp + r < nparts) n[r] = fmaf(wts[(pp + r) * G + gi], recv_o[((pp + r) * G + gi) * D + dd], n[r]);
       }
-      out[gi * kHd + dd] = __float2half_rn((n0 + n1) / den[gi]);
+      const float num = ((n[0] + n[1]) + (n[2] + n[3])) + ((n[4] + n[5]) + (n[6] + n[7]));
+      out[gi * kHd + dd] = __float2half_rn(num / den[gi]);
     }
   }
 
