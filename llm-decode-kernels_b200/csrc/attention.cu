@@ -20,10 +20,11 @@
 //   round trip) and V rows by ldmatrix.trans. The new token's k and v never go through the ring:
 //   the lane that addresses cache row `pos` points ldmatrix at the freshly rotated row instead, and
 //   rows past the slice end read a zero row, so no shared-memory patching or zero-filling is needed;
-// * every warp's (max, sum, unnormalized output) is a partial. Rank q of the cluster owns output
-//   dims [q*D, (q+1)*D), D = head_dim / S; each warp pushes the slices of its partial straight into
-//   the owners' shared memory with st.async (completion counted by the owner's mbarrier, so only
-//   the receiver waits), and each owner combines its dims over the 4*S partials in parallel.
+// * the four warps' (max, sum, unnormalized output) are combined into the CTA's partial in shared
+//   memory. Rank q of the cluster owns output dims [q*D, (q+1)*D), D = head_dim / S; the CTA pushes
+//   the slices of its partial straight into the owners' shared memory with st.async (completion
+//   counted by the owner's mbarrier, so only the receiver waits), and each owner combines its dims
+//   over the S partials (a half-warp per head).
 // `pos` is read on the device, so the launch can be captured in a CUDA graph once and replayed for
 // every step.
 #include <algorithm>
@@ -40,7 +41,6 @@ constexpr int kChunk = 64;                    // cache positions per ring slot: 
 constexpr int kMaxRing = 4;
 constexpr int kMaxGroup = 8;  // query heads per kv head
 constexpr int kMaxSplit = 16;  // cluster of up to 16 CTAs (non-portable size, allowed on B200)
-constexpr int kMaxParts = kMaxSplit * kCWarps;
 
 struct AttnParams {
   const __half* qkv;  // [B, (nq + 2 nkv) * hd]
@@ -116,9 +116,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(16) __half qs[G][kHd + 8];  // rotated q; +8 halves: conflict-free fragment reads
   __shared__ __align__(16) __half knew[kHd], vnew[kHd];
   __shared__ __align__(16) __half vzero[8];
-  __shared__ __align__(16) float recv_o[kCWarps * G * kHd];   // [partial][head][D] (4S partials x D = 4 hd)
-  __shared__ __align__(16) float recv_ml[kMaxParts * G * 2];  // [partial][head] {max, sum}
-  __shared__ float wts[kMaxParts * G];
+  __shared__ __align__(16) float pre_o[kCWarps * G * kHd];    // this CTA's warps' outputs [warp][head][dim]
+  __shared__ float pre_ml[kCWarps * G * 2];                   // [warp][head] {max, sum}
+  __shared__ float pre_w[kCWarps * G];                        // [warp][head] weight in the CTA's partial
+  __shared__ float cml[G * 2];                                // the CTA's partial per head {max, sum}
+  __shared__ __align__(16) float recv_o[G * kHd];             // [rank][head][D] (S partials x D = hd)
+  __shared__ __align__(16) float recv_ml[kMaxSplit * G * 2];  // [rank][head] {max, sum}
+  __shared__ float wts[kMaxSplit * G];
   __shared__ float den[G];
   __shared__ __align__(8) uint64_t full[kMaxRing], empty[kMaxRing], recv;
   extern __shared__ __align__(128) uint8_t dsm_raw[];
@@ -126,7 +130,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int h = blockIdx.x, b = blockIdx.y, rank = blockIdx.z, S = gridDim.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int nparts = S * kCWarps;
+  const int nparts = S;  // one partial per cluster rank (its 4 warps combined first)
   const int D = kHd / S;  // output dims this rank combines (S is a power of two <= head_dim / 2)
 
   if (tid == 0) {
@@ -327,26 +331,63 @@ __global__ void __launch_bounds__(kThreads, 1)
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
   }
 
-  // ------------------------------------------------------------------ push partials to their owners
+  // ------------------------------------------------------------------ this CTA's partial, pushed to the owners
   if (S > 1) cluster_wait();  // (1)
-  if (warp < kCWarps && g < G) {
-    const int part = rank * kCWarps + warp;
+  if (warp < kCWarps) {
+    // the 4 warps' (max, sum, unnormalized output) of every head combined in shared memory first, so
+    // an owner adds S partials instead of 4 S
+    if (g < G) {
 #pragma unroll
-    for (int j = 0; j < kTiles; ++j) {
-      const int dd0 = 8 * j + 2 * t;
-      const int q = dd0 / D;
-      float* dst = &recv_o[(part * G + g) * D + dd0 % D];
-      if (S > 1)
-        st_async_v2_f32(map_shared_rank(dst, q), o[j][0], o[j][1], map_shared_rank(&recv, q));
-      else
-        *reinterpret_cast<float2*>(dst) = make_float2(o[j][0], o[j][1]);
+      for (int j = 0; j < kTiles; ++j)
+        *reinterpret_cast<float2*>(&pre_o[(warp * G + g) * kHd + 8 * j + 2 * t]) = make_float2(o[j][0], o[j][1]);
+      if (t == 0) {
+        pre_ml[(warp * G + g) * 2] = m_run;
+        pre_ml[(warp * G + g) * 2 + 1] = l_run;
+      }
     }
-    for (int q = t; q < S; q += 4) {
-      float* dst = &recv_ml[(part * G + g) * 2];
+    consumers_sync();
+    if (tid < G) {
+      float mx = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kCWarps; ++w)
+        if (pre_ml[(w * G + tid) * 2 + 1] > 0.f) mx = fmaxf(mx, pre_ml[(w * G + tid) * 2]);
+      float ls = 0.f;
+#pragma unroll
+      for (int w = 0; w < kCWarps; ++w) {
+        const float l = pre_ml[(w * G + tid) * 2 + 1];
+        const float wt = l > 0.f ? __expf(pre_ml[(w * G + tid) * 2] - mx) : 0.f;
+        pre_w[w * G + tid] = wt;
+        ls = fmaf(wt, l, ls);
+      }
+      cml[2 * tid] = mx;
+      cml[2 * tid + 1] = ls;
+    }
+    consumers_sync();
+    // output dims (two at a time) to the rank that owns them; (max, sum) of every head to every rank
+    for (int e = tid; e < G * kHd / 2; e += kCWarps * 32) {
+      const int gi = e / (kHd / 2), d = 2 * (e % (kHd / 2));
+      float v0 = 0.f, v1 = 0.f;
+#pragma unroll
+      for (int w = 0; w < kCWarps; ++w) {
+        const float wt = pre_w[w * G + gi];
+        const float2 ov = *reinterpret_cast<const float2*>(&pre_o[(w * G + gi) * kHd + d]);
+        v0 = fmaf(wt, ov.x, v0);
+        v1 = fmaf(wt, ov.y, v1);
+      }
+      const int q = d / D;
+      float* dst = &recv_o[(rank * G + gi) * D + d % D];
       if (S > 1)
-        st_async_v2_f32(map_shared_rank(dst, q), m_run, l_run, map_shared_rank(&recv, q));
+        st_async_v2_f32(map_shared_rank(dst, q), v0, v1, map_shared_rank(&recv, q));
       else
-        *reinterpret_cast<float2*>(dst) = make_float2(m_run, l_run);
+        *reinterpret_cast<float2*>(dst) = make_float2(v0, v1);
+    }
+    for (int e = tid; e < G * S; e += kCWarps * 32) {
+      const int gi = e % G, q = e / G;
+      float* dst = &recv_ml[(rank * G + gi) * 2];
+      if (S > 1)
+        st_async_v2_f32(map_shared_rank(dst, q), cml[2 * gi], cml[2 * gi + 1], map_shared_rank(&recv, q));
+      else
+        *reinterpret_cast<float2*>(dst) = make_float2(cml[2 * gi], cml[2 * gi + 1]);
     }
   }
   if (warp < kCWarps) {
@@ -390,9 +431,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __half* out = p.out + static_cast<int64_t>(b) * p.nq * kHd + h * G * kHd + rank * D;
     for (int e = tid; e < G * D; e += kCWarps * 32) {
       const int gi = e / D, dd = e % D;
-      // 8 independent sums (partials pp = r mod 8), so the shared-memory loads of the up to 64
-      // partials overlap instead of forming one chain of dependent multiply-adds; nparts = 4 S is a
-      // multiple of 4, and of 8 from S = 2 on
+      // 8 independent sums (partials pp = r mod 8), so the shared-memory loads of the up to 16
+      // partials overlap instead of forming one chain of dependent multiply-adds
       float n[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       for (int pp = 0; pp < nparts; pp += 8) {
 #pragma unroll
