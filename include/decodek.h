@@ -105,8 +105,8 @@ int dk_dequantize_int4(const int32_t* qweight, const void* scales, const void* z
  * y[M, N] fp16 = x[M, K] fp16 @ dequant(W).T (+ bias[N]), fp32 accumulation.
  * x rows have stride ldx, y rows stride ldy (elements). bias may be NULL. cfg may be NULL.
  * Dispatch by rows (fast-path shapes: N % 8 == 0, group_size 128, 16-byte aligned operands):
- * up to 15 rows, or 16 with K < 4096: the decode GEMV, up to 16 rows per launch (fewer when a long K
- * slice leaves no tile for the staged rows); 16-127 rows with N >= 128: the tcgen05 small-M kernel;
+ * up to 8 rows, or up to 16 with K < 4096: the decode GEMV, up to 16 rows per launch (fewer when a long
+ * K slice leaves no tile for the staged rows); 9-127 rows with N >= 128: the tcgen05 small-M kernel;
  * M >= 128 and N >= 128: the tcgen05 tensor-core GEMM (kernels/w4a16.py:31-97). The tcgen05 kernels
  * round every dequantized weight to fp16 like the reference's dequantize-then-matmul. DK_FLAG_GEMV
  * keeps any M on the decode GEMV. Other shapes run a one-thread-per-output kernel. */
@@ -331,7 +331,7 @@ int dk_step_ops(const dk_step_plan* plan, int32_t* kinds, int32_t capacity, int3
 
 typedef struct dk_tp_comm dk_tp_comm;
 
-/* Bytes of one rank's exchange buffer for launches of up to max_m rows (max 16) and max_n columns. */
+/* Bytes of one rank's exchange buffer for launches of up to max_m rows (max 64) and max_n columns. */
 int dk_tp_buffer_bytes(int32_t world, int64_t max_m, int64_t max_n, uint64_t* bytes);
 /* Set-up only (allocates and synchronizes): cudaMalloc `bytes` on the current device, zero them,
  * return the pointer and its IPC handle (DK_TP_IPC_HANDLE_BYTES bytes written to ipc_handle). */
@@ -357,8 +357,10 @@ int dk_tp_comm_set_wait(dk_tp_comm* comm, uint64_t wait_ns);
  * receives the full y. Every rank must make the same sequence of calls on one communicator with the
  * same M, N and K (the kernels of different ranks meet per CTA; a CTA that waits more than ~2 s for
  * a peer gives up, leaves its columns of y unwritten and sets DK_DEVERR_TP_WAIT). Needs the fast
- * path's conditions (group_size 128, N % 8 == 0, 16-byte aligned operands), N <= max_n, and runs
- * M in launches of up to min(16, max_m) rows. */
+ * path's conditions (group_size 128, N % 8 == 0, 16-byte aligned operands), N <= max_n. 17 .. max_m
+ * rows (max_m <= 64) run as ONE launch of the tcgen05 small-M kernel (N >= 128; one pass over the
+ * weights) with the same allreduce epilogue; otherwise the decode GEMV in launches of up to
+ * min(16, max_m) rows. */
 int dk_w4a16_matmul_allreduce(const void* x, int64_t ldx, const int32_t* qweight, const void* scales,
                               const void* zeros, const void* bias, void* y, int64_t ldy, int64_t M, int64_t N,
                               int64_t K, int64_t group_size, const dk_matmul_config* cfg,

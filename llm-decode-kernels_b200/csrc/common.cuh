@@ -212,6 +212,72 @@ __device__ __forceinline__ uint2 ld_volatile_v2(const uint32_t* p) {
   return v;
 }
 
+// ---- fused-allreduce cells (row-sharded projections; see the buffer layout above)
+__device__ __forceinline__ uint32_t* tp_cell(const TPArgs& tp, int q, unsigned long long ep, int src, int m, int n) {
+  return tp.cells[q] +
+         2 * (((static_cast<size_t>(ep & 1) * tp.world + src) * tp.max_m + m) * static_cast<size_t>(tp.max_n) + n);
+}
+
+__device__ __forceinline__ void tp_push(const TPArgs& tp, unsigned long long ep, int m, int n, float v) {
+  const uint32_t tag = static_cast<uint32_t>(ep);
+  for (int q = 0; q < tp.world; ++q) st_volatile_v2(tp_cell(tp, q, ep, tp.rank, m, n), __float_as_uint(v), tag);
+}
+
+__device__ __forceinline__ void tp_push4(const TPArgs& tp, unsigned long long ep, int m, int n, float4 v) {
+  const uint32_t tag = static_cast<uint32_t>(ep);
+  for (int q = 0; q < tp.world; ++q) {
+    uint32_t* c = tp_cell(tp, q, ep, tp.rank, m, n);  // n % 4 == 0: 32-byte aligned
+    st_volatile_v4(c, __float_as_uint(v.x), tag, __float_as_uint(v.y), tag);
+    st_volatile_v4(c + 4, __float_as_uint(v.z), tag, __float_as_uint(v.w), tag);
+  }
+}
+
+// Bounded polling: false once the CTA gave up (another thread timed out) or this wait passed the
+// limit (then it records the device error and makes the CTA give up).
+__device__ __forceinline__ bool tp_keep_waiting(int it, uint64_t& t0, volatile int* give_up, int* err,
+                                                uint64_t limit) {
+  if (*give_up) return false;
+  if (it == 0) {
+    t0 = globaltimer_ns();
+  } else if ((it & 63) == 0 && globaltimer_ns() - t0 > (limit ? limit : kWaitLimitNs)) {
+    record_device_error(err, DK_DEVERR_TP_WAIT);
+    *give_up = 1;
+    return false;
+  }
+  return true;
+}
+
+// The four values of cells c[0..3] (32 bytes) once all four carry `tag`.
+__device__ __forceinline__ bool tp_poll4(const uint32_t* c, uint32_t tag, float (&out)[4], volatile int* give_up,
+                                         int* err, uint64_t limit) {
+  uint64_t t0 = 0;
+  for (int it = 0;; ++it) {
+    const uint4 a = ld_volatile_v4(c), b = ld_volatile_v4(c + 4);
+    if (a.y == tag && a.w == tag && b.y == tag && b.w == tag) {
+      out[0] = __uint_as_float(a.x);
+      out[1] = __uint_as_float(a.z);
+      out[2] = __uint_as_float(b.x);
+      out[3] = __uint_as_float(b.z);
+      return true;
+    }
+    if (!tp_keep_waiting(it, t0, give_up, err, limit)) return false;
+  }
+}
+
+__device__ __forceinline__ bool tp_poll1(const uint32_t* c, uint32_t tag, float& out, volatile int* give_up, int* err,
+                                         uint64_t limit) {
+  uint64_t t0 = 0;
+  for (int it = 0;; ++it) {
+    const uint2 a = ld_volatile_v2(c);
+    if (a.y == tag) {
+      out = __uint_as_float(a.x);
+      return true;
+    }
+    if (!tp_keep_waiting(it, t0, give_up, err, limit)) return false;
+  }
+}
+
+
 // Pull the 128-byte line holding p into L2 (a hint; no data returns to the thread).
 __device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
 

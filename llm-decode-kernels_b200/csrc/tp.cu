@@ -46,10 +46,10 @@ extern "C" {
 int dk_tp_buffer_bytes(int32_t world, int64_t max_m, int64_t max_n, uint64_t* bytes) {
   using namespace dk;
   if (bytes == nullptr) return set_error(DK_ERR_INVALID, "dk_tp_buffer_bytes: bytes is NULL");
-  if (world < 1 || world > DK_TP_MAX_WORLD || max_m < 1 || max_m > 16 || max_n < 8 || max_n % 8 != 0 ||
+  if (world < 1 || world > DK_TP_MAX_WORLD || max_m < 1 || max_m > 64 || max_n < 8 || max_n % 8 != 0 ||
       max_n > (int64_t(1) << 24))
     return set_error(DK_ERR_INVALID,
-                     "dk_tp_buffer_bytes: need 1 <= world <= %d, 1 <= max_m <= 16, max_n a positive multiple of 8",
+                     "dk_tp_buffer_bytes: need 1 <= world <= %d, 1 <= max_m <= 64, max_n a positive multiple of 8",
                      DK_TP_MAX_WORLD);
   *bytes = kTpHeaderBytes + 2ull * static_cast<uint64_t>(world) * max_m * max_n * 8;
   return DK_OK;

@@ -225,70 +225,6 @@ __device__ __forceinline__ void consume_chunk_stage(const uint8_t* __restrict__ 
 // so CTA i covers the same columns everywhere) and adds them in rank order. Two slots suffice: a rank
 // starts launch e + 2 only after its launch e + 1 finished, and every CTA of that launch read all
 // ranks' launch e + 1 values, which they wrote after their launch e had finished reading.
-__device__ __forceinline__ uint32_t* tp_cell(const TPArgs& tp, int q, unsigned long long ep, int src, int m, int n) {
-  return tp.cells[q] +
-         2 * (((static_cast<size_t>(ep & 1) * tp.world + src) * tp.max_m + m) * static_cast<size_t>(tp.max_n) + n);
-}
-
-__device__ __forceinline__ void tp_push(const TPArgs& tp, unsigned long long ep, int m, int n, float v) {
-  const uint32_t tag = static_cast<uint32_t>(ep);
-  for (int q = 0; q < tp.world; ++q) st_volatile_v2(tp_cell(tp, q, ep, tp.rank, m, n), __float_as_uint(v), tag);
-}
-
-__device__ __forceinline__ void tp_push4(const TPArgs& tp, unsigned long long ep, int m, int n, float4 v) {
-  const uint32_t tag = static_cast<uint32_t>(ep);
-  for (int q = 0; q < tp.world; ++q) {
-    uint32_t* c = tp_cell(tp, q, ep, tp.rank, m, n);  // n % 4 == 0: 32-byte aligned
-    st_volatile_v4(c, __float_as_uint(v.x), tag, __float_as_uint(v.y), tag);
-    st_volatile_v4(c + 4, __float_as_uint(v.z), tag, __float_as_uint(v.w), tag);
-  }
-}
-
-// Bounded polling: false once the CTA gave up (another thread timed out) or this wait passed the
-// limit (then it records the device error and makes the CTA give up).
-__device__ __forceinline__ bool tp_keep_waiting(int it, uint64_t& t0, volatile int* give_up, int* err,
-                                                uint64_t limit) {
-  if (*give_up) return false;
-  if (it == 0) {
-    t0 = globaltimer_ns();
-  } else if ((it & 63) == 0 && globaltimer_ns() - t0 > (limit ? limit : kWaitLimitNs)) {
-    record_device_error(err, DK_DEVERR_TP_WAIT);
-    *give_up = 1;
-    return false;
-  }
-  return true;
-}
-
-// The four values of cells c[0..3] (32 bytes) once all four carry `tag`.
-__device__ __forceinline__ bool tp_poll4(const uint32_t* c, uint32_t tag, float (&out)[4], volatile int* give_up,
-                                         int* err, uint64_t limit) {
-  uint64_t t0 = 0;
-  for (int it = 0;; ++it) {
-    const uint4 a = ld_volatile_v4(c), b = ld_volatile_v4(c + 4);
-    if (a.y == tag && a.w == tag && b.y == tag && b.w == tag) {
-      out[0] = __uint_as_float(a.x);
-      out[1] = __uint_as_float(a.z);
-      out[2] = __uint_as_float(b.x);
-      out[3] = __uint_as_float(b.z);
-      return true;
-    }
-    if (!tp_keep_waiting(it, t0, give_up, err, limit)) return false;
-  }
-}
-
-__device__ __forceinline__ bool tp_poll1(const uint32_t* c, uint32_t tag, float& out, volatile int* give_up, int* err,
-                                         uint64_t limit) {
-  uint64_t t0 = 0;
-  for (int it = 0;; ++it) {
-    const uint2 a = ld_volatile_v2(c);
-    if (a.y == tag) {
-      out = __uint_as_float(a.x);
-      return true;
-    }
-    if (!tp_keep_waiting(it, t0, give_up, err, limit)) return false;
-  }
-}
-
 // Called by every thread of the CTA after its last push. Columns: [c_begin*32, min(c_end*32, N)) with
 // split 1; with a cluster split S the elements e = m*ncols + col with e % S == cluster rank.
 __device__ void tp_finish(const GemvParams& p, unsigned long long ep, bool ok, int c_begin, int c_end, int upt,
@@ -1208,7 +1144,8 @@ int launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight, const voi
 void skinny_choice(int64_t rows, int64_t N, int64_t K, int* mb_out, int* split_out);
 int launch_skinny_tc(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const void* zeros,
                      const void* bias, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, bool static_weights,
-                     cudaStream_t st);
+                     cudaStream_t st,
+                     const TPArgs* tp = nullptr);
 }  // namespace dk
 
 extern "C" int dk_w4a16_matmul(const void* x, int64_t ldx, const int32_t* qweight, const void* scales,
@@ -1377,6 +1314,17 @@ extern "C" int dk_w4a16_matmul_allreduce(const void* x, int64_t ldx, const int32
   if (!fast_ok(x, ldx, qweight, scales, zeros, N, K, group_size, flags))
     return set_error(DK_ERR_UNSUPPORTED,
                      "w4a16_matmul_allreduce: needs group_size 128, N %% 8 == 0 and 16-byte aligned operands");
+  // more than 16 rows (up to the communicator's max_m): the tcgen05 small-M kernel with the same
+  // allreduce epilogue, all rows in one launch (one weight pass; the ranks' launches match because M
+  // is the same on every rank and the kernel's row tile holds all of them)
+  // (more rows than max_m, or DK_FLAG_GEMV: the decode GEMV in launches of up to min(16, max_m) rows)
+  if (M > 16 && M <= tp.max_m && !(flags & DK_FLAG_GEMV)) {
+    int mb = 0, split = 0;
+    skinny_choice(M, N, K, &mb, &split);
+    if (mb != 0 && M <= mb)
+      return launch_skinny_tc(x, ldx, qweight, scales, zeros, bias, y, ldy, M, N, K,
+                              (flags & DK_FLAG_STATIC_WEIGHTS) != 0, reinterpret_cast<cudaStream_t>(stream), &tp);
+  }
   return run_fast(x, ldx, qweight, scales, zeros, bias, y, ldy, M, N, K, group_size, cfg, 0, NormArgs(),
                   reinterpret_cast<cudaStream_t>(stream), &tp);
 }

@@ -27,6 +27,8 @@
 #include <cstdio>
 #include <mutex>
 
+#include <cstring>
+
 #include "common.cuh"
 #include "tcgen05.cuh"
 
@@ -461,7 +463,45 @@ struct SkinnyParams {
   int ks;      // 64-K steps per cluster rank
   int static_weights;
   int* err;
+  TPArgs tp;  // tp.world > 0: a row-sharded launch with the allreduce fused in (skinny_tp_finish)
 };
+
+// The fused allreduce of a row-sharded small-M launch (dk_w4a16_matmul_allreduce above 16 rows): the
+// epilogue pushed this rank's partial sums of the CTA's [M x 128] tile into every rank's cells (no
+// bias); each CTA then polls the cells of its own elements from every rank (with a cluster split S,
+// the elements e with e % S == cluster rank), adds them in rank order plus the bias, and stores y.
+// The last CTA to arrive advances the communicator's epoch. The same protocol and cells as the
+// decode GEMV's fused allreduce (the ranks' grids may differ: cells are addressed by row and column).
+__device__ void skinny_tp_finish(const SkinnyParams& p, unsigned long long ep, bool ok, int n0, int S, int crank) {
+  const TPArgs& tp = p.tp;
+  const uint32_t tag = static_cast<uint32_t>(ep);
+  __shared__ int s_give_up;
+  if (threadIdx.x == 0) s_give_up = ok ? 0 : 1;
+  __syncthreads();
+  if (ok) {
+    volatile int* give_up = &s_give_up;
+    const int ncols = min(kSkBN, p.N - n0);
+    for (int e = threadIdx.x; e < p.M * ncols; e += blockDim.x) {
+      if (e % S != crank) continue;
+      const int m = e / ncols, n = n0 + e % ncols;
+      float a = 0.f;
+      bool good = true;
+      for (int q = 0; q < tp.world && good; ++q) {
+        float v = 0.f;
+        good = tp_poll1(tp_cell(tp, tp.rank, ep, q, m, n), tag, v, give_up, p.err, tp.wait_ns);
+        a += v;
+      }
+      if (!good) continue;
+      if (p.bias != nullptr) a += __half2float(p.bias[n]);
+      p.y[static_cast<int64_t>(m) * p.ldy + n] = __float2half_rn(a);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(tp.arrive, 1u) == gridDim.x * gridDim.y - 1) {
+    *tp.arrive = 0;  // the next launch on this communicator uses epoch ep + 1
+    *reinterpret_cast<volatile unsigned long long*>(tp.epoch) = ep;
+  }
+}
 
 __host__ __device__ constexpr int skinny_smem_bytes(int MB, int ks) {
   return kSkOffX + ks * MB * 128 + (2 * kSkStages + 2) * 8 + 16 + 1024;
@@ -489,6 +529,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* done = xready + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   __shared__ int s_fail;
+  __shared__ unsigned long long s_ep;  // fused allreduce: this launch's epoch
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * kSkBN;
@@ -574,6 +615,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------------- x staging, then dequantization
     const int t = threadIdx.x - 64;
     pdl_wait();  // x comes from the previous kernel
+    // the epoch the previous launch on the communicator left (it finished before pdl_wait returned)
+    if (p.tp.world > 0 && t == 0) s_ep = *reinterpret_cast<volatile unsigned long long*>(p.tp.epoch) + 1;
     {
       const int nchunks = nk * (kBK / 8);  // 16-byte chunks per staged row
       for (int idx = t; idx < MB * nchunks; idx += kDeqThreads) {
@@ -684,6 +727,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (kFp8 && n < p.N) v[j] *= __half2float(p.scale[n]);
         if (S == 1) {
           if (m < p.M && n < p.N) {
+            if (p.tp.world > 0) {  // this rank's partial sum (the bias is added once, by the finish)
+              tp_push(p.tp, s_ep, m, n, v[j]);
+              continue;
+            }
             float a = v[j];
             if (p.bias != nullptr) a += __half2float(p.bias[n]);
             p.y[static_cast<int64_t>(m) * p.ldy + n] = __float2half_rn(a);
@@ -706,6 +753,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (__syncthreads_or(!have && warp >= 2)) {
       cluster_sync();
       cluster_sync();
+      if (p.tp.world > 0) skinny_tp_finish(p, s_ep, false, n0, S, rank);  // arrive all the same
       return;
     }
     cluster_sync();
@@ -715,11 +763,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (m >= p.M || n >= p.N) continue;
       float a = 0.f;
       for (int r = 0; r < S; ++r) a += ld_shared_cluster_f32(map_shared_rank(red + e, r));
+      if (p.tp.world > 0) {
+        tp_push(p.tp, s_ep, m, n, a);
+        continue;
+      }
       if (p.bias != nullptr) a += __half2float(p.bias[n]);
       p.y[static_cast<int64_t>(m) * p.ldy + n] = __float2half_rn(a);
     }
     cluster_sync();  // keep the partial sums alive until every rank has read them
   }
+  if (p.tp.world > 0) skinny_tp_finish(p, s_ep, !failed, n0, S, rank);
 }
 
 template <int MB, bool kFp8>
@@ -770,13 +823,15 @@ namespace {
 template <bool kFp8>
 int launch_skinny_core(const CUtensorMap& mq, const CUtensorMap& ms, const CUtensorMap& mz, const void* x, int64_t ldx,
                        const void* scale, const void* bias, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
-                       bool static_weights, cudaStream_t st) {
+                       bool static_weights, cudaStream_t st, const TPArgs* tp = nullptr) {
   for (int64_t m0 = 0; m0 < M;) {
     int mb = 0, S = 0;
     skinny_choice(M - m0, N, K, &mb, &S);
     if (mb == 0) return set_error(DK_ERR_UNSUPPORTED, "small-M tcgen05 gemm: no tile fits (N=%lld, K=%lld)",
                                   (long long)N, (long long)K);
     const int rows = static_cast<int>(std::min<int64_t>(mb, M - m0));
+    if (tp != nullptr && rows > tp->max_m)
+      return set_error(DK_ERR_UNSUPPORTED, "w4a16_matmul_allreduce: %d rows exceed the communicator", rows);
     SkinnyParams p;
     p.scale = static_cast<const __half*>(scale);
     p.x = static_cast<const __half*>(x) + m0 * ldx;
@@ -791,6 +846,10 @@ int launch_skinny_core(const CUtensorMap& mq, const CUtensorMap& ms, const CUten
     p.ks = (p.ktiles + S - 1) / S;
     p.static_weights = static_weights ? 1 : 0;
     p.err = device_info().err_word;
+    if (tp != nullptr)
+      p.tp = *tp;
+    else
+      std::memset(&p.tp, 0, sizeof(p.tp));
     const int smem = skinny_smem_bytes(mb, p.ks);
     const dim3 grid(static_cast<unsigned>((N + kSkBN - 1) / kSkBN), static_cast<unsigned>(S), 1);
     cudaError_t e = cudaSuccess;
@@ -821,7 +880,7 @@ int launch_skinny_core(const CUtensorMap& mq, const CUtensorMap& ms, const CUten
 
 int launch_skinny_tc(const void* x, int64_t ldx, const int32_t* qweight, const void* scales, const void* zeros,
                      const void* bias, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, bool static_weights,
-                     cudaStream_t st) {
+                     cudaStream_t st, const TPArgs* tp) {
   CUtensorMap mq, ms, mz;
   if (!make_tensor_map_2d(&mq, qweight, CU_TENSOR_MAP_DATA_TYPE_INT32, N, K / 8, N * 4, kSkBN, kBK / 8,
                           CU_TENSOR_MAP_SWIZZLE_NONE) ||
@@ -830,7 +889,7 @@ int launch_skinny_tc(const void* x, int64_t ldx, const int32_t* qweight, const v
       !make_tensor_map_2d(&mz, zeros, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, N, K / 128, N * 2, kSkBN, 1,
                           CU_TENSOR_MAP_SWIZZLE_NONE))
     return DK_ERR_CUDA;
-  return launch_skinny_core<false>(mq, ms, mz, x, ldx, nullptr, bias, y, ldy, M, N, K, static_weights, st);
+  return launch_skinny_core<false>(mq, ms, mz, x, ldx, nullptr, bias, y, ldy, M, N, K, static_weights, st, tp);
 }
 
 // The e4m3 weight-only form (kernels/fp8.py:200-223 at 16..127 rows): wq [K, N] bytes, scale fp16 [N].

@@ -13,7 +13,8 @@ K splits land on 128-wide quantization groups, so a shard's packed weights, scal
 exactly the corresponding slices of the unsharded quantization (groups never straddle ranks).
 
 `TPComm` owns one exchange buffer per rank, mapped into every peer with CUDA IPC;
-`w4a16_matmul_allreduce` is one kernel per 16 rows that computes this rank's partial sums, pushes
+`w4a16_matmul_allreduce` is one kernel (per 16 rows on the decode GEMV, up to 64 rows in one tcgen05
+small-M launch) that computes this rank's partial sums, pushes
 them into every rank's buffer over NVLink and adds the ranks' partials of its own columns in rank
 order (every rank gets the same bits). `TensorParallel` is what the runner calls: the fused kernel,
 or an NCCL allreduce after the plain kernel (`mode="nccl"`, the library baseline), and the
@@ -223,7 +224,8 @@ class TensorParallel:
     """What a tensor-parallel runner needs from its group: the shard plan, the reduction of a
     row-sharded projection, and the greedy argmax over vocabulary shards.
 
-    mode "fused": w4a16_matmul_allreduce (quantized kernel backends, up to 16 rows per launch).
+    mode "fused": w4a16_matmul_allreduce (quantized kernel backends; up to 16 rows on the decode GEMV,
+    17-32 rows on the tcgen05 small-M kernel, each with the allreduce in its epilogue).
     mode "nccl": the backend's own projection, then torch.distributed.all_reduce of the fp16 output
     (any backend, any device: the baseline and the CPU/gloo path)."""
 
@@ -244,12 +246,12 @@ class TensorParallel:
 
     def setup(self, hidden: int, device) -> None:
         if self.mode == "fused" and self.comm is None:
-            self.comm = TPComm(max_n=hidden, max_m=16, group=self.group, device=device)
+            self.comm = TPComm(max_n=hidden, max_m=self.FUSED_MAX_ROWS, group=self.group, device=device)
 
-    # rows up to which the fused GEMV + allreduce kernel is used: it runs 16 rows per launch, so above
-    # that the tcgen05 small-M kernel (one pass over the weights) plus NCCL is faster (7B TP=2 at batch
-    # 32: 4760 vs 4539 tok/s); prefill-sized inputs use the GEMM plus NCCL
-    FUSED_MAX_ROWS = 16
+    # rows up to which the projection carries its allreduce: the decode GEMV up to 16 rows, the tcgen05
+    # small-M kernel (one pass over the weights) from 17 to 32; prefill-sized inputs use the GEMM plus
+    # NCCL
+    FUSED_MAX_ROWS = 32
 
     def reduce_linear(self, be, x, p):
         """sum over ranks of the row-sharded projection p of x (+ p.bias once)."""

@@ -211,6 +211,45 @@ def test_allreduce_world1_matches_matmul(M, N, K, cfg):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("M,N,K,with_bias", [(17, 1536, 1536, True), (24, 3584, 2432, False), (32, 1536, 9472, True),
+                                             (32, 4096, 1024, False)])
+def test_allreduce_world1_small_m_tcgen05(M, N, K, with_bias):
+    """17..max_m rows run the tcgen05 small-M kernel with the allreduce epilogue in one launch: at world 1
+    the result is that kernel's plain output (w4a16_matmul above 16 rows) bit for bit, on repeated
+    calls (the epoch advances every launch) and under a CUDA graph."""
+    from kernels.bench.harness import capture
+    from kernels.tp import TPComm, w4a16_matmul_allreduce
+    from kernels.w4a16 import w4a16_matmul
+
+    qw, s, z = _quant_layer(N, K, 4)
+    x = torch.randn(M, K, device="cuda").half()
+    b = (torch.randn(N, device="cuda") * 0.1).half() if with_bias else None
+    comm = TPComm(max_n=4096, max_m=32)
+    try:
+        ref = w4a16_matmul(x, qw, s, z, bias=b)
+        for _ in range(3):
+            assert torch.equal(w4a16_matmul_allreduce(x, qw, s, z, comm, bias=b), ref)
+        out = {}
+
+        def step():
+            out["y"] = w4a16_matmul_allreduce(x, qw, s, z, comm, bias=b)
+
+        step()
+        torch.cuda.synchronize()
+        graph, _ = capture(step)
+        for _ in range(3):
+            graph.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(out["y"], ref)
+        del graph
+        from kernels import _lib
+
+        assert _lib.device_error() == 0
+    finally:
+        comm.close()
+
+
+@pytest.mark.gpu
 def test_allreduce_world1_in_cuda_graph():
     from kernels.bench.harness import capture
     from kernels.tp import TPComm, w4a16_matmul_allreduce
@@ -262,9 +301,11 @@ def _fused_worker(rank, world, port, q):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     comm = None
     try:
-        comm = TPComm(max_n=4096)
+        comm = TPComm(max_n=4096, max_m=32)
         results = []
-        for M, N, K in ((1, 3584, 2048), (4, 1536, 1024), (16, 2048, 2048), (1, 1024, 8192)):
+        # 17-32 rows: the tcgen05 small-M kernel with the allreduce epilogue, one launch
+        for M, N, K in ((1, 3584, 2048), (4, 1536, 1024), (16, 2048, 2048), (1, 1024, 8192), (24, 1536, 2048),
+                        (32, 3584, 4096)):
             qw, s, z = _quant_layer(N, K, 7)  # the same full layer on every rank
             g = torch.Generator().manual_seed(11)
             x = torch.randn(M, K, generator=g).half().cuda()
