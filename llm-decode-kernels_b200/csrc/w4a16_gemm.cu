@@ -468,8 +468,8 @@ struct SkinnyParams {
 
 // The fused allreduce of a row-sharded small-M launch (dk_w4a16_matmul_allreduce above 16 rows): the
 // epilogue pushed this rank's partial sums of the CTA's [M x 128] tile into every rank's cells (no
-// bias); each CTA then polls the cells of its own elements from every rank (with a cluster split S,
-// the elements e with e % S == cluster rank), adds them in rank order plus the bias, and stores y.
+// bias); each CTA then polls the cells of its own column quads from every rank (with a cluster split
+// S, the quads e with e % S == cluster rank), adds them in rank order plus the bias, and stores y.
 // The last CTA to arrive advances the communicator's epoch. The same protocol and cells as the
 // decode GEMV's fused allreduce (the ranks' grids may differ: cells are addressed by row and column).
 __device__ void skinny_tp_finish(const SkinnyParams& p, unsigned long long ep, bool ok, int n0, int S, int crank) {
@@ -480,20 +480,43 @@ __device__ void skinny_tp_finish(const SkinnyParams& p, unsigned long long ep, b
   __syncthreads();
   if (ok) {
     volatile int* give_up = &s_give_up;
-    const int ncols = min(kSkBN, p.N - n0);
-    for (int e = threadIdx.x; e < p.M * ncols; e += blockDim.x) {
+    // four adjacent columns at a time (N % 8 == 0): every rank's two 16-byte cell loads are issued
+    // before the first is checked, so a quad costs one round trip, not one per rank and column
+    const int nq = min(kSkBN, p.N - n0) / 4;
+    for (int e = threadIdx.x; e < p.M * nq; e += blockDim.x) {
       if (e % S != crank) continue;
-      const int m = e / ncols, n = n0 + e % ncols;
-      float a = 0.f;
+      const int m = e / nq, n = n0 + 4 * (e % nq);
+      uint4 lo[DK_TP_MAX_WORLD], hi[DK_TP_MAX_WORLD];
+#pragma unroll
+      for (int q = 0; q < DK_TP_MAX_WORLD; ++q)
+        if (q < tp.world) {
+          const uint32_t* c = tp_cell(tp, tp.rank, ep, q, m, n);
+          lo[q] = ld_volatile_v4(c);
+          hi[q] = ld_volatile_v4(c + 4);
+        }
+      float sum[4] = {0.f, 0.f, 0.f, 0.f};
       bool good = true;
-      for (int q = 0; q < tp.world && good; ++q) {
-        float v = 0.f;
-        good = tp_poll1(tp_cell(tp, tp.rank, ep, q, m, n), tag, v, give_up, p.err, tp.wait_ns);
-        a += v;
+#pragma unroll
+      for (int q = 0; q < DK_TP_MAX_WORLD; ++q) {
+        if (q >= tp.world || !good) break;
+        float v[4];
+        if (lo[q].y == tag && lo[q].w == tag && hi[q].y == tag && hi[q].w == tag) {
+          v[0] = __uint_as_float(lo[q].x);
+          v[1] = __uint_as_float(lo[q].z);
+          v[2] = __uint_as_float(hi[q].x);
+          v[3] = __uint_as_float(hi[q].z);
+        } else {
+          good = tp_poll4(tp_cell(tp, tp.rank, ep, q, m, n), tag, v, give_up, p.err, tp.wait_ns);
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) sum[c] += v[c];
       }
       if (!good) continue;
-      if (p.bias != nullptr) a += __half2float(p.bias[n]);
-      p.y[static_cast<int64_t>(m) * p.ldy + n] = __float2half_rn(a);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (p.bias != nullptr) sum[c] += __half2float(p.bias[n + c]);
+        p.y[static_cast<int64_t>(m) * p.ldy + n + c] = __float2half_rn(sum[c]);
+      }
     }
   }
   __syncthreads();
