@@ -79,7 +79,8 @@ def test_tp_entry_points_validate_without_a_gpu():
     assert h.dk_tp_buffer_bytes(2, 16, 3584, ctypes.byref(n)) == 0
     assert n.value == 256 + 2 * 2 * 16 * 3584 * 8
     assert h.dk_tp_buffer_bytes(9, 16, 3584, ctypes.byref(n)) == -1
-    assert h.dk_tp_buffer_bytes(2, 17, 3584, ctypes.byref(n)) == -1
+    assert h.dk_tp_buffer_bytes(2, 64, 3584, ctypes.byref(n)) == 0  # up to 64 rows (the small-M kernel)
+    assert h.dk_tp_buffer_bytes(2, 65, 3584, ctypes.byref(n)) == -1
     assert h.dk_tp_buffer_bytes(2, 16, 3585, ctypes.byref(n)) == -1
     comm = ctypes.c_void_p()
     bufs = (ctypes.c_void_p * 2)(None, None)
