@@ -256,6 +256,8 @@ class TensorParallel:
     def reduce_linear(self, be, x, p):
         """sum over ranks of the row-sharded projection p of x (+ p.bias once)."""
         rows = x.numel() // x.shape[-1]
+        if self.world == 1:  # nothing to reduce: the plain projection
+            return be.linear(x, p)
         if (self.mode == "fused" and self.comm is not None and p.qweight is not None and p.zeros is not None
                 and rows <= self.FUSED_MAX_ROWS):
             return w4a16_matmul_allreduce(x, p.qweight, p.scales, p.zeros, self.comm, bias=p.bias,

@@ -418,8 +418,9 @@ def test_allreduce_world2_matches_unsharded():
 # ------------------------------------------------------------------------------ runner on GPUs
 @pytest.mark.gpu
 def test_tp_runner_world1_fused_is_the_plain_runner():
-    """World 1: the tensor-parallel runner (fused allreduce kernels on its own buffer) decodes the
-    same tokens with the same logits as the unsharded runner, eagerly and under the CUDA graph."""
+    """World 1: the tensor-parallel runner (a one-rank group reduces nothing: the plain projections)
+    decodes the same tokens with the same logits as the unsharded runner, eagerly and under the CUDA
+    graph. The fused kernel itself at world 1 is tested above, against the plain matmul."""
     from kernels.e2e.model import QwenRunner, make_backend
     from kernels.e2e.run import GraphDecoder
     from kernels.tp import TensorParallel
