@@ -309,12 +309,22 @@ def gemv_roofline(runner, peak_gbs: float) -> dict:
 
     r = torch.randn(1, 1, H, device="cuda", dtype=torch.float16)
 
-    def chain():
-        for L in runner.layers:
-            be.norm_linear(x, L.ln1, runner.eps, r, L.qkv)
+    split_sums = getattr(be, "partials", False) and runner.tp is None
+
+    def chain():  # as QwenRunner._decode_layers issues them at one row (down_proj's partial sums included)
+        parts, n = None, len(runner.layers)
+        for i, L in enumerate(runner.layers):
+            if parts is not None:
+                be.norm_linear_partials(parts, runner.layers[i - 1].down.bias, L.ln1, runner.eps, r, L.qkv)
+            else:
+                be.norm_linear(x, L.ln1, runner.eps, r, L.qkv)
             be.linear(a, L.o)
             act, _ = be.norm_gate_up_act(x, L.ln2, runner.eps, r, L.gate_up)
-            be.linear(act, L.down)
+            if split_sums and i + 1 < n:
+                parts = be.linear_partials(act, L.down)
+            else:
+                be.linear(act, L.down)
+                parts = None
 
     chain()
     torch.cuda.synchronize()
