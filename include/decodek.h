@@ -106,7 +106,8 @@ int dk_dequantize_int4(const int32_t* qweight, const void* scales, const void* z
  * x rows have stride ldx, y rows stride ldy (elements). bias may be NULL. cfg may be NULL.
  * Dispatch by rows (fast-path shapes: N % 8 == 0, group_size 128, 16-byte aligned operands):
  * up to 8 rows, or up to 16 with K < 4096: the decode GEMV, up to 16 rows per launch (fewer when a long
- * K slice leaves no tile for the staged rows); 9-127 rows with N >= 128: the tcgen05 small-M kernel;
+ * K slice leaves no tile for the staged rows); 9-16 rows with K >= 4096 and 17-127 rows, N >= 128: the
+ * tcgen05 small-M kernel;
  * M >= 128 and N >= 128: the tcgen05 tensor-core GEMM (kernels/w4a16.py:31-97). The tcgen05 kernels
  * round every dequantized weight to fp16 like the reference's dequantize-then-matmul. DK_FLAG_GEMV
  * keeps any M on the decode GEMV. Other shapes run a one-thread-per-output kernel. */
