@@ -432,6 +432,7 @@ __device__ __forceinline__ uint4 load_x8(const GemvParams& p, int m, int k) {
   return out;
 }
 
+template <int kBatch>
 __device__ __forceinline__ void stage_x(const GemvParams& p, uint8_t* xs, float* cx, int s_begin, int nst, bool writer,
                                         bool factored, const NormW& nwp) {
   constexpr int kThr = kWarps * 32;
@@ -491,64 +492,83 @@ __device__ __forceinline__ void stage_x(const GemvParams& p, uint8_t* xs, float*
   // One item = 8 K values of one row. nblk is a multiple of 32, so every warp iteration has 32 items
   // in range and the 16 lanes of a half-warp hold the 16 blocks of one 128-group: the factored path
   // reduces its {C, X} with shuffles in a fixed order (deterministic) - no second pass.
-  for (int base = (tid & ~31); base < p.M * nblk; base += kThr) {
-    const int i = base + (tid & 31);
-    const int m = i / nblk, b = i % nblk;
-    const int k = (kb0 + b) * 8;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (k < p.K) {
+  // The loads of kBatch iterations are issued before any of them is stored (a 16-row slice is up to
+  // 12 iterations per thread: one L2 round trip per kBatch iterations instead of one per iteration).
+  // Item i still goes to the thread it went to one iteration at a time.
+  const int items = p.M * nblk;
+  for (int base0 = (tid & ~31); base0 < items; base0 += kBatch * kThr) {
+    uint4 vb[kBatch], rb[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      vb[u] = rb[u] = make_uint4(0, 0, 0, 0);
+      const int i = base0 + u * kThr + (tid & 31);
+      if (base0 + u * kThr >= items) continue;  // warp-uniform: items is a multiple of 32
+      const int m = i / nblk, b = i % nblk;
+      const int k = (kb0 + b) * 8;
+      if (k >= p.K) continue;
       if (keep)  // this thread read block kb0 + b (= tid + j * 256) in the pass above
-        v = (kb0 + b) < kThr ? keep0 : keep1;
+        vb[u] = (kb0 + b) < kThr ? keep0 : keep1;
       else
-        v = load_x8(p, m, k);
-      if (norm) {
-        __half2* vh = reinterpret_cast<__half2*>(&v);
-        if (p.res != nullptr && !keep) {
-          const uint4 r = __ldcg(reinterpret_cast<const uint4*>(p.res + m * p.ldr + k));
-          const __half2* rh = reinterpret_cast<const __half2*>(&r);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) vh[j] = __hadd2_rn(vh[j], rh[j]);
-        }
-        // one row: block b of the slice is this thread's block tid + j * kThr (prefetched above)
-        const uint4 wv = (p.M == 1 && b < 2 * kThr) ? (b < kThr ? nwp.w[0] : nwp.w[1])
-                                                    : __ldg(reinterpret_cast<const uint4*>(p.norm_w + k));
-        const __half2* wh = reinterpret_cast<const __half2*>(&wv);
-        const float s = inv[m];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = __half22float2(vh[j]);
-          vh[j] = __hmul2_rn(wh[j], __floats2half2_rn(__fmul_rn(f.x, s), __fmul_rn(f.y, s)));
-        }
-      }
+        vb[u] = load_x8(p, m, k);
+      if (norm && p.res != nullptr && !keep) rb[u] = __ldcg(reinterpret_cast<const uint4*>(p.res + m * p.ldr + k));
     }
-    uint4 o;
-    o.x = prmt(v.x, v.z, 0x5410);  // (x0, x4)
-    o.y = prmt(v.x, v.z, 0x7632);  // (x1, x5)
-    o.z = prmt(v.y, v.w, 0x5410);  // (x2, x6)
-    o.w = prmt(v.y, v.w, 0x7632);  // (x3, x7)
-    if (factored) {  // odd K meets 1024 + 16 q: stage x / 16 (exact, a power of two)
-      o.y = hmul2_rn(o.y, 0x2C002C00u);
-      o.w = hmul2_rn(o.w, 0x2C002C00u);
-      // {C, X} of this 128-group and row: C = 1024 * sum of the staged values, X = the sum of the x
-      // each weight is multiplied by (odd K: 16 * staged)
-      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&o.x));
-      const float2 bb = __half22float2(*reinterpret_cast<const __half2*>(&o.y));
-      const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&o.z));
-      const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&o.w));
-      const float even = (a.x + a.y) + (c.x + c.y), odd = (bb.x + bb.y) + (d.x + d.y);
-      float C = even + odd, X = fmaf(16.f, odd, even);
 #pragma unroll
-      for (int off = 8; off > 0; off >>= 1) {
-        C += __shfl_xor_sync(0xffffffffu, C, off);
-        X += __shfl_xor_sync(0xffffffffu, X, off);
+    for (int u = 0; u < kBatch; ++u) {
+      const int base = base0 + u * kThr;
+      if (base >= items) break;  // warp-uniform
+      const int i = base + (tid & 31);
+      const int m = i / nblk, b = i % nblk;
+      const int k = (kb0 + b) * 8;
+      uint4 v = vb[u];
+      if (k < p.K) {
+        if (norm) {
+          __half2* vh = reinterpret_cast<__half2*>(&v);
+          if (p.res != nullptr && !keep) {
+            const __half2* rh = reinterpret_cast<const __half2*>(&rb[u]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) vh[j] = __hadd2_rn(vh[j], rh[j]);
+          }
+          // one row: block b of the slice is this thread's block tid + j * kThr (prefetched above)
+          const uint4 wv = (p.M == 1 && b < 2 * kThr) ? (b < kThr ? nwp.w[0] : nwp.w[1])
+                                                      : __ldg(reinterpret_cast<const uint4*>(p.norm_w + k));
+          const __half2* wh = reinterpret_cast<const __half2*>(&wv);
+          const float s = inv[m];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = __half22float2(vh[j]);
+            vh[j] = __hmul2_rn(wh[j], __floats2half2_rn(__fmul_rn(f.x, s), __fmul_rn(f.y, s)));
+          }
+        }
       }
-      if ((tid & 15) == 0) {
-        float* dst = cx + 2 * ((b >> 4) * 16 + m);  // [group in slice][16 rows]{C, X}
-        dst[0] = 1024.f * C;
-        dst[1] = X;
+      uint4 o;
+      o.x = prmt(v.x, v.z, 0x5410);  // (x0, x4)
+      o.y = prmt(v.x, v.z, 0x7632);  // (x1, x5)
+      o.z = prmt(v.y, v.w, 0x5410);  // (x2, x6)
+      o.w = prmt(v.y, v.w, 0x7632);  // (x3, x7)
+      if (factored) {  // odd K meets 1024 + 16 q: stage x / 16 (exact, a power of two)
+        o.y = hmul2_rn(o.y, 0x2C002C00u);
+        o.w = hmul2_rn(o.w, 0x2C002C00u);
+        // {C, X} of this 128-group and row: C = 1024 * sum of the staged values, X = the sum of the x
+        // each weight is multiplied by (odd K: 16 * staged)
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&o.x));
+        const float2 bb = __half22float2(*reinterpret_cast<const __half2*>(&o.y));
+        const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&o.z));
+        const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&o.w));
+        const float even = (a.x + a.y) + (c.x + c.y), odd = (bb.x + bb.y) + (d.x + d.y);
+        float C = even + odd, X = fmaf(16.f, odd, even);
+#pragma unroll
+        for (int off = 8; off > 0; off >>= 1) {
+          C += __shfl_xor_sync(0xffffffffu, C, off);
+          X += __shfl_xor_sync(0xffffffffu, X, off);
+        }
+        if ((tid & 15) == 0) {
+          float* dst = cx + 2 * ((b >> 4) * 16 + m);  // [group in slice][16 rows]{C, X}
+          dst[0] = 1024.f * C;
+          dst[1] = X;
+        }
       }
+      *reinterpret_cast<uint4*>(xs + m * p.xs_pitch + b * 16) = o;
     }
-    *reinterpret_cast<uint4*>(xs + m * p.xs_pitch + b * 16) = o;
   }
   asm volatile("bar.sync 1, %0;" ::"r"(kThr) : "memory");
 }
@@ -643,7 +663,7 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 3 - NT)  // M <= 8: two CTA
     }
     pdl_wait();  // x (and the residual) come from the previous kernels
     if (p.tp.world > 0 && threadIdx.x == 0) s_ep = *reinterpret_cast<volatile unsigned long long*>(p.tp.epoch) + 1;
-    stage_x(p, smem + L.xs_off, reinterpret_cast<float*>(smem + L.cx_off), s_begin, nst,
+    stage_x<NT == 1 ? 1 : 4>(p, smem + L.xs_off, reinterpret_cast<float*>(smem + L.cx_off), s_begin, nst,
             blockIdx.x == 0 && blockIdx.y == 0, !EXACT, nwp);  // ends with a barrier
     const unsigned long long ep = s_ep;
     const int g = lane >> 2;  // MMA group: A rows g, g+8 ; B column g

@@ -157,19 +157,34 @@ __global__ void __launch_bounds__((kWarps8 + 1) * 32, 3 - NT)
     {
       // x[:, K slice] -> shared memory; in each 16-element block lane t's 4 values come first:
       // (x_t, x_{t+4}, x_{t+8}, x_{t+12}) for t = 0..3
+      // The M > 8 variant (up to 24 iterations per thread at 16 rows) issues the loads of kB
+      // iterations before it stores any of them; item i goes to the same thread either way.
       const int k0 = s_begin * kRows;
       const int nblk = nst * (kRows / 16);
-      for (int i = threadIdx.x; i < p.M * nblk * 4; i += kWarps8 * 32) {
-        const int m = i / (nblk * 4), rem = i % (nblk * 4), b = rem / 4, t = rem % 4;
-        const int k = k0 + b * 16 + t;
-        __half v[4];
+      constexpr int kB = NT == 1 ? 1 : 4;
+      constexpr int kThr8 = kWarps8 * 32;
+      const int items = p.M * nblk * 4;
+      for (int i0 = threadIdx.x; i0 < items; i0 += kB * kThr8) {
+        __half v[kB][4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-          v[e] = (k + 4 * e < p.K) ? __ldcg(p.x + m * p.ldx + k + 4 * e) : __float2half(0.f);
-        uint2 o;
-        o.x = half2_bits(v[0], v[1]);
-        o.y = half2_bits(v[2], v[3]);
-        *reinterpret_cast<uint2*>(smem + L.xs_off + m * p.xs_pitch + b * 32 + t * 8) = o;
+        for (int u = 0; u < kB; ++u) {
+          const int i = i0 + u * kThr8;
+          const int m = i / (nblk * 4), rem = i % (nblk * 4), b = rem / 4, t = rem % 4;
+          const int k = k0 + b * 16 + t;
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            v[u][e] = (i < items && k + 4 * e < p.K) ? __ldcg(p.x + m * p.ldx + k + 4 * e) : __float2half(0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < kB; ++u) {
+          const int i = i0 + u * kThr8;
+          if (i >= items) break;
+          const int m = i / (nblk * 4), rem = i % (nblk * 4), b = rem / 4, t = rem % 4;
+          uint2 o;
+          o.x = half2_bits(v[u][0], v[u][1]);
+          o.y = half2_bits(v[u][2], v[u][3]);
+          *reinterpret_cast<uint2*>(smem + L.xs_off + m * p.xs_pitch + b * 32 + t * 8) = o;
+        }
       }
       asm volatile("bar.sync 1, %0;" ::"r"(kWarps8 * 32) : "memory");
     }
