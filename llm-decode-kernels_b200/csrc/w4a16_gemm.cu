@@ -446,6 +446,12 @@ constexpr int kSkSZ = kSkBN * 2;                   // one scale (or zero) row
 constexpr int kSkABytes = kSkBN * kBK * 2;         // 16 KB dequantized weight tile
 constexpr int kSkXBudget = 96 * 1024;              // staged x slice per CTA
 constexpr int kSkMaxSplit = 8;
+// A split leaves every CTA at least this many 64-K steps (when a split is needed at all). Shallower
+// splits were slower: qkv 2048 x 1536 at 32 rows took 23.9 us at S = 8 (3 steps per CTA, 16 clusters
+// of 8) and 12.6 us at S = 4; batch-32 decode 12307 -> 13867 tok/s. The likely cause is that fewer
+// 8-CTA clusters are resident at once than 148 / 8, so the last ones ran as a second wave (o_proj's
+// 12 clusters of 8 were as fast as S = 4).
+constexpr int kSkMinSteps = 6;
 constexpr int kSkOffW = kSkStages * kSkABytes;
 constexpr int kSkOffS = kSkOffW + kSkStages * kSkWSlot;
 constexpr int kSkOffZ = kSkOffS + kSkStages * kSkSZ;
@@ -832,6 +838,7 @@ void skinny_choice(int64_t rows, int64_t N, int64_t K, int* mb_out, int* split_o
       if ((S - 1) * ks >= ktiles) continue;             // every rank gets at least one K step
       if (ks * mb * 128 > kSkXBudget) continue;         // staged x slice
       if (best && tiles_n * S > sms) break;             // one wave of CTAs
+      if (best && ks < kSkMinSteps) break;              // enough K steps per CTA
       best = S;
     }
     if (best) {
