@@ -650,6 +650,7 @@ def run_ours(args, world, rank, local):
                        {"backend": "ours", "batch": 4},
                        {"backend": "ours", "batch": 4, "fused": True},
                        {"backend": "ours", "batch": 16},
+                       {"backend": "ours", "batch": 32},
                        {"backend": "ours_fp8", "batch": 1},
                        {"backend": "ours_fp8", "batch": 16},
                        {"backend": "ours_lm", "batch": 1}):
