@@ -492,9 +492,9 @@ __device__ __forceinline__ void stage_x(const GemvParams& p, uint8_t* xs, float*
   // One item = 8 K values of one row. nblk is a multiple of 32, so every warp iteration has 32 items
   // in range and the 16 lanes of a half-warp hold the 16 blocks of one 128-group: the factored path
   // reduces its {C, X} with shuffles in a fixed order (deterministic) - no second pass.
-  // The loads of kBatch iterations are issued before any of them is stored (a 16-row slice is up to
-  // 12 iterations per thread: one L2 round trip per kBatch iterations instead of one per iteration).
-  // Item i still goes to the thread it went to one iteration at a time.
+  // The loads of kBatch iterations are issued before any of them is stored (16 rows of a 1536-wide K
+  // slice are 12 iterations per thread: one L2 round trip per kBatch iterations instead of one per
+  // iteration). Item i still goes to the thread it went to one iteration at a time.
   const int items = p.M * nblk;
   for (int base0 = (tid & ~31); base0 < items; base0 += kBatch * kThr) {
     uint4 vb[kBatch], rb[kBatch];

@@ -157,8 +157,8 @@ __global__ void __launch_bounds__((kWarps8 + 1) * 32, 3 - NT)
     {
       // x[:, K slice] -> shared memory; in each 16-element block lane t's 4 values come first:
       // (x_t, x_{t+4}, x_{t+8}, x_{t+12}) for t = 0..3
-      // The M > 8 variant (up to 24 iterations per thread at 16 rows) issues the loads of kB
-      // iterations before it stores any of them; item i goes to the same thread either way.
+      // The M > 8 variant (24 iterations per thread for 16 rows of a 1536-wide K slice) issues the
+      // loads of kB iterations before it stores any of them; item i goes to the same thread either way.
       const int k0 = s_begin * kRows;
       const int nblk = nst * (kRows / 16);
       constexpr int kB = NT == 1 ? 1 : 4;
